@@ -1,0 +1,353 @@
+"""Benchmark of the paged decode hot path (isolated paged-decode attention at
+the Qwen3-0.6B shape, bf16).
+
+One STEP = one layer's decode KV append + paged GQA decode attention over B sequences (and, with
+N > 1 ranks, the NCCL all-gather of the per-head outputs).  Weak scaling over the head partition:
+at N ranks the global batch is 256*N sequences and rank r holds KV heads [r*8/N, (r+1)*8/N), so
+every rank reads the same bytes per step as one GPU at N=1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0.  ``value`` = KV bytes read per step by all ranks (sum of context
+lengths x 4096 B for 8 KV heads x 128 dims x K+V x bf16) / max-over-ranks device time per step.
+``e2e`` = the same metric through the public op with host (pinned) inputs copied in and the output
+copied out every step.  ``--impl reference`` times the CPU restatement of the reference's torch
+path (gather the padded history, expand GQA, matmul/softmax/matmul) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "mini-infra-qwen3_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+# BASELINE config 2
+HQ, HKV, D, BS = 16, 8, 128, 16
+B_PER_RANK = 256
+CTX_LO, CTX_HI = 128, 4096
+KV_BYTES_PER_TOKEN = 2 * HKV * D * 2  # K+V, all 8 KV heads, bf16
+SEED = 1234
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def workload(world: int, rank: int, device):
+    """Seeded C2 inputs for this rank: contexts, block tables, pools (own KV heads), q, new K/V."""
+    b = B_PER_RANK * world
+    h_loc = HKV // world
+    rng = np.random.RandomState(SEED)
+    ctx = rng.randint(CTX_LO, CTX_HI + 1, size=b).astype(np.int64)  # includes the appended token
+    need = -(-ctx // BS)
+    used = int(need.sum())
+    num_blocks = 1 + used + used // 10  # exactly the needed blocks + 10% free + null block
+    perm = rng.permutation(np.arange(1, num_blocks))[:used]
+    max_blocks = int(need.max())
+    tables = np.zeros((b, max_blocks), dtype=np.int64)
+    offs = np.concatenate([[0], np.cumsum(need)])
+    for i in range(b):
+        tables[i, : need[i]] = perm[offs[i] : offs[i + 1]]
+    pos = ctx - 1
+    slots = tables[np.arange(b), pos // BS] * BS + pos % BS
+    g = torch.Generator(device=device).manual_seed(SEED + 17 * rank)
+    kp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
+    vp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
+    q = torch.randn((b, HQ // world, D), generator=g, device=device, dtype=torch.bfloat16)
+    kn = torch.randn((b, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
+    vn = torch.randn((b, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
+    return dict(b=b, ctx=ctx, tables=tables, slots=slots, num_blocks=num_blocks, kp=kp, vp=vp, q=q, kn=kn, vn=vn,
+                h_loc=h_loc)
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        if shutil.which("nvidia-smi"):
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[4:8]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8) -> dict:
+    """Time the oracle port of the reference's CPU decode (gather + GQA expand + matmul/softmax)."""
+    from oracle import paged_oracle as po
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
+    rng = np.random.RandomState(SEED + 1)
+    total_tokens, total_t, n = 0, 0.0, 0
+    while total_t < seconds or n == 0:
+        ctx = rng.randint(CTX_LO, CTX_HI + 1, size=per_sample).astype(np.int64)
+        need = -(-ctx // BS)
+        nb = 1 + int(need.sum())
+        tables = np.zeros((per_sample, int(need.max())), dtype=np.int64)
+        perm = rng.permutation(np.arange(1, nb))
+        off = 0
+        for i in range(per_sample):
+            tables[i, : need[i]] = perm[off : off + need[i]]
+            off += need[i]
+        kp = po.f32_to_bf16(rng.standard_normal((nb, BS, HKV, D)).astype(np.float32))
+        vp = po.f32_to_bf16(rng.standard_normal((nb, BS, HKV, D)).astype(np.float32))
+        q = po.f32_to_bf16(rng.standard_normal((per_sample, HQ, D)).astype(np.float32))
+        t0 = time.perf_counter()
+        po.paged_decode_attention(q, kp, vp, tables, ctx, D**-0.5)
+        total_t += time.perf_counter() - t0
+        total_tokens += int(ctx.sum())
+        n += 1
+    return {
+        "value": total_tokens * KV_BYTES_PER_TOKEN / total_t / 1e9,
+        "unit": "GB/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{n} x {per_sample} sequences of config 2 (ctx U[{CTX_LO},{CTX_HI}]), numpy fp32 oracle, "
+                  f"{total_t:.1f} s of CPU work",
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    per_step = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_decode_sample(seconds=2.0 if i < args.warmup else 6.0)
+        if i >= args.warmup:
+            per_step.append(r)
+            cb = r
+    value = float(np.mean([r["value"] for r in per_step]))
+    cb = dict(cb, value=value)
+    line = {
+        "metric": "paged decode KV-read GB/s", "value": value, "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config2_decode_op_cpu_sample", "seq_len": f"U[{CTX_LO},{CTX_HI}]"},
+        "cpu_baseline": cb, "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    from mini_infra_b200 import ops
+    from mini_infra_b200.model.qwen3 import HeadPartition, gather_heads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        group = dist.group.WORLD
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if HKV % world:
+        raise SystemExit(f"{HKV} KV heads cannot be split over {world} ranks")
+    part = HeadPartition(rank, world, group)
+
+    w = workload(world, rank, device)
+    b = w["b"]
+    tables = torch.from_numpy(w["tables"]).to(device)
+    ctx = torch.from_numpy(w["ctx"]).to(device)
+    slots = torch.from_numpy(w["slots"]).to(device)
+    scale = D**-0.5
+    out = torch.empty((b, (HQ // world) * D), dtype=torch.bfloat16, device=device)
+    ws = ops.workspace(device, ops.decode_workspace_bytes(b, HQ // world, w["kp"], tables.shape[1]))
+
+    def step():
+        ops.paged_decode(w["q"], w["kp"], w["vp"], tables, ctx, scale, key_new=w["kn"], value_new=w["vn"],
+                         slot_mapping=slots, out=out, ws=ws)
+        return gather_heads(out, part)
+
+    def attn_only():
+        ops.paged_decode(w["q"], w["kp"], w["vp"], tables, ctx, scale, out=out, ws=ws)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    def timed(fn, steps) -> float:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        barrier()
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=device, dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for _ in range(args.warmup):
+        step()
+    with ClockSampler(local) as clocks:
+        ms = timed(step, args.steps)
+    kv_bytes_global = float(w["ctx"].sum()) * KV_BYTES_PER_TOKEN  # all ranks together read every head once
+    value = kv_bytes_global / (ms * 1e-3) / 1e9
+
+    # roofline of the attention kernels alone (split-K kernel + combine): algorithmic bytes per launch
+    for _ in range(3):
+        attn_only()
+    ms_attn = timed(attn_only, max(args.steps // 2, 10))
+    h_loc = w["h_loc"]
+    alg_bytes = (float(w["ctx"].sum()) * 2 * h_loc * D * 2  # K+V of this rank's heads
+                 + b * (HQ // world) * D * 2 * 2 + tables.numel() * 8 + b * 8)  # q + out + tables + ctx
+    achieved = alg_bytes / (ms_attn * 1e-3) / 1e9
+    peaks = measured_peaks()
+
+    # end to end through the public op: pinned host inputs -> device -> op -> pinned host output
+    h_q = w["q"].cpu().pin_memory()
+    h_kn, h_vn = w["kn"].cpu().pin_memory(), w["vn"].cpu().pin_memory()
+    meta = torch.cat([slots.cpu(), ctx.cpu(), tables.cpu().reshape(-1)]).pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_q, d_kn, d_vn = torch.empty_like(w["q"]), torch.empty_like(w["kn"]), torch.empty_like(w["vn"])
+    d_meta = torch.empty(meta.shape, dtype=torch.long, device=device)
+
+    def e2e_step():
+        d_q.copy_(h_q, non_blocking=True)
+        d_kn.copy_(h_kn, non_blocking=True)
+        d_vn.copy_(h_vn, non_blocking=True)
+        d_meta.copy_(meta, non_blocking=True)
+        sl, cx, tb = d_meta[:b], d_meta[b : 2 * b], d_meta[2 * b :].view(b, -1)
+        ops.paged_decode(d_q, w["kp"], w["vp"], tb, cx, scale, key_new=d_kn, value_new=d_vn, slot_mapping=sl,
+                         out=out, ws=ws)
+        full = gather_heads(out, part)
+        h_out.copy_(out, non_blocking=True)
+        return full
+
+    for _ in range(3):
+        e2e_step()
+    ms_e2e = timed(e2e_step, max(args.steps // 2, 10))
+    h2d = h_q.numel() * 2 + h_kn.numel() * 2 + h_vn.numel() * 2 + meta.numel() * 8
+    d2h = h_out.numel() * 2
+    e2e_value = kv_bytes_global / (ms_e2e * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_decode_sample()
+    if rank == 0:
+        line = {
+            "metric": "paged decode KV-read GB/s",
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "config2_paged_decode_op_qwen3_0.6b_shape",
+                "global_batch": b, "seq_len": f"U[{CTX_LO},{CTX_HI}]", "heads": f"{HQ}q/{HKV}kv",
+                "head_dim": D, "block_size": BS, "pool_blocks_per_rank": w["num_blocks"],
+                "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU",
+                "l2": "inputs larger than L2 (KV pool ~2.4 GB per rank)",
+                "step": "append + paged decode (split-K + combine)" + (" + NCCL all-gather" if world > 1 else ""),
+            },
+            "roofline": {
+                "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                "kernel": "decode_split_kernel + decode_combine_kernel", "ms_per_launch": ms_attn,
+            },
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

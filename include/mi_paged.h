@@ -1,0 +1,146 @@
+/*
+ * mi_paged.h — C ABI of the B200 paged KV-cache library (libmi_paged.so, sm_100a).
+ *
+ * The library holds the device side of mini-infra-qwen3's paged KV-cache hot path.  Every entry
+ * point takes plain device pointers, element strides and sizes, plus the CUDA stream to launch on
+ * (a cudaStream_t passed as void*; NULL = legacy default stream).  Nothing here allocates, frees
+ * or synchronizes: callers own every buffer (pools, metadata, outputs, workspace) and calls are
+ * asynchronous on the given stream.  Integer metadata (block tables, slots, lengths) is int64,
+ * as the reference's PagedRunner packs it.
+ *
+ * Layouts (the reference's own, worker/paged_kv_cache.py:15-20):
+ *   pool      [num_blocks, block_size, num_kv_heads, head_dim], contiguous; slot = block*bs + offset
+ *   block 0   is the null block: it pads block tables and is never allocated
+ *   tables    [batch, table_stride] int64, row b lists the physical blocks of sequence b
+ *
+ * Return value: MI_OK (0) or a negative MI_ERR_* code; mi_last_error() then describes it.
+ * Device-side checks (out-of-range block ids or slots, bounded waits that ran out) never trap:
+ * they set bits in a sticky device status word read back with mi_read_status().
+ */
+#ifndef MI_PAGED_H
+#define MI_PAGED_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define MI_F32 0
+#define MI_BF16 1
+#define MI_F16 2
+
+/* return codes */
+#define MI_OK 0
+#define MI_ERR_INVALID (-1)     /* argument rejected on the host before any launch */
+#define MI_ERR_CUDA (-2)        /* a CUDA call or launch failed */
+#define MI_ERR_UNSUPPORTED (-3) /* valid arguments, but no kernel variant for them */
+
+/* device status bits (sticky, see mi_read_status) */
+#define MI_STATUS_BAD_BLOCK 1u   /* a block table entry was outside [0, num_blocks) */
+#define MI_STATUS_BAD_SLOT 2u    /* a destination slot was outside [0, num_blocks*block_size) */
+#define MI_STATUS_TIMEOUT 4u     /* a bounded wait inside a kernel gave up */
+#define MI_STATUS_BAD_LENGTH 8u  /* a context/chunk length exceeded what the block table covers */
+#define MI_STATUS_BAD_INDEX 16u  /* a scatter source row/position was outside the source tensor */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mi_version(void);
+
+/* Text of the last host-side error of the calling thread ("" if none). */
+const char* mi_last_error(void);
+
+/* Read (and optionally clear) the device status word of the current device.  Synchronizes
+ * `stream`.  *status_out receives the MI_STATUS_* bits seen since the last clear. */
+int mi_read_status(unsigned int* status_out, int clear, void* stream);
+
+/*
+ * mi_kv_scatter — copy tokens into one layer's K and V pools, K and V in one launch.
+ * Replaces PagedKVCachePool.write_prefill (worker/paged_kv_cache.py:74-95:
+ *   pool.view(-1,H,D).index_copy_(0, slot_mapping, key[token_rows, :, token_positions, :]))
+ * and the decode append of Qwen3Attention._apply_paged_kv_pool (model/qwen3.py:282-283).
+ *
+ * k_src/v_src element (r, h, p, d) is at  r*s[0] + h*s[1] + p*s[2] + d  (elements; d contiguous),
+ * with s = k_strides / v_strides (3 entries each).  Token i copies source (token_rows[i], :,
+ * token_positions[i], :) to pool slot slot_mapping[i].  token_rows == NULL means row i;
+ * token_positions == NULL means position 0 (decode append: source [B, H, D]).
+ * src_rows / src_positions bound the source (its B and L; L = 1 for a decode append): tokens whose
+ * row/position fall outside are skipped and flagged, as are out-of-range slots.  Slots must be
+ * distinct (as index_copy_ requires).
+ */
+int mi_kv_scatter(const void* k_src, const void* v_src, const int64_t* k_strides, const int64_t* v_strides,
+                  int64_t src_rows, int64_t src_positions, const int64_t* token_rows,
+                  const int64_t* token_positions, const int64_t* slot_mapping, int64_t num_tokens, void* k_pool,
+                  void* v_pool, int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, int dtype,
+                  void* stream);
+
+/*
+ * mi_kv_store_chunks — PagedRunner.store_prefill (worker/paged_runner.py:104-136) on the device:
+ * row b's valid tokens are the last chunk_lens[b] positions of the padded length `padded_len`;
+ * token j goes to logical position start_positions[b] + j, i.e. slot
+ * block_tables[b, pos / bs] * bs + pos % bs.  No host-side slot list is needed.
+ * Source strides as in mi_kv_scatter.  chunk_lens/start_positions are int64 [batch] on device.
+ */
+int mi_kv_store_chunks(const void* k_src, const void* v_src, const int64_t* k_strides, const int64_t* v_strides,
+                       int64_t batch, int64_t padded_len, const int64_t* chunk_lens, const int64_t* start_positions,
+                       const int64_t* block_tables, int64_t table_stride, void* k_pool, void* v_pool,
+                       int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, int dtype, void* stream);
+
+/*
+ * mi_kv_gather_blocks — PagedKVCachePool.gather_blocks for one pool (worker/paged_kv_cache.py:54-72):
+ * out[b, j] = pool[block_ids[b, j]], out contiguous [batch, blocks_per_row, bs, H_kv, D].
+ */
+int mi_kv_gather_blocks(const void* pool, const int64_t* block_ids, int64_t batch, int64_t blocks_per_row,
+                        void* out, int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, int dtype,
+                        void* stream);
+
+/*
+ * mi_paged_decode — one decode step of paged GQA attention for one layer (one query token per
+ * sequence).  Replaces the history gather + _attend of the paged branch
+ * (model/qwen3.py:285-292 and :219-255, bias of :513-527): sequence b attends to positions
+ * [0, context_lens[b]) of its block table; query head hq reads KV head hq / (num_q_heads/num_kv_heads).
+ * Softmax and accumulation are fp32.  The new token must already be in the pool (mi_kv_scatter),
+ * unless k_new/v_new/slot_mapping are given, in which case they are appended first (same launch
+ * sequence, same stream).
+ *
+ *   q        [batch, num_q_heads, head_dim]  element (b, h, d) at b*q_strides[0] + h*q_strides[1] + d
+ *   out      [batch, num_q_heads*head_dim]   row b at b*out_stride
+ *   k_new    [batch, num_kv_heads, head_dim] (optional) strides new_strides[0..1]
+ *   workspace  >= mi_paged_decode_workspace_size(...) bytes, 256-byte aligned (split-K partials)
+ */
+size_t mi_paged_decode_workspace_size(int64_t batch, int num_q_heads, int num_kv_heads, int head_dim,
+                                      int64_t max_blocks_per_seq, int block_size, int dtype);
+int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,
+                    const int64_t* new_strides, const int64_t* slot_mapping, void* k_pool, void* v_pool,
+                    int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                    const int64_t* block_tables, int64_t table_stride, int64_t max_blocks_per_seq,
+                    const int64_t* context_lens, int64_t batch, int num_q_heads, float scale, void* out,
+                    int64_t out_stride, void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/*
+ * mi_paged_prefill — varlen chunked-prefill attention for one layer.  Replaces, for
+ * PagedRunner.run_prefill_chunk_step (worker/paged_runner.py:32-102), the all-layer history
+ * gather (gather_blocks), torch.cat(history, chunk) (model/qwen3.py:328-329), the padded causal
+ * mask (:438-485) and _attend (:219-255).  Row b's chunk holds chunk_lens[b] valid tokens
+ * right-aligned in padded_len (left padding); its token j is logical position
+ * start_positions[b] + j and attends causally to the chunk and to the first start_positions[b]
+ * positions of its history, read in place from the pools through block_tables.
+ * Output rows of padding positions are written as zeros.
+ *
+ *   q        [batch, padded_len, num_q_heads, head_dim], element (b,p,h,d) at
+ *            b*q_strides[0] + p*q_strides[1] + h*q_strides[2] + d
+ *   k_chunk  [batch, padded_len, num_kv_heads, head_dim], strides kv_strides[0..2] (v_chunk same)
+ *   out      [batch, padded_len, num_q_heads*head_dim] contiguous
+ */
+int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chunk, const void* v_chunk,
+                     const int64_t* kv_strides, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                     int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
+                     int64_t table_stride, const int64_t* start_positions, const int64_t* chunk_lens, int64_t batch,
+                     int64_t padded_len, int num_q_heads, float scale, void* out, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MI_PAGED_H */

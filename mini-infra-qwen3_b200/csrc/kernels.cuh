@@ -1,0 +1,130 @@
+// Kernel argument blocks and launcher declarations shared by the .cu files and the C-ABI layer.
+// All strides here are in BYTES (the C-ABI takes element strides and converts).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mi {
+
+struct ScatterArgs {
+  const char* k_src;
+  const char* v_src;
+  int64_t k_sb[3];  // row, head, position
+  int64_t v_sb[3];
+  const int64_t* rows;       // may be null: row = token index
+  const int64_t* positions;  // may be null: position 0
+  const int64_t* slots;
+  int64_t num_tokens;
+  int64_t src_rows;       // bounds of the source: rows and positions
+  int64_t src_positions;
+  char* k_pool;
+  char* v_pool;
+  int64_t num_slots;
+  int heads;
+  int row_bytes;  // head_dim * element size
+};
+
+struct StoreChunksArgs {
+  const char* k_src;
+  const char* v_src;
+  int64_t k_sb[3];
+  int64_t v_sb[3];
+  int64_t batch;
+  int64_t padded_len;
+  const int64_t* chunk_lens;
+  const int64_t* starts;
+  const int64_t* block_tables;
+  int64_t table_stride;
+  char* k_pool;
+  char* v_pool;
+  int64_t num_blocks;
+  int block_size;
+  int heads;
+  int row_bytes;
+};
+
+struct GatherArgs {
+  const char* pool;
+  const int64_t* block_ids;
+  char* out;
+  int64_t num_blocks;
+  int64_t block_bytes;
+};
+
+cudaError_t launch_kv_scatter(const ScatterArgs& a, int vec_bytes, cudaStream_t s);
+cudaError_t launch_kv_store_chunks(const StoreChunksArgs& a, int vec_bytes, cudaStream_t s);
+cudaError_t launch_kv_gather_blocks(const GatherArgs& a, int64_t items, int vec_bytes, cudaStream_t s);
+
+// ------------------------------------------------------------------------------------------
+// Paged decode
+// ------------------------------------------------------------------------------------------
+struct DecodeArgs {
+  const char* q;
+  int64_t q_sb, q_sh;  // bytes
+  const char* k_pool;  // used by the scalar path (the TMA path reads through tensor maps)
+  const char* v_pool;
+  const int64_t* block_tables;
+  int64_t table_stride;
+  int64_t max_blocks;  // columns of block_tables that are valid to read
+  const int64_t* context_lens;
+  int64_t batch;
+  int64_t num_blocks;
+  int hq, hkv, groups;
+  int head_dim;
+  int block_size;
+  float scale_log2;  // softmax scale * log2(e)
+  int split_pages;   // pages handled by one split
+  int max_splits;    // grid.x of the split kernel
+  int parts_per_split;
+  int max_parts;     // max_splits * parts_per_split
+  float* ws_o;       // [batch, hq, max_parts, head_dim]
+  float* ws_ml;      // [batch, hq, max_parts, 2]
+  char* out;
+  int64_t out_sb;    // bytes
+};
+
+struct DecodePlan {
+  bool use_mma;
+  int heads_per_cta;  // HB
+  int parts_per_split;
+  int split_pages;
+  int max_splits;
+  size_t ws_bytes;
+};
+
+DecodePlan plan_decode(int64_t batch, int hq, int hkv, int head_dim, int64_t max_blocks, int block_size, int dtype);
+
+// Launches the split kernel and the combine kernel (or the scalar single-pass kernel).
+cudaError_t launch_paged_decode(const DecodeArgs& a, const DecodePlan& plan, const CUtensorMap* tm_k,
+                                const CUtensorMap* tm_v, int dtype, cudaStream_t s);
+
+// ------------------------------------------------------------------------------------------
+// Paged chunked prefill
+// ------------------------------------------------------------------------------------------
+struct PrefillArgs {
+  const char* q;
+  int64_t q_sb[3];  // row, position, head (bytes)
+  const char* k_chunk;
+  const char* v_chunk;
+  int64_t kv_sb[3];
+  const char* k_pool;
+  const char* v_pool;
+  int64_t num_blocks;
+  const int64_t* block_tables;
+  int64_t table_stride;
+  const int64_t* starts;
+  const int64_t* chunk_lens;
+  int64_t batch;
+  int64_t padded_len;
+  int hq, hkv, groups;
+  int head_dim;
+  int block_size;
+  float scale_log2;
+  char* out;  // [batch, padded_len, hq*head_dim] contiguous
+};
+
+cudaError_t launch_paged_prefill(const PrefillArgs& a, int dtype, cudaStream_t s);
+
+}  // namespace mi

@@ -1,0 +1,6 @@
+// Unity translation unit of libmi_paged.so: one TU so that the device status word and the kernels
+// share one module without relocatable device code.
+#include "kv_scatter.cu"
+#include "paged_decode.cu"
+#include "paged_prefill.cu"
+#include "api.cu"

@@ -1,0 +1,113 @@
+"""Paged backend (reference ``engine/paged_schedule_backend.py``): glues scheduler, runner and pool.
+
+Per prefill step: chunk forward (model_ms, StepTimer), then ``store_prefill`` timed as cache_ms
+(host wall clock between two synchronisations).  Per decode step: host packing + H2D timed as
+cache_ms, then the decode forward (model_ms).  ``accessed_kv_cache_tokens`` counts history tokens
+read: sum of chunk starts (prefill) and sum of context lengths (decode).
+"""
+
+from __future__ import annotations
+
+import time
+from collections.abc import Sequence
+
+import torch
+
+from mini_infra_b200.core.block_manager import KVCacheManager, num_blocks_for_tokens, required_pool_blocks
+from mini_infra_b200.core.request import Request, RequestState
+from mini_infra_b200.core.scheduler import PrefillChunk
+from mini_infra_b200.core.types import BatchingMethod, PagedCacheConfig
+from mini_infra_b200.device import synchronize
+from mini_infra_b200.engine.metrics import PagedCacheProfile
+from mini_infra_b200.engine.schedule_backend import ScheduleStepOutput
+from mini_infra_b200.worker import PagedKVCachePool, PagedRunner
+
+
+class PagedScheduleBackend:
+    def __init__(
+        self,
+        model: torch.nn.Module,
+        requests: Sequence[Request],
+        max_running_requests: int,
+        paged_cache_config: PagedCacheConfig,
+        batching_method: BatchingMethod = BatchingMethod.CONTINUOUS,
+        pad_token_id: int = 0,
+    ) -> None:
+        self.model = model
+        self.device = next(model.parameters()).device
+        self.max_running_requests = max_running_requests
+        self.batching_method = batching_method
+        self.paged_cache_config = paged_cache_config
+        self.block_size = paged_cache_config.block_size
+        num_blocks = paged_cache_config.num_blocks or required_pool_blocks(
+            requests, max_running_requests, self.block_size)
+        largest = max(num_blocks_for_tokens(r.prompt_len + r.max_new_tokens - 1, self.block_size) for r in requests)
+        if largest > num_blocks - 1:
+            raise ValueError(f"num_blocks={num_blocks} cannot hold one request's {largest} blocks (+1 null block)")
+        config = model.config  # type: ignore[attr-defined]
+        attn = model.model.layers[0].self_attn  # type: ignore[attr-defined]
+        self.runner = PagedRunner(model, pad_token_id)
+        self.pool = PagedKVCachePool(
+            num_layers=config.num_hidden_layers,
+            num_blocks=num_blocks,
+            block_size=self.block_size,
+            num_kv_heads=attn.num_kv_heads,
+            head_dim=config.head_dim,
+            dtype=next(model.parameters()).dtype,
+            device=self.device,
+        )
+        self.kv_cache_manager = KVCacheManager(self.block_size, num_blocks)
+
+    @property
+    def kv_cache_config(self) -> PagedCacheConfig:
+        return self.paged_cache_config
+
+    def execute_prefill(self, chunks: Sequence[PrefillChunk]) -> ScheduleStepOutput:
+        tables = [self.kv_cache_manager.block_table(c.state.request.request_idx) for c in chunks]
+        starts = [c.start for c in chunks]
+        out = self.runner.run_prefill_chunk_step(
+            [c.state.request.token_ids[c.start : c.end] for c in chunks], starts, tables, self.pool)
+        synchronize(self.device)
+        t0 = time.perf_counter()
+        self.runner.store_prefill(self.pool, out.prefill_cache, tables, [c.num_tokens for c in chunks], starts)
+        synchronize(self.device)
+        cache_ms = (time.perf_counter() - t0) * 1000.0
+        return ScheduleStepOutput(
+            next_tokens=[t for t, c in zip(out.next_tokens, chunks) if c.is_last],
+            model_ms=out.model_ms,
+            cache_ms=cache_ms,
+            physical_batch_size=len(chunks),
+            live_kv_cache_bytes=self.kv_cache_manager.num_used_blocks * self.pool.bytes_per_block,
+            kv_cache_pool_bytes=self.pool.total_bytes,
+            accessed_kv_cache_tokens=sum(starts),
+        )
+
+    def execute_decode(self, scheduled: Sequence[RequestState]) -> ScheduleStepOutput:
+        synchronize(self.device)
+        t0 = time.perf_counter()
+        ids, pos, md = self.runner.prepare_decode_inputs(
+            [self.kv_cache_manager.block_table(s.request.request_idx) for s in scheduled],
+            last_tokens=[s.generated[-1] for s in scheduled],
+            positions=[s.cache_length for s in scheduled],
+            block_size=self.block_size,
+        )
+        synchronize(self.device)
+        cache_ms = (time.perf_counter() - t0) * 1000.0
+        out = self.runner.run_decode_step(ids, pos, md, self.pool)
+        return ScheduleStepOutput(
+            next_tokens=out.next_tokens,
+            model_ms=out.model_ms,
+            cache_ms=cache_ms,
+            physical_batch_size=len(scheduled),
+            live_kv_cache_bytes=self.kv_cache_manager.num_used_blocks * self.pool.bytes_per_block,
+            kv_cache_pool_bytes=self.pool.total_bytes,
+            accessed_kv_cache_tokens=sum(s.cache_length + 1 for s in scheduled),
+        )
+
+    def retire(self, finished: Sequence[RequestState], *, is_idle: bool) -> None:
+        return None
+
+    def collect_paged_cache_profile(self) -> PagedCacheProfile:
+        m = self.kv_cache_manager
+        return PagedCacheProfile(self.block_size, self.pool.bytes_per_block, self.pool.num_blocks, m.peak_used_blocks,
+                                 m.block_cold_allocation_count, m.block_reuse_count, m.block_release_count)

@@ -1,0 +1,279 @@
+"""Qwen3 causal LM whose attention runs on the paged-KV CUDA kernels.
+
+Projections, norms, RoPE, MLP and lm_head are plain PyTorch (cuBLAS GEMMs, elementwise ops) with
+the reference's numerics (``model/qwen3.py``: fp32 RMSNorm statistics :67-78, fp32 RoPE angles
+cast to the model dtype :95-109, rotate-half RoPE :112-144).  Attention has two entry forms:
+
+* ``PagedAttentionMetadata`` (decode, one token per row, same fields as the reference :27-42):
+  the new K/V are appended at ``slot_mapping`` and attention reads history in place through
+  ``block_tables`` — ``mi_paged_decode``;
+* ``ChunkPrefillMetadata`` (chunked prefill): each row's chunk is right-aligned in the padded
+  length; history is read in place from the pools — ``mi_paged_prefill``.  With no metadata the
+  call is a prefill without history (all rows start at position 0, left padding from
+  ``attention_mask``).
+
+Tensor layout inside the model: activations [B, L, hidden]; Q/K/V [B, L, heads, head_dim].
+Present K/V returned by prefill are [B, H_kv, L, D] views (the reference's ``KVCache`` layout).
+
+Head partition (``tp_world > 1``): the layer keeps query heads [r*Hq/P, (r+1)*Hq/P) and KV heads
+[r*H/P, (r+1)*H/P); its pools hold only those KV heads; the attention output is all-gathered
+over the process group before the replicated o_proj.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from typing import NamedTuple
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from mini_infra_b200 import ops
+from mini_infra_b200.model.config import Qwen3Config
+
+PastKeyValue = tuple[torch.Tensor, torch.Tensor]
+
+
+class PagedAttentionMetadata(NamedTuple):
+    """Decode-step addressing (reference model/qwen3.py:27-42).
+
+    slot_mapping [B] int64: slot of the new token; block_tables [B, max_blocks] int64, null-padded;
+    context_lens [B] int64 including the new token; kv_pools: per layer (key_pool, value_pool).
+    """
+
+    slot_mapping: torch.Tensor
+    block_tables: torch.Tensor
+    context_lens: torch.Tensor
+    kv_pools: tuple[PastKeyValue, ...] = ()
+
+
+class ChunkPrefillMetadata(NamedTuple):
+    """Chunked-prefill addressing: history tables [B, nb] (null-padded, may have 0 columns),
+    start_positions [B] (history length per row), chunk_lens [B] (valid tokens, right-aligned)."""
+
+    block_tables: torch.Tensor
+    start_positions: torch.Tensor
+    chunk_lens: torch.Tensor
+    kv_pools: tuple[PastKeyValue, ...] = ()
+
+
+class DenseAttentionMetadata(NamedTuple):
+    """Kept for API compatibility; the dense KV path is not part of this package."""
+
+    past_key_values: tuple[PastKeyValue, ...]
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, hidden_size: int, eps: float):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(hidden_size))
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dtype = x.dtype
+        xf = x.float()
+        normed = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
+        return self.weight * normed.to(dtype)
+
+
+class RotaryEmbedding(nn.Module):
+    def __init__(self, head_dim: int, rope_theta: float):
+        super().__init__()
+        exponents = torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim
+        self.register_buffer("inv_freq", 1.0 / (rope_theta**exponents), persistent=False)
+
+    def forward(self, position_ids: torch.Tensor, dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
+        """cos/sin [B, L, D] in `dtype`, from fp32 angles."""
+        angles = position_ids.float().unsqueeze(-1) * self.inv_freq
+        emb = torch.cat((angles, angles), dim=-1)
+        return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [B, L, heads, D] rotated by cos/sin [B, L, 1, D] (rotate-half form)."""
+    half = x.shape[-1] // 2
+    rotated = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * cos + rotated * sin
+
+
+class HeadPartition(NamedTuple):
+    """Which slice of the heads this process owns (rank r of world P)."""
+
+    rank: int = 0
+    world: int = 1
+    group: object | None = None
+
+
+def gather_heads(attn: torch.Tensor, partition: HeadPartition) -> torch.Tensor:
+    """[N, local heads * D] -> [N, all heads * D] in global head order (NCCL all-gather over the
+    partition's group; rank r contributes query heads [r*Hq/P, (r+1)*Hq/P))."""
+    if partition.world == 1:
+        return attn
+    import torch.distributed as dist
+
+    n, width = attn.shape
+    gathered = torch.empty((partition.world * n, width), dtype=attn.dtype, device=attn.device)
+    dist.all_gather_into_tensor(gathered, attn.contiguous(), group=partition.group)
+    return gathered.view(partition.world, n, width).transpose(0, 1).reshape(n, partition.world * width)
+
+
+class Qwen3Attention(nn.Module):
+    def __init__(self, config: Qwen3Config, partition: HeadPartition = HeadPartition()):
+        super().__init__()
+        if config.num_key_value_heads % partition.world:
+            raise ValueError(f"{config.num_key_value_heads} KV heads cannot be split over {partition.world} ranks")
+        self.partition = partition
+        self.head_dim = config.head_dim
+        self.num_heads = config.num_attention_heads // partition.world
+        self.num_kv_heads = config.num_key_value_heads // partition.world
+        self.scaling = config.head_dim**-0.5
+        self.q_proj = nn.Linear(config.hidden_size, self.num_heads * self.head_dim, bias=False)
+        self.k_proj = nn.Linear(config.hidden_size, self.num_kv_heads * self.head_dim, bias=False)
+        self.v_proj = nn.Linear(config.hidden_size, self.num_kv_heads * self.head_dim, bias=False)
+        self.o_proj = nn.Linear(config.num_attention_heads * self.head_dim, config.hidden_size, bias=False)
+        self.q_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
+        self.k_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
+
+    def _project(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+        b, length, _ = x.shape
+        q = self.q_norm(self.q_proj(x).view(b, length, self.num_heads, self.head_dim))
+        k = self.k_norm(self.k_proj(x).view(b, length, self.num_kv_heads, self.head_dim))
+        v = self.v_proj(x).view(b, length, self.num_kv_heads, self.head_dim)
+        cos, sin = cos.unsqueeze(2), sin.unsqueeze(2)
+        return _rotate(q, cos, sin), _rotate(k, cos, sin), v
+
+    def forward(self, x, cos, sin, kv_pool: PastKeyValue | None, metadata):
+        b, length, _ = x.shape
+        q, k, v = self._project(x, cos, sin)
+        if isinstance(metadata, PagedAttentionMetadata):
+            key_pool, value_pool = kv_pool
+            attn = ops.paged_decode(
+                q.view(b, self.num_heads, self.head_dim), key_pool, value_pool, metadata.block_tables,
+                metadata.context_lens, self.scaling, key_new=k.view(b, self.num_kv_heads, self.head_dim),
+                value_new=v.view(b, self.num_kv_heads, self.head_dim), slot_mapping=metadata.slot_mapping,
+            )
+            present = kv_pool
+        else:
+            key_pool, value_pool = kv_pool if kv_pool is not None else (None, None)
+            attn = ops.paged_prefill(
+                q, k, v, key_pool, value_pool, metadata.block_tables, metadata.start_positions, metadata.chunk_lens,
+                self.scaling,
+            ).view(b * length, self.num_heads * self.head_dim)
+            present = (k.transpose(1, 2), v.transpose(1, 2))
+        attn = gather_heads(attn.view(b * length, -1), self.partition).view(b, length, -1)
+        return self.o_proj(attn), present
+
+
+class Qwen3MLP(nn.Module):
+    def __init__(self, config: Qwen3Config):
+        super().__init__()
+        self.gate_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
+        self.up_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+class Qwen3DecoderLayer(nn.Module):
+    def __init__(self, config: Qwen3Config, partition: HeadPartition = HeadPartition()):
+        super().__init__()
+        self.self_attn = Qwen3Attention(config, partition)
+        self.mlp = Qwen3MLP(config)
+        self.input_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+
+    def forward(self, x, cos, sin, kv_pool, metadata):
+        attn, present = self.self_attn(self.input_layernorm(x), cos, sin, kv_pool, metadata)
+        x = x + attn
+        x = x + self.mlp(self.post_attention_layernorm(x))
+        return x, present
+
+
+class Qwen3Model(nn.Module):
+    def __init__(self, config: Qwen3Config, partition: HeadPartition = HeadPartition()):
+        super().__init__()
+        self.config = config
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
+        self.layers = nn.ModuleList([Qwen3DecoderLayer(config, partition) for _ in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.rotary_emb = RotaryEmbedding(config.head_dim, config.rope_theta)
+
+    def forward(self, input_ids, attention_mask=None, position_ids=None, attn_metadata=None):
+        if input_ids.ndim != 2 or input_ids.shape[1] < 1:
+            raise ValueError("input_ids must be a non-empty [batch, sequence] tensor")
+        b, length = input_ids.shape
+        device = input_ids.device
+        hidden = self.embed_tokens(input_ids)
+        if isinstance(attn_metadata, DenseAttentionMetadata):
+            raise NotImplementedError("the dense KV path is out of scope here; use PagedAttentionMetadata")
+        if isinstance(attn_metadata, PagedAttentionMetadata):
+            if length != 1:
+                raise ValueError("paged decode input_ids must be [batch, 1]")
+            if position_ids is None or position_ids.shape != (b, 1):
+                raise ValueError("paged decode needs position_ids of shape [batch, 1]")
+            if len(attn_metadata.kv_pools) != len(self.layers):
+                raise ValueError("kv_pools must hold one (key, value) pool pair per layer")
+            pools = attn_metadata.kv_pools
+        elif attn_metadata is None:
+            if attention_mask is None:
+                lens = torch.full((b,), length, dtype=torch.long, device=device)
+            else:
+                if attention_mask.shape != (b, length):
+                    raise ValueError(f"attention_mask must be {(b, length)}, got {tuple(attention_mask.shape)}")
+                lens = attention_mask.to(torch.long).sum(dim=1)
+            if position_ids is None:
+                position_ids = torch.arange(length, device=device).unsqueeze(0).expand(b, -1)
+            attn_metadata = ChunkPrefillMetadata(
+                block_tables=torch.empty((b, 0), dtype=torch.long, device=device),
+                start_positions=torch.zeros((b,), dtype=torch.long, device=device),
+                chunk_lens=lens,
+            )
+            pools = [None] * len(self.layers)
+        else:
+            if position_ids is None or position_ids.shape != (b, length):
+                raise ValueError("chunked prefill needs position_ids of shape [batch, length]")
+            pools = attn_metadata.kv_pools if attn_metadata.kv_pools else [None] * len(self.layers)
+        cos, sin = self.rotary_emb(position_ids, hidden.dtype)
+        presents = []
+        for layer, pool in zip(self.layers, pools):
+            hidden, present = layer(hidden, cos, sin, pool, attn_metadata)
+            presents.append(present)
+        return self.norm(hidden), presents
+
+
+class Qwen3ForCausalLM(nn.Module):
+    def __init__(self, config: Qwen3Config, partition: HeadPartition = HeadPartition()):
+        super().__init__()
+        self.config = config
+        self.partition = partition
+        self.model = Qwen3Model(config, partition)
+        self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+        self.tie_weights()
+
+    def tie_weights(self) -> None:
+        self.lm_head.weight = self.model.embed_tokens.weight
+
+    def forward(self, input_ids, attention_mask=None, position_ids=None, attn_metadata=None, last_only=False):
+        """Logits [B, L, V] (or [B, 1, V] of the last position when ``last_only``) and per-layer presents."""
+        hidden, presents = self.model(input_ids, attention_mask, position_ids, attn_metadata)
+        if last_only:
+            hidden = hidden[:, -1:, :]
+        return self.lm_head(hidden), presents
+
+
+__all__ = [
+    "ChunkPrefillMetadata",
+    "DenseAttentionMetadata",
+    "HeadPartition",
+    "PagedAttentionMetadata",
+    "PastKeyValue",
+    "Qwen3Attention",
+    "Qwen3DecoderLayer",
+    "Qwen3ForCausalLM",
+    "Qwen3MLP",
+    "Qwen3Model",
+    "RMSNorm",
+    "RotaryEmbedding",
+]

@@ -1,0 +1,150 @@
+"""Paged KV-cache executor (reference ``worker/paged_runner.py`` API).
+
+Stateless; takes block tables as ``list[list[int]]`` from the control plane and packs each
+step's integer metadata into ONE int64 host buffer, copied to the device in one transfer, whose
+sections become contiguous views (ids, positions, starts/lengths or slots/context lengths, block
+tables).  Attention reads history in place from the pools; nothing gathers the history.
+
+* ``run_prefill_chunk_step`` — left-padded chunk forward; history of row i is the first
+  ceil(start_i / bs) blocks of its table; returns the chunk's K/V as ``prefill_cache``
+  ([B, H_kv, L, D] per layer, valid tokens right-aligned) and the greedy token of each row's
+  last position;
+* ``store_prefill`` — writes those tokens to their slots; the slot arithmetic
+  (table[pos // bs] * bs + pos % bs) runs on the device;
+* ``prepare_decode_inputs`` / ``run_decode_step`` — decode step, append fused in the attention op.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from typing import NamedTuple
+
+import torch
+
+from mini_infra_b200.device import StepTimer
+from mini_infra_b200.model.qwen3 import ChunkPrefillMetadata, PagedAttentionMetadata
+from mini_infra_b200.worker.base_runner import BaseModelRunner, PrefillOutput
+from mini_infra_b200.worker.kv_cache import KVCache
+from mini_infra_b200.worker.paged_kv_cache import PagedKVCachePool
+from mini_infra_b200.worker.sampler import greedy_sample
+
+_NULL_BLOCK_ID = 0
+
+
+class PagedDecodeOutput(NamedTuple):
+    next_tokens: list[int]
+    model_ms: float
+
+
+def _to_device(values: list[int], device: torch.device) -> torch.Tensor:
+    """One pinned host buffer -> one asynchronous H2D copy."""
+    host = torch.tensor(values, dtype=torch.long)
+    if device.type == "cuda":
+        host = host.pin_memory()
+    return host.to(device, non_blocking=True)
+
+
+class PagedRunner(BaseModelRunner):
+    def run_prefill_chunk_step(
+        self,
+        chunk_token_ids: Sequence[Sequence[int]],
+        start_positions: Sequence[int],
+        block_tables: Sequence[Sequence[int]],
+        pool: PagedKVCachePool | None,
+    ) -> PrefillOutput:
+        b = len(chunk_token_ids)
+        lens = [len(t) for t in chunk_token_ids]
+        if b == 0 or min(lens) < 1:
+            raise ValueError("every chunk must hold at least one token")
+        width = max(lens)
+        bs = pool.block_size if pool is not None else 1
+        n_hist = [-(-int(s) // bs) for s in start_positions]
+        if pool is None and any(n_hist):
+            raise ValueError("a chunk with history needs the pool")
+        nb = max(n_hist)
+        flat: list[int] = []
+        for toks, n in zip(chunk_token_ids, lens):
+            flat += [self.pad_token_id] * (width - n) + [int(t) for t in toks]
+        for s, n in zip(start_positions, lens):
+            flat += [0] * (width - n) + list(range(int(s), int(s) + n))
+        flat += [int(s) for s in start_positions] + lens
+        for table, h in zip(block_tables, n_hist):
+            if len(table) < h:
+                raise ValueError(f"block table {list(table)} does not cover {h} history blocks")
+            flat += [int(x) for x in table[:h]] + [_NULL_BLOCK_ID] * (nb - h)
+        packed = _to_device(flat, self.device)
+        o = b * width
+        input_ids = packed[:o].view(b, width)
+        position_ids = packed[o : 2 * o].view(b, width)
+        starts = packed[2 * o : 2 * o + b]
+        chunk_lens = packed[2 * o + b : 2 * o + 2 * b]
+        tables = packed[2 * o + 2 * b :].view(b, nb)
+        metadata = ChunkPrefillMetadata(
+            block_tables=tables, start_positions=starts, chunk_lens=chunk_lens,
+            kv_pools=tuple(pool.kv_pools) if pool is not None else (),
+        )
+        with StepTimer(self.device) as timer:
+            logits, presents = self.model(input_ids, position_ids=position_ids, attn_metadata=metadata, last_only=True)
+            next_token, _ = greedy_sample(logits)
+        return PrefillOutput(next_token.squeeze(-1).tolist(), KVCache(presents), timer.elapsed_ms)
+
+    def store_prefill(
+        self,
+        pool: PagedKVCachePool,
+        prefill_cache: KVCache,
+        block_tables: Sequence[Sequence[int]],
+        chunk_lens: Sequence[int],
+        start_positions: Sequence[int],
+    ) -> None:
+        """Write each row's last chunk_lens[i] tokens to logical positions start_i ... (no sync, no timing)."""
+        b = len(block_tables)
+        bs = pool.block_size
+        need = [-(-(int(s) + int(n)) // bs) for s, n in zip(start_positions, chunk_lens)]
+        for table, k in zip(block_tables, need):
+            if len(table) < k:
+                raise ValueError(f"block table {list(table)} does not cover {k} blocks")
+        width = max(max(need), 1)
+        flat = [int(n) for n in chunk_lens] + [int(s) for s in start_positions]
+        for table, k in zip(block_tables, need):
+            flat += [int(x) for x in table[:k]] + [_NULL_BLOCK_ID] * (width - k)
+        packed = _to_device(flat, self.device)
+        pool.store_chunks(prefill_cache, packed[:b], packed[b : 2 * b], packed[2 * b :].view(b, width))
+
+    def prepare_decode_inputs(
+        self,
+        block_tables: Sequence[Sequence[int]],
+        last_tokens: Sequence[int],
+        positions: Sequence[int],
+        block_size: int,
+    ) -> tuple[torch.Tensor, torch.Tensor, PagedAttentionMetadata]:
+        """ids [B,1], positions [B,1], metadata (slot_mapping, null-padded block_tables, context_lens)."""
+        b = len(block_tables)
+        max_blocks = max(len(t) for t in block_tables)
+        slots = [int(t[p // block_size]) * block_size + p % block_size for t, p in zip(block_tables, positions)]
+        flat = [int(x) for x in last_tokens] + [int(p) for p in positions] + slots + [int(p) + 1 for p in positions]
+        for t in block_tables:
+            flat += [int(x) for x in t] + [_NULL_BLOCK_ID] * (max_blocks - len(t))
+        packed = _to_device(flat, self.device)
+        metadata = PagedAttentionMetadata(
+            slot_mapping=packed[2 * b : 3 * b],
+            block_tables=packed[4 * b :].view(b, max_blocks),
+            context_lens=packed[3 * b : 4 * b],
+        )
+        return packed[:b].view(b, 1), packed[b : 2 * b].view(b, 1), metadata
+
+    def run_decode_step(
+        self,
+        input_ids: torch.Tensor,
+        position_ids: torch.Tensor,
+        metadata: PagedAttentionMetadata,
+        pool: PagedKVCachePool,
+    ) -> PagedDecodeOutput:
+        with StepTimer(self.device) as timer:
+            logits, _ = self.model(
+                input_ids, position_ids=position_ids, attn_metadata=metadata._replace(kv_pools=tuple(pool.kv_pools))
+            )
+            next_token, _ = greedy_sample(logits)
+        return PagedDecodeOutput(next_token.squeeze(-1).tolist(), timer.elapsed_ms)
+
+
+__all__ = ["PagedDecodeOutput", "PagedRunner"]

@@ -1,0 +1,106 @@
+"""End-to-end paged engine on the GPU.
+
+* C1 tiny model (fp32): greedy token ids identical to what the REFERENCE engine produced
+  (tests/golden/engine.json), for 32 and 64 decode steps, tied and untied heads, prefill-first
+  and chunked-prefill — the drop-in claim for caching-method=paged-kv-cache.
+* Runner-level checks mirroring the reference's own paged tests: chunked prefill in rounds
+  leaves the same K/V in the pool as a one-shot prefill and yields the same first token.
+"""
+
+import json
+from pathlib import Path
+
+import pytest
+import torch
+
+from mini_infra_b200.core import (
+    BatchingMethod, ChunkedPrefillConfig, KVCacheManager, PagedCacheConfig, PrefillFirstConfig, SchedulerConfig,
+    make_requests,
+)
+from mini_infra_b200.engine import EngineConfig, run_scheduler
+from mini_infra_b200.model import Qwen3Config, build_model
+from mini_infra_b200 import ops
+from mini_infra_b200.worker import PagedKVCachePool, PagedRunner
+
+GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "engine.json").read_text())
+pytestmark = pytest.mark.gpu
+
+
+def c1_model(tied: bool):
+    cfg = Qwen3Config(**GOLDEN["model"], torch_dtype="float32")
+    return build_model(cfg, seed=GOLDEN["weight_seed"], device="cuda", dtype=torch.float32,
+                       untied_head_seed=None if tied else 1234)
+
+
+@pytest.fixture(autouse=True)
+def no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+@pytest.mark.parametrize("case", GOLDEN["cases"], ids=lambda c: c["name"])
+def test_engine_tokens_identical_to_reference(case):
+    model = c1_model(case["tied"])
+    policy = PrefillFirstConfig() if case["batching_policy"] == "prefill-first" else ChunkedPrefillConfig(
+        case["token_budget"])
+    cfg = EngineConfig(PagedCacheConfig(block_size=16), BatchingMethod.CONTINUOUS,
+                       scheduler_config=SchedulerConfig(case["max_running_requests"], policy))
+    result = run_scheduler(cfg, model, make_requests(case["prompts"], case["max_new_tokens"]), None,
+                           stop_on_eos=False)
+    assert [s.token_ids for s in result.sequences] == case["tokens"]
+    assert result.schedule_metrics.num_prefill_steps == case["num_prefill_steps"]
+    assert result.schedule_metrics.num_decode_steps == case["num_decode_steps"]
+    assert result.paged_cache is not None and result.paged_cache.peak_used_blocks > 0
+    assert ops.read_status() == 0
+
+
+@pytest.mark.parametrize("block_size", [1, 3, 4, 16])
+def test_chunked_prefill_rounds_match_one_shot_prefill(block_size):
+    model = c1_model(tied=False)
+    prompts = [[(j * 5 + 3) % 80 + 1 for j in range(11)], [(j * 7 + 2) % 80 + 1 for j in range(6)]]
+    rounds = [[(0, 0, 5), (1, 0, 2)], [(0, 5, 8), (1, 2, 6)], [(0, 8, 11)]]
+    cfg = model.config
+    manager = KVCacheManager(block_size, num_blocks=64)
+    pool = PagedKVCachePool(cfg.num_hidden_layers, 64, block_size, cfg.num_key_value_heads, cfg.head_dim,
+                            torch.float32, torch.device("cuda"))
+    runner = PagedRunner(model)
+    first = {}
+    with torch.inference_mode():
+        for chunks in rounds:
+            for idx, s, e in chunks:
+                assert manager.allocate_slots(idx, e - s)
+            tables = [manager.block_table(idx) for idx, _, _ in chunks]
+            starts = [s for _, s, _ in chunks]
+            out = runner.run_prefill_chunk_step([prompts[i][s:e] for i, s, e in chunks], starts, tables, pool)
+            runner.store_prefill(pool, out.prefill_cache, tables, [e - s for _, s, e in chunks], starts)
+            for (idx, _, e), tok in zip(chunks, out.next_tokens):
+                if e == len(prompts[idx]):
+                    first[idx] = tok
+        for idx, prompt in enumerate(prompts):
+            whole = runner.run_prefill_step([prompt])
+            assert whole.next_tokens[0] == first[idx]
+            for layer, (k_ref, v_ref) in enumerate(whole.prefill_cache):
+                kp, vp = pool.kv_pools[layer]
+                table = manager.block_table(idx)
+                k = torch.cat([kp[b] for b in table])[: len(prompt)].transpose(0, 1)
+                v = torch.cat([vp[b] for b in table])[: len(prompt)].transpose(0, 1)
+                torch.testing.assert_close(k, k_ref[0], atol=1e-5, rtol=0)
+                torch.testing.assert_close(v, v_ref[0], atol=1e-5, rtol=0)
+
+
+def test_prepare_decode_inputs_golden_values():
+    model = c1_model(tied=True)
+    runner = PagedRunner(model)
+    ids, pos, md = runner.prepare_decode_inputs([[9, 4], [7]], [11, 22], [5, 2], 4)
+    assert ids.tolist() == [[11], [22]] and pos.tolist() == [[5], [2]]
+    assert md.slot_mapping.tolist() == [17, 30] and md.context_lens.tolist() == [6, 3]
+    assert md.block_tables.tolist() == [[9, 4], [7, 0]]
+
+
+def test_pool_layout_and_byte_accounting():
+    pool = PagedKVCachePool(2, 10, 4, 2, 32, torch.float32, torch.device("cuda"))
+    kp, vp = pool.kv_pools[0]
+    assert kp.shape == (10, 4, 2, 32) == vp.shape and not kp.any()
+    assert pool.bytes_per_block == 2 * 2 * 4 * 2 * 32 * 4 and pool.total_bytes == 10 * pool.bytes_per_block

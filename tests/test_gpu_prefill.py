@@ -1,0 +1,81 @@
+"""Chunked-prefill paged attention against the oracle and the reference's golden outputs."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from gpu_util import assert_attention_close, to_cuda, to_numpy
+from mini_infra_b200 import ops
+from oracle import paged_oracle as po
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+pytestmark = pytest.mark.gpu
+
+
+def _tables(tables_list, starts, bs):
+    n_hist = [(s + bs - 1) // bs for s in starts]
+    nb = max(n_hist)
+    t = np.zeros((len(starts), nb), dtype=np.int64)
+    for i, (tab, n) in enumerate(zip(tables_list, n_hist)):
+        t[i, :n] = tab[:n]
+    return t
+
+
+def run_prefill(inp, bs, d):
+    # kernel layout: [B, L, heads, D]
+    q = to_cuda(inp["query"]).transpose(1, 2)
+    k = to_cuda(inp["key_chunk"]).transpose(1, 2)
+    v = to_cuda(inp["value_chunk"]).transpose(1, 2)
+    kp, vp = to_cuda(inp["key_pool"]), to_cuda(inp["value_pool"])
+    tables = torch.from_numpy(_tables(inp["tables_list"], inp["starts"], bs)).cuda()
+    out = ops.paged_prefill(q, k, v, kp, vp, tables, torch.tensor(inp["starts"]).cuda(),
+                            torch.tensor(inp["chunk_lens"]).cuda(), d**-0.5)
+    assert ops.read_status() == 0
+    return out
+
+
+@pytest.mark.parametrize("case", cases.PREFILL_CASES, ids=[c[0] for c in cases.PREFILL_CASES])
+def test_prefill_golden_cases(case):
+    name, dtype, hq, h, d, bs, starts, lens, _ = case
+    golden = np.load(GOLDEN / "prefill.npz")
+    inp = cases.prefill_inputs(case)
+    out = run_prefill(inp, bs, d)
+    want = po.chunk_prefill_attention(inp["query"], inp["key_chunk"], inp["value_chunk"], inp["key_pool"],
+                                      inp["value_pool"], inp["tables_list"], starts, lens, d**-0.5)
+    valid = golden[f"{name}/valid"]
+    got = po.as_float(to_numpy(out), np.float64)
+    assert_attention_close(got[valid], want[valid], dtype)
+    assert not got[~valid].any()  # padding rows are zeros
+    ref = po.as_float(golden[f"{name}/out"], np.float64)
+    tol = 1e-5 * np.abs(ref[valid]).max() if dtype == "float32" else 3e-2
+    assert np.abs(got[valid] - ref[valid]).max() <= tol
+
+
+def _random_prefill(hq, h, d, bs, starts, lens, dtype, seed):
+    case = ("rnd", dtype, hq, h, d, bs, starts, lens, seed)
+    return cases.prefill_inputs(case)
+
+
+RANDOM = [
+    # hq, h, d, bs, starts, lens, dtype
+    (16, 8, 128, 16, [512, 37, 0, 1000], [128, 128, 100, 7], "bfloat16"),
+    (32, 8, 128, 16, [300, 2048], [64, 128], "bfloat16"),
+    (8, 2, 64, 32, [100, 0, 64], [33, 64, 1], "bfloat16"),
+    (16, 8, 128, 16, [700, 16], [128, 128], "float32"),
+]
+
+
+@pytest.mark.parametrize("shape", RANDOM, ids=[str(s[:6]) for s in RANDOM])
+def test_prefill_random_shapes(shape):
+    hq, h, d, bs, starts, lens, dtype = shape
+    inp = _random_prefill(hq, h, d, bs, starts, lens, dtype, seed=sum(starts) % 997)
+    out = run_prefill(inp, bs, d)
+    want = po.chunk_prefill_attention(inp["query"], inp["key_chunk"], inp["value_chunk"], inp["key_pool"],
+                                      inp["value_pool"], inp["tables_list"], starts, lens, d**-0.5)
+    length = max(lens)
+    valid = np.arange(length)[None, :] >= (length - np.asarray(lens))[:, None]
+    got = po.as_float(to_numpy(out), np.float64)
+    assert_attention_close(got[valid], want[valid], dtype)
