@@ -131,15 +131,21 @@ class ClockSampler:
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8) -> dict:
-    """Time the oracle port of the reference's CPU decode (gather + GQA expand + matmul/softmax)."""
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8, rng=None, max_samples: int | None = None) -> dict:
+    """Time the torch-CPU restatement of the reference's decode (gather + GQA expand + matmul/softmax).
+
+    Runs samples of `per_sample` config-2 sequences until `seconds` of CPU work (or `max_samples`)."""
     from oracle import paged_oracle as po
 
-    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    threads = host_threads()
     torch.set_num_threads(threads)
-    rng = np.random.RandomState(SEED + 1)
+    rng = rng if rng is not None else np.random.RandomState(SEED + 1)
     total_tokens, total_t, n = 0, 0.0, 0
-    while total_t < seconds or n == 0:
+    while (total_t < seconds or n == 0) and (max_samples is None or n < max_samples):
         ctx = rng.randint(CTX_LO, CTX_HI + 1, size=per_sample).astype(np.int64)
         need = -(-ctx // BS)
         nb = 1 + int(need.sum())
@@ -149,11 +155,13 @@ def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8) -> dict:
         for i in range(per_sample):
             tables[i, : need[i]] = perm[off : off + need[i]]
             off += need[i]
-        kp = po.f32_to_bf16(rng.standard_normal((nb, BS, HKV, D)).astype(np.float32))
-        vp = po.f32_to_bf16(rng.standard_normal((nb, BS, HKV, D)).astype(np.float32))
-        q = po.f32_to_bf16(rng.standard_normal((per_sample, HQ, D)).astype(np.float32))
+        g = torch.Generator().manual_seed(int(rng.randint(1 << 30)))
+        kp = torch.randn((nb, BS, HKV, D), generator=g).to(torch.bfloat16)
+        vp = torch.randn((nb, BS, HKV, D), generator=g).to(torch.bfloat16)
+        q = torch.randn((per_sample, HQ, D), generator=g).to(torch.bfloat16)
+        tab, cx = torch.from_numpy(tables), torch.from_numpy(ctx)
         t0 = time.perf_counter()
-        po.paged_decode_attention(q, kp, vp, tables, ctx, D**-0.5)
+        po.torch_paged_decode(q, kp, vp, tab, cx, D**-0.5)
         total_t += time.perf_counter() - t0
         total_tokens += int(ctx.sum())
         n += 1
@@ -162,24 +170,35 @@ def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8) -> dict:
         "unit": "GB/s",
         "cores": threads,
         "kind": "port",
-        "sample": f"{n} x {per_sample} sequences of config 2 (ctx U[{CTX_LO},{CTX_HI}]), numpy fp32 oracle, "
-                  f"{total_t:.1f} s of CPU work",
+        "sample": f"{n} x {per_sample} sequences of config 2 (ctx U[{CTX_LO},{CTX_HI}]), bf16 torch-CPU "
+                  f"restatement of the reference's gather + GQA expand + matmul/softmax, {total_t:.1f} s of CPU work",
+        "tokens": total_tokens,
+        "seconds": total_t,
     }
 
 
-def run_reference(args) -> None:
+def run_reference(args, budget_s: float = 150.0) -> None:
+    """Reference arm: the CPU restatement of the reference's decode path on the host cores.
+
+    Each step is a bounded sample of config 2 (n_seq sequences), with n_seq sized from one probe so
+    that warmup + steps fit in about `budget_s` seconds whatever --steps is."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    per_step = []
-    cb = None
+    rng = np.random.RandomState(SEED + 2)
+    probe = cpu_decode_sample(seconds=0.0, per_sample=1, rng=rng, max_samples=1)
+    n_seq = int(max(1, min(32, (budget_s / (args.steps + args.warmup)) / max(probe["seconds"], 1e-6))))
+    tokens, secs = 0, 0.0
     for i in range(args.warmup + args.steps):
-        r = cpu_decode_sample(seconds=2.0 if i < args.warmup else 6.0)
+        r = cpu_decode_sample(seconds=0.0, per_sample=n_seq, rng=rng, max_samples=1)
         if i >= args.warmup:
-            per_step.append(r)
-            cb = r
-    value = float(np.mean([r["value"] for r in per_step]))
-    cb = dict(cb, value=value)
+            tokens += r["tokens"]
+            secs += r["seconds"]
+    value = tokens * KV_BYTES_PER_TOKEN / secs / 1e9
+    cb = {"value": value, "unit": "GB/s", "cores": host_threads(), "kind": "port",
+          "sample": f"{args.steps} timed steps x {n_seq} sequences of config 2 (ctx U[{CTX_LO},{CTX_HI}]), "
+                    f"bf16 torch-CPU restatement of the reference's gather + GQA expand + matmul/softmax, "
+                    f"{secs:.1f} s of CPU work"}
     line = {
         "metric": "paged decode KV-read GB/s", "value": value, "unit": "GB/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,

@@ -257,8 +257,36 @@ def chunk_prefill_attention(
     return out
 
 
+def torch_paged_decode(query, key_pool, value_pool, block_tables, context_lens, scale: float):
+    """The reference's decode attention as the same torch CPU op sequence, in the operands' dtype.
+
+    query [B, Hq, D]; pools [N, bs, H_kv, D]; block_tables [B, nb]; context_lens [B] (torch CPU
+    tensors).  Follows model/qwen3.py:288-291 (block-table gather of the padded history), :513-527
+    (finfo.min bias beyond the context), :147-156 (repeat_interleave GQA expand) and :243-255
+    (scaled scores + bias, fp32 softmax, probs cast back, probs @ V).  Used as the timed CPU
+    baseline (it costs what the reference costs) and pinned to the reference's golden outputs.
+    """
+    import torch
+
+    b, hq, d = query.shape
+    _, bs, h, _ = key_pool.shape
+    dtype = query.dtype
+    max_len = block_tables.shape[1] * bs
+    hist_k = key_pool[block_tables].view(b, max_len, h, d).transpose(1, 2)
+    hist_v = value_pool[block_tables].view(b, max_len, h, d).transpose(1, 2)
+    allowed = (torch.arange(max_len).unsqueeze(0) < context_lens.unsqueeze(1)).view(b, 1, 1, max_len)
+    bias = torch.zeros(allowed.shape, dtype=dtype)
+    bias.masked_fill_(~allowed, torch.finfo(dtype).min)
+    k = hist_k.repeat_interleave(hq // h, dim=1)
+    v = hist_v.repeat_interleave(hq // h, dim=1)
+    scores = torch.matmul(query.unsqueeze(2), k.transpose(2, 3)) * scale + bias
+    probs = torch.softmax(scores, dim=-1, dtype=torch.float32).to(dtype)
+    return torch.matmul(probs, v).transpose(1, 2).contiguous().view(b, hq * d)
+
+
 __all__ = [
     "NULL_BLOCK_ID",
+    "torch_paged_decode",
     "append_decode",
     "as_float",
     "bf16_to_f32",

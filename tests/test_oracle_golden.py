@@ -88,6 +88,32 @@ def test_scatter_oracle_matches_reference(case, scatter_golden):
     assert not kp.reshape(-1, h, d)[untouched].any() and not vp.reshape(-1, h, d)[untouched].any()
 
 
+@pytest.mark.parametrize("case", cases.DECODE_CASES, ids=[c[0] for c in cases.DECODE_CASES])
+def test_torch_cpu_restatement_matches_reference(case, decode_golden):
+    """The timed CPU baseline reproduces the reference's own outputs (same ops, same dtype)."""
+    import torch
+
+    name, dtype, b, hq, h, d = case[:6]
+    inp = cases.decode_inputs(case)
+    kp, vp = inp["key_pool"].copy(), inp["value_pool"].copy()
+    po.append_decode(kp, vp, inp["key_new"], inp["value_new"], inp["slot_mapping"])
+
+    def t(a):
+        a = np.asarray(a)
+        if a.dtype == np.uint16:
+            return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+        return torch.from_numpy(a)
+
+    out = po.torch_paged_decode(t(inp["query"]), t(kp), t(vp), t(inp["block_tables"]), t(inp["context_lens"]),
+                                d**-0.5)
+    want = decode_golden[f"{name}/out"]
+    if dtype == "float32":
+        np.testing.assert_allclose(out.numpy(), want, rtol=1e-5, atol=1e-6)
+    else:
+        got = po.bf16_to_f32(out.view(torch.int16).numpy().view(np.uint16))
+        assert np.abs(got - po.bf16_to_f32(want)).max() <= 1e-2
+
+
 def test_decode_index_matches_reference():
     golden = json.loads((GOLDEN / "decode_index.json").read_text())
     for c in golden["cases"]:
