@@ -119,6 +119,27 @@ int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, 
                     int64_t out_stride, void* workspace, size_t workspace_bytes, int dtype, void* stream);
 
 /*
+ * mi_paged_decode_static_scratch — mi_paged_decode for callers that cannot allocate device memory.
+ * No counterpart in the reference: it exists for callers of this library that have no way to
+ * provide the split-K workspace — code issuing the decode while a CUDA graph is being captured
+ * (cudaMalloc is not capturable), hosts binding the C ABI without a device allocator of their own,
+ * and loops that cannot afford cudaMalloc's implicit synchronisation.  Same arguments and results
+ * as mi_paged_decode minus the workspace: the split-K partials go to a file-scope device array of
+ * MI_STATIC_SCRATCH_BYTES that every GPU loading the library holds until the process exits.
+ * Nothing is allocated.  A call whose partials would exceed the array is rejected with
+ * MI_ERR_UNSUPPORTED (use mi_paged_decode then).  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current): make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race and must be serialised.
+ */
+#define MI_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
+int mi_paged_decode_static_scratch(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,
+                                   const int64_t* new_strides, const int64_t* slot_mapping, void* k_pool,
+                                   void* v_pool, int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                                   const int64_t* block_tables, int64_t table_stride, int64_t max_blocks_per_seq,
+                                   const int64_t* context_lens, int64_t batch, int num_q_heads, float scale,
+                                   void* out, int64_t out_stride, int dtype, void* stream);
+
+/*
  * mi_paged_prefill — varlen chunked-prefill attention for one layer.  Replaces, for
  * PagedRunner.run_prefill_chunk_step (worker/paged_runner.py:32-102), the all-layer history
  * gather (gather_blocks), torch.cat(history, chunk) (model/qwen3.py:328-329), the padded causal

@@ -4,3 +4,4 @@
 #include "paged_decode.cu"
 #include "paged_prefill.cu"
 #include "api.cu"
+#include "api_static.cu"

@@ -36,6 +36,10 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _I64P, _P, _P, _I64P, _P, _P, _P, _L, _I, _I, _I, _P, _L, _L, _P, _L, _I, ctypes.c_float, _P, _L, _P,
          ctypes.c_size_t, _I, _P],
     ),
+    "mi_paged_decode_static_scratch": (
+        _I,
+        [_P, _I64P, _P, _P, _I64P, _P, _P, _P, _L, _I, _I, _I, _P, _L, _L, _P, _L, _I, ctypes.c_float, _P, _L, _I, _P],
+    ),
     "mi_paged_prefill": (
         _I,
         [_P, _I64P, _P, _P, _I64P, _P, _P, _L, _I, _I, _I, _P, _L, _P, _P, _L, _L, _I, ctypes.c_float, _P, _I, _P],
