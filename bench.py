@@ -35,12 +35,23 @@ for _p in (ROOT, ROOT / "mini-infra-qwen3_b200"):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-# BASELINE config 2
+# BASELINE config 2 (the default workload; also the CPU baseline's shape)
 HQ, HKV, D, BS = 16, 8, 128, 16
 B_PER_RANK = 256
 CTX_LO, CTX_HI = 128, 4096
 KV_BYTES_PER_TOKEN = 2 * HKV * D * 2  # K+V, all 8 KV heads, bf16
 SEED = 1234
+
+# name -> (hq, hkv, batch, ctx_lo, ctx_hi, layer calls per step, resident layer pools, batch scales with N)
+WORKLOADS = {
+    # config 2: one layer of the Qwen3-0.6B decode op; weak scaling (256 sequences per rank)
+    "c2": dict(hq=16, hkv=8, batch=256, ctx=(128, 4096), layers=1, resident=1, weak=True,
+               name="config2_paged_decode_op_qwen3_0.6b_shape"),
+    # config 5: Qwen3-8B heads, batch 512, contexts U[1024, 32768], 36 layer calls per step cycling over
+    # 4 resident layer pools (~142 GB per box); strong scaling (the heads are split over N ranks)
+    "c5": dict(hq=32, hkv=8, batch=512, ctx=(1024, 32768), layers=36, resident=4, weak=False,
+               name="config5_paged_decode_sweep_qwen3_8b_shape"),
+}
 
 
 def measured_peaks() -> dict:
@@ -51,12 +62,13 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def workload(world: int, rank: int, device):
-    """Seeded C2 inputs for this rank: contexts, block tables, pools (own KV heads), q, new K/V."""
-    b = B_PER_RANK * world
-    h_loc = HKV // world
+def workload(spec: dict, world: int, rank: int, device):
+    """Seeded inputs for this rank: contexts, block tables, resident pools (own KV heads), q, new K/V."""
+    b = spec["batch"] * (world if spec["weak"] else 1)
+    h_loc = spec["hkv"] // world
+    lo, hi = spec["ctx"]
     rng = np.random.RandomState(SEED)
-    ctx = rng.randint(CTX_LO, CTX_HI + 1, size=b).astype(np.int64)  # includes the appended token
+    ctx = rng.randint(lo, hi + 1, size=b).astype(np.int64)  # includes the appended token
     need = -(-ctx // BS)
     used = int(need.sum())
     num_blocks = 1 + used + used // 10  # exactly the needed blocks + 10% free + null block
@@ -69,13 +81,17 @@ def workload(world: int, rank: int, device):
     pos = ctx - 1
     slots = tables[np.arange(b), pos // BS] * BS + pos % BS
     g = torch.Generator(device=device).manual_seed(SEED + 17 * rank)
-    kp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
-    vp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
-    q = torch.randn((b, HQ // world, D), generator=g, device=device, dtype=torch.bfloat16)
+    pools = []
+    for _ in range(spec["resident"]):
+        kp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
+        vp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
+        pools.append((kp, vp))
+    hq_loc = spec["hq"] // world
+    q = torch.randn((b, hq_loc, D), generator=g, device=device, dtype=torch.bfloat16)
     kn = torch.randn((b, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
     vn = torch.randn((b, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
-    return dict(b=b, ctx=ctx, tables=tables, slots=slots, num_blocks=num_blocks, kp=kp, vp=vp, q=q, kn=kn, vn=vn,
-                h_loc=h_loc)
+    return dict(b=b, ctx=ctx, tables=tables, slots=slots, num_blocks=num_blocks, pools=pools, q=q, kn=kn, vn=vn,
+                h_loc=h_loc, hq_loc=hq_loc)
 
 
 class ClockSampler:
@@ -212,11 +228,17 @@ def run_reference(args, budget_s: float = 150.0) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 3000 for c2, 20 for c5)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 20 for c2, 3 for c5)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    spec = WORKLOADS[args.workload]
+    if args.steps is None:
+        args.steps = 3000 if spec["layers"] == 1 else 20
+    if args.warmup is None:
+        args.warmup = 20 if spec["layers"] == 1 else 3
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
@@ -241,26 +263,30 @@ def main() -> None:
         group = dist.group.WORLD
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    if HKV % world:
-        raise SystemExit(f"{HKV} KV heads cannot be split over {world} ranks")
+    if spec["hkv"] % world:
+        raise SystemExit(f"{spec['hkv']} KV heads cannot be split over {world} ranks")
     part = HeadPartition(rank, world, group)
 
-    w = workload(world, rank, device)
-    b = w["b"]
+    w = workload(spec, world, rank, device)
+    b, hq_loc, h_loc = w["b"], w["hq_loc"], w["h_loc"]
     tables = torch.from_numpy(w["tables"]).to(device)
     ctx = torch.from_numpy(w["ctx"]).to(device)
     slots = torch.from_numpy(w["slots"]).to(device)
     scale = D**-0.5
-    out = torch.empty((b, (HQ // world) * D), dtype=torch.bfloat16, device=device)
-    ws = ops.workspace(device, ops.decode_workspace_bytes(b, HQ // world, w["kp"], tables.shape[1]))
+    out = torch.empty((b, hq_loc * D), dtype=torch.bfloat16, device=device)
+    pools = w["pools"]
+    ws = ops.workspace(device, ops.decode_workspace_bytes(b, hq_loc, pools[0][0], tables.shape[1]))
+    layers = spec["layers"]
 
     def step():
-        ops.paged_decode(w["q"], w["kp"], w["vp"], tables, ctx, scale, key_new=w["kn"], value_new=w["vn"],
-                         slot_mapping=slots, out=out, ws=ws)
-        return gather_heads(out, part)
+        for layer in range(layers):
+            kp, vp = pools[layer % len(pools)]
+            ops.paged_decode(w["q"], kp, vp, tables, ctx, scale, key_new=w["kn"], value_new=w["vn"],
+                             slot_mapping=slots, out=out, ws=ws)
+            gather_heads(out, part)
 
     def attn_only():
-        ops.paged_decode(w["q"], w["kp"], w["vp"], tables, ctx, scale, out=out, ws=ws)
+        ops.paged_decode(w["q"], pools[0][0], pools[0][1], tables, ctx, scale, out=out, ws=ws)
 
     def barrier():
         if world > 1:
@@ -286,16 +312,17 @@ def main() -> None:
         step()
     with ClockSampler(local) as clocks:
         ms = timed(step, args.steps)
-    kv_bytes_global = float(w["ctx"].sum()) * KV_BYTES_PER_TOKEN  # all ranks together read every head once
+    kv_token_bytes = 2 * spec["hkv"] * D * 2  # K+V of every KV head, bf16
+    kv_bytes_global = float(w["ctx"].sum()) * kv_token_bytes * layers  # all ranks together read every head once
     value = kv_bytes_global / (ms * 1e-3) / 1e9
 
-    # roofline of the attention kernels alone (split-K kernel + combine): algorithmic bytes per launch
+    # roofline of the attention launch alone (split-K kernel + combine): algorithmic bytes per launch
     for _ in range(3):
         attn_only()
-    ms_attn = timed(attn_only, max(args.steps // 2, 10))
-    h_loc = w["h_loc"]
+    n_attn = max(min(args.steps // 2, 1000), 10)
+    ms_attn = timed(attn_only, n_attn)
     alg_bytes = (float(w["ctx"].sum()) * 2 * h_loc * D * 2  # K+V of this rank's heads
-                 + b * (HQ // world) * D * 2 * 2 + tables.numel() * 8 + b * 8)  # q + out + tables + ctx
+                 + b * hq_loc * D * 2 * 2 + tables.numel() * 8 + b * 8)  # q + out + tables + ctx
     achieved = alg_bytes / (ms_attn * 1e-3) / 1e9
     peaks = measured_peaks()
 
@@ -308,22 +335,23 @@ def main() -> None:
     d_meta = torch.empty(meta.shape, dtype=torch.long, device=device)
 
     def e2e_step():
-        d_q.copy_(h_q, non_blocking=True)
-        d_kn.copy_(h_kn, non_blocking=True)
-        d_vn.copy_(h_vn, non_blocking=True)
         d_meta.copy_(meta, non_blocking=True)
         sl, cx, tb = d_meta[:b], d_meta[b : 2 * b], d_meta[2 * b :].view(b, -1)
-        ops.paged_decode(d_q, w["kp"], w["vp"], tb, cx, scale, key_new=d_kn, value_new=d_vn, slot_mapping=sl,
-                         out=out, ws=ws)
-        full = gather_heads(out, part)
-        h_out.copy_(out, non_blocking=True)
-        return full
+        for layer in range(layers):
+            kp, vp = pools[layer % len(pools)]
+            d_q.copy_(h_q, non_blocking=True)
+            d_kn.copy_(h_kn, non_blocking=True)
+            d_vn.copy_(h_vn, non_blocking=True)
+            ops.paged_decode(d_q, kp, vp, tb, cx, scale, key_new=d_kn, value_new=d_vn, slot_mapping=sl, out=out,
+                             ws=ws)
+            gather_heads(out, part)
+            h_out.copy_(out, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
-    ms_e2e = timed(e2e_step, max(args.steps // 2, 10))
-    h2d = h_q.numel() * 2 + h_kn.numel() * 2 + h_vn.numel() * 2 + meta.numel() * 8
-    d2h = h_out.numel() * 2
+    ms_e2e = timed(e2e_step, max(min(args.steps // 2, 1000), 5))
+    h2d = meta.numel() * 8 + layers * (h_q.numel() + h_kn.numel() + h_vn.numel()) * 2
+    d2h = layers * h_out.numel() * 2
     e2e_value = kv_bytes_global / (ms_e2e * 1e-3) / 1e9
 
     cpu = None
@@ -339,17 +367,21 @@ def main() -> None:
             "warmup": args.warmup,
             "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if spec["weak"] else "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
             "config": {
-                "workload": "config2_paged_decode_op_qwen3_0.6b_shape",
-                "global_batch": b, "seq_len": f"U[{CTX_LO},{CTX_HI}]", "heads": f"{HQ}q/{HKV}kv",
-                "head_dim": D, "block_size": BS, "pool_blocks_per_rank": w["num_blocks"],
+                "workload": spec["name"],
+                "global_batch": b, "seq_len": f"U[{spec['ctx'][0]},{spec['ctx'][1]}]",
+                "heads": f"{spec['hq']}q/{spec['hkv']}kv", "head_dim": D, "block_size": BS,
+                "layer_calls_per_step": layers, "resident_layer_pools": spec["resident"],
+                "pool_blocks_per_layer": w["num_blocks"],
+                "pool_gb_per_rank": round(2 * spec["resident"] * w["num_blocks"] * BS * h_loc * D * 2 / 1e9, 2),
                 "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU",
-                "l2": "inputs larger than L2 (KV pool ~2.4 GB per rank)",
-                "step": "append + paged decode (split-K + combine)" + (" + NCCL all-gather" if world > 1 else ""),
+                "l2": "inputs larger than L2 (every layer call reads >= 2 GB of pool)",
+                "step": "per layer call: append + paged decode (split-K + combine)"
+                        + (" + NCCL all-gather" if world > 1 else ""),
             },
             "roofline": {
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -358,7 +390,7 @@ def main() -> None:
             },
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 3 * layers * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
