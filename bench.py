@@ -42,6 +42,12 @@ CTX_LO, CTX_HI = 128, 4096
 KV_BYTES_PER_TOKEN = 2 * HKV * D * 2  # K+V, all 8 KV heads, bf16
 SEED = 1234
 
+# DRAM traffic of one decode_split launch on config 2 from the committed ncu capture
+# (profiles/decode_split_c2.md: dram__bytes_read.sum + dram__bytes_write.sum) and that launch's
+# algorithmic bytes; other workloads scale it by the tokens processed (traffic grows in proportion).
+NCU_TRAFFIC_C2 = 2.296959e9 + 13.282816e6
+NCU_ALGORITHMIC_C2 = 2.217e9
+
 # name -> (hq, hkv, batch, ctx_lo, ctx_hi, layer calls per step, resident layer pools, batch scales with N)
 WORKLOADS = {
     # config 2: one layer of the Qwen3-0.6B decode op; weak scaling (256 sequences per rank)
@@ -385,7 +391,11 @@ def main() -> None:
             },
             "roofline": {
                 "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                "traffic": NCU_TRAFFIC_C2 if args.workload == "c2" and world == 1
+                else alg_bytes * NCU_TRAFFIC_C2 / NCU_ALGORITHMIC_C2,
+                "traffic_unit": "bytes per launch (ncu dram read+write; scaled from config 2 by tokens "
+                                "unless workload c2 on one GPU)",
                 "kernel": "decode_split_kernel + decode_combine_kernel", "ms_per_launch": ms_attn,
             },
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
