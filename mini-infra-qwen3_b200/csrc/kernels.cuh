@@ -126,5 +126,8 @@ struct PrefillArgs {
 };
 
 cudaError_t launch_paged_prefill(const PrefillArgs& a, int dtype, cudaStream_t s);
+// tcgen05 variant (bf16/fp16, head_dim 128, G in {1,2,4,8}, 16-byte aligned operands)
+bool prefill_tc_supported(const PrefillArgs& a, int dtype);
+cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, int dtype, cudaStream_t s);
 
 }  // namespace mi

@@ -2,6 +2,7 @@
 // share one module without relocatable device code.
 #include "kv_scatter.cu"
 #include "paged_decode.cu"
+#include "paged_prefill_tc.cu"
 #include "paged_prefill.cu"
 #include "api.cu"
 #include "api_static.cu"

@@ -1,5 +1,6 @@
 // Varlen chunked-prefill paged attention, sm_100a.
 //
+// Dispatch: bf16/fp16 with head_dim 128 run the tcgen05 kernel (paged_prefill_tc.cu).
 // Generic kernel (every dtype, head_dim <= 256, any block size): one warp per (row, padded
 // position, query head).  The query's keys are the first `start` positions of its history, read
 // in place from the pools through the block table, followed causally by the chunk's own keys up
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(128) prefill_scalar_kernel(const PrefillArgs a
 cudaError_t launch_paged_prefill(const PrefillArgs& a, int dtype, cudaStream_t s) {
   const int64_t warps = a.batch * a.padded_len * a.hq;
   if (warps == 0) return cudaSuccess;
+  if (prefill_tc_supported(a, dtype)) return launch_paged_prefill_tc(a, dtype, s);
   const unsigned blocks = (unsigned)((warps + 3) / 4);
   switch (dtype) {
     case MI_BF16: prefill_scalar_kernel<__nv_bfloat16><<<blocks, 128, 0, s>>>(a); break;

@@ -79,3 +79,65 @@ def test_prefill_random_shapes(shape):
     valid = np.arange(length)[None, :] >= (length - np.asarray(lens))[:, None]
     got = po.as_float(to_numpy(out), np.float64)
     assert_attention_close(got[valid], want[valid], dtype)
+
+
+TC_SHAPES = [
+    # hq, h, d, bs, starts, lens  (bf16, head_dim 128: the tcgen05 kernel)
+    (8, 8, 128, 16, [0, 5, 130], [1, 127, 128]),        # G=1
+    (64, 8, 128, 16, [70, 0], [16, 40]),                # G=8: 16 tokens per q-tile
+    (16, 8, 128, 16, [3000, 129, 0], [128, 128, 128]),  # long history, several KV tiles
+    (16, 8, 128, 32, [257], [300]),                     # chunk spans several q-tiles; block size 32
+    (32, 8, 128, 1, [33, 7], [9, 64]),                  # block size 1
+]
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=[str(s) for s in TC_SHAPES])
+def test_prefill_tensor_core_path(shape):
+    hq, h, d, bs, starts, lens = shape
+    inp = _random_prefill(hq, h, d, bs, starts, lens, "bfloat16", seed=len(starts) * 31 + sum(lens))
+    out = run_prefill(inp, bs, d)
+    want = po.chunk_prefill_attention(inp["query"], inp["key_chunk"], inp["value_chunk"], inp["key_pool"],
+                                      inp["value_pool"], inp["tables_list"], starts, lens, d**-0.5)
+    length = max(lens)
+    valid = np.arange(length)[None, :] >= (length - np.asarray(lens))[:, None]
+    got = po.as_float(to_numpy(out), np.float64)
+    assert_attention_close(got[valid], want[valid], "bfloat16")
+    assert not got[~valid].any()
+
+
+def test_prefill_tensor_core_rescales_on_growing_scores():
+    """Queries aligned with later keys make the running max jump by far more than 2^8 across KV
+    tiles, so the TMEM accumulator rescale path runs; result must still match the oracle."""
+    hq, h, d, bs, starts, lens = 16, 8, 128, 16, [600], [128]
+    inp = _random_prefill(hq, h, d, bs, starts, lens, "float32", seed=77)
+    rng = np.random.RandomState(5)
+    kp = inp["key_pool"]
+    table = inp["tables_list"][0]
+    for t in range(600):  # history keys grow in magnitude with position
+        kp[table[t // bs], t % bs] *= 0.02 + t / 25.0
+    q = inp["query"] * 0.5 + rng.standard_normal(inp["query"].shape).astype(np.float32) * 0.1
+    bf = {k: po.f32_to_bf16(v) for k, v in dict(query=q, key_chunk=inp["key_chunk"], value_chunk=inp["value_chunk"],
+                                                 key_pool=kp, value_pool=inp["value_pool"]).items()}
+    inp.update(bf)
+    out = run_prefill(inp, bs, d)
+    want = po.chunk_prefill_attention(inp["query"], inp["key_chunk"], inp["value_chunk"], inp["key_pool"],
+                                      inp["value_pool"], inp["tables_list"], starts, lens, d**-0.5)
+    assert_attention_close(out, want, "bfloat16")
+
+
+def test_prefill_tensor_core_fp16():
+    hq, h, d, bs, starts, lens = 16, 8, 128, 16, [200, 0], [64, 100]
+    inp = _random_prefill(hq, h, d, bs, starts, lens, "float32", seed=99)
+    t = lambda k: to_cuda(inp[k]).half()  # noqa: E731
+    tables = torch.from_numpy(_tables(inp["tables_list"], starts, bs)).cuda()
+    out = ops.paged_prefill(t("query").transpose(1, 2), t("key_chunk").transpose(1, 2),
+                            t("value_chunk").transpose(1, 2), t("key_pool"), t("value_pool"), tables,
+                            torch.tensor(starts).cuda(), torch.tensor(lens).cuda(), d**-0.5)
+    assert ops.read_status() == 0
+    as16 = {k: to_numpy(t(k).float()) for k in ("query", "key_chunk", "value_chunk", "key_pool", "value_pool")}
+    want = po.chunk_prefill_attention(as16["query"], as16["key_chunk"], as16["value_chunk"], as16["key_pool"],
+                                      as16["value_pool"], inp["tables_list"], starts, lens, d**-0.5)
+    length = max(lens)
+    valid = np.arange(length)[None, :] >= (length - np.asarray(lens))[:, None]
+    got = out.float().cpu().numpy()
+    assert_attention_close(got[valid], want[valid], "float16")
