@@ -231,15 +231,117 @@ def run_reference(args, budget_s: float = 150.0) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_c4(args) -> None:
+    """Config 4: chunked-prefill mixed step at the Qwen3-0.6B shape (one GPU).
+
+    16 prompts with lengths U[4096, 16384] are each at a seeded chunk index k (start = 128 k, chunk
+    = min(128, L - start), the cap token_budget 2048 // 16 candidates gives); 64 decode sequences
+    have contexts U[512, 8192].  Per layer the reference alternates a prefill step and a decode
+    step; here one "mixed step" = one chunked-prefill attention launch + one decode launch, and
+    each is also timed alone.  Prefill FLOPs are the causal algorithmic count
+    4 * chunk * (start + (chunk + 1) / 2) * Hq * D per row."""
+    from mini_infra_b200 import ops
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    rng = np.random.RandomState(SEED + 4)
+    hq, hkv = 16, 8
+    lens_total = rng.randint(4096, 16385, size=16)
+    starts = np.array([128 * rng.randint(0, (n - 1) // 128 + 1) for n in lens_total], dtype=np.int64)
+    chunks = np.minimum(128, lens_total - starts).astype(np.int64)
+    dec_ctx = rng.randint(512, 8193, size=64).astype(np.int64)
+    need = [-(-(int(s) + int(c)) // BS) for s, c in zip(starts, chunks)] + [-(-int(c) // BS) for c in dec_ctx]
+    used = sum(need)
+    num_blocks = 1 + used + used // 10
+    perm = rng.permutation(np.arange(1, num_blocks))
+    tabs, off = [], 0
+    for n in need:
+        tabs.append(perm[off : off + n])
+        off += n
+    pre_tab = np.zeros((16, max(need[:16])), dtype=np.int64)
+    for i in range(16):
+        pre_tab[i, : need[i]] = tabs[i]
+    dec_tab = np.zeros((64, max(need[16:])), dtype=np.int64)
+    for i in range(64):
+        dec_tab[i, : need[16 + i]] = tabs[16 + i]
+    g = torch.Generator(device=device).manual_seed(SEED)
+    rnd = lambda *sh: torch.randn(sh, generator=g, device=device, dtype=torch.bfloat16)  # noqa: E731
+    kp, vp = rnd(num_blocks, BS, hkv, D), rnd(num_blocks, BS, hkv, D)
+    length = int(chunks.max())
+    q, kc, vc = rnd(16, length, hq, D), rnd(16, length, hkv, D), rnd(16, length, hkv, D)
+    qd = rnd(64, hq, D)
+    t = lambda a: torch.from_numpy(a).to(device)  # noqa: E731
+    pre_tab_d, starts_d, chunks_d, dec_tab_d, dec_ctx_d = t(pre_tab), t(starts), t(chunks), t(dec_tab), t(dec_ctx)
+    out_p = torch.empty((16, length, hq * D), dtype=torch.bfloat16, device=device)
+    out_d = torch.empty((64, hq * D), dtype=torch.bfloat16, device=device)
+    ws = ops.workspace(device, ops.decode_workspace_bytes(64, hq, kp, dec_tab.shape[1]))
+
+    def prefill():
+        ops.paged_prefill(q, kc, vc, kp, vp, pre_tab_d, starts_d, chunks_d, D**-0.5, out=out_p)
+
+    def decode():
+        ops.paged_decode(qd, kp, vp, dec_tab_d, dec_ctx_d, D**-0.5, out=out_d, ws=ws)
+
+    def mixed():
+        prefill()
+        decode()
+
+    def timed(fn, n):
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / n
+
+    for _ in range(args.warmup):
+        mixed()
+    with ClockSampler(device.index or 0) as clocks:
+        ms_mixed = timed(mixed, args.steps)
+    ms_pre = timed(prefill, args.steps)
+    ms_dec = timed(decode, args.steps)
+    flops = float(np.sum(4.0 * chunks * (starts + (chunks + 1) / 2.0))) * hq * D
+    pre_bytes = float(np.sum(starts + chunks)) * 2 * hkv * D * 2 + 2 * 16 * length * hq * D * 2
+    dec_bytes = float(dec_ctx.sum()) * 2 * hkv * D * 2
+    tflops = flops / (ms_pre * 1e-3) / 1e12
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak_t = float(peaks.get("bf16_tflops", 1590.0))
+    line = {
+        "metric": "chunked-prefill attention TFLOP/s", "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_mixed, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config4_chunked_prefill_mixed_step_qwen3_0.6b_shape", "prefill_rows": 16,
+                   "chunk_tokens": int(chunks.sum()), "history_tokens": int(starts.sum()),
+                   "decode_rows": 64, "decode_ctx_tokens": int(dec_ctx.sum()),
+                   "step": "1 chunked-prefill launch + 1 decode launch (one layer)"},
+        "prefill": {"ms": ms_pre, "tflops": tflops, "gbs": pre_bytes / (ms_pre * 1e-3) / 1e9,
+                    "algorithmic_gflop": flops / 1e9, "kernel": "prefill_tc_kernel"},
+        "decode": {"ms": ms_dec, "gbs": dec_bytes / (ms_dec * 1e-3) / 1e9},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak_t, "unit": "TFLOP/s",
+                     "frac": tflops / peak_t, "traffic": None,
+                     "peak_source": "measured" if peaks else "fallback"},
+        "gpu_launches": args.steps * 2 + args.steps * 2,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default 3000 for c2, 20 for c5)")
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 20 for c2, 3 for c5)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c4"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.workload == "c4":
+        args.steps = args.steps or 200
+        args.warmup = args.warmup or 5
+        run_c4(args)
+        return
     spec = WORKLOADS[args.workload]
     if args.steps is None:
         args.steps = 3000 if spec["layers"] == 1 else 20
