@@ -153,12 +153,17 @@ int mi_paged_decode_static_scratch(const void* q, const int64_t* q_strides, cons
  *            b*q_strides[0] + p*q_strides[1] + h*q_strides[2] + d
  *   k_chunk  [batch, padded_len, num_kv_heads, head_dim], strides kv_strides[0..2] (v_chunk same)
  *   out      [batch, padded_len, num_q_heads*head_dim] contiguous
+ *   workspace  >= mi_paged_prefill_workspace_size(...) bytes, 256-byte aligned (split-KV partials
+ *            of long histories; the size depends only on the arguments of that function)
  */
+size_t mi_paged_prefill_workspace_size(int64_t batch, int64_t padded_len, int num_q_heads, int num_kv_heads,
+                                       int head_dim, int64_t table_stride, int block_size, int dtype);
 int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chunk, const void* v_chunk,
                      const int64_t* kv_strides, const void* k_pool, const void* v_pool, int64_t num_blocks,
                      int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
                      int64_t table_stride, const int64_t* start_positions, const int64_t* chunk_lens, int64_t batch,
-                     int64_t padded_len, int num_q_heads, float scale, void* out, int dtype, void* stream);
+                     int64_t padded_len, int num_q_heads, float scale, void* out, void* workspace,
+                     size_t workspace_bytes, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -319,11 +319,29 @@ int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, 
   return e == cudaSuccess ? MI_OK : cuda_fail(e, "mi_paged_decode launch");
 }
 
+size_t mi_paged_prefill_workspace_size(int64_t batch, int64_t padded_len, int num_q_heads, int num_kv_heads,
+                                       int head_dim, int64_t table_stride, int block_size, int dtype) {
+  if (batch <= 0 || padded_len <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads)
+    return 0;
+  if ((dtype != MI_BF16 && dtype != MI_F16) || head_dim != 128) return 0;
+  mi::PrefillArgs a{};
+  a.batch = batch;
+  a.padded_len = padded_len;
+  a.hq = num_q_heads;
+  a.hkv = num_kv_heads;
+  a.groups = num_q_heads / num_kv_heads;
+  a.head_dim = head_dim;
+  a.table_stride = table_stride;
+  a.block_size = block_size;
+  return mi::prefill_tc_workspace_bytes(a);
+}
+
 int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chunk, const void* v_chunk,
                      const int64_t* kv_strides, const void* k_pool, const void* v_pool, int64_t num_blocks,
                      int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
                      int64_t table_stride, const int64_t* start_positions, const int64_t* chunk_lens, int64_t batch,
-                     int64_t padded_len, int num_q_heads, float scale, void* out, int dtype, void* stream) {
+                     int64_t padded_len, int num_q_heads, float scale, void* out, void* workspace,
+                     size_t workspace_bytes, int dtype, void* stream) {
   if (int rc = check_pool_geometry(num_blocks, block_size, num_kv_heads, head_dim, dtype)) return rc;
   if (batch < 0 || padded_len < 0 || table_stride < 0) return fail(MI_ERR_INVALID, "negative size");
   if (batch == 0 || padded_len == 0) return MI_OK;
@@ -361,7 +379,17 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
   a.block_size = block_size;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.out = static_cast<char*>(out);
-  cudaError_t e = mi::launch_paged_prefill(a, dtype, static_cast<cudaStream_t>(stream));
+  float* ws = nullptr;
+  if (mi::prefill_tc_supported(a, dtype)) {
+    const size_t need = mi::prefill_tc_workspace_bytes(a);
+    if (need > 0) {
+      if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+        return fail(MI_ERR_INVALID, "prefill workspace must be >= %zu bytes and 256-byte aligned (got %zu)", need,
+                    workspace_bytes);
+      ws = static_cast<float*>(workspace);
+    }
+  }
+  cudaError_t e = mi::launch_paged_prefill(a, ws, dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MI_OK : cuda_fail(e, "mi_paged_prefill launch");
 }
 

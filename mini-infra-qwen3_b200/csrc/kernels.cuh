@@ -125,9 +125,11 @@ struct PrefillArgs {
   char* out;  // [batch, padded_len, hq*head_dim] contiguous
 };
 
-cudaError_t launch_paged_prefill(const PrefillArgs& a, int dtype, cudaStream_t s);
-// tcgen05 variant (bf16/fp16, head_dim 128, G in {1,2,4,8}, 16-byte aligned operands)
+cudaError_t launch_paged_prefill(const PrefillArgs& a, float* ws, int dtype, cudaStream_t s);
+// tcgen05 variant (bf16/fp16, head_dim 128, G in {1,2,4,8}, 16-byte aligned operands); its split-KV
+// partials need prefill_tc_workspace_bytes(a) bytes of workspace (0 when no row tile splits)
 bool prefill_tc_supported(const PrefillArgs& a, int dtype);
-cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, int dtype, cudaStream_t s);
+size_t prefill_tc_workspace_bytes(const PrefillArgs& a);
+cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, int dtype, cudaStream_t s);
 
 }  // namespace mi

@@ -1,29 +1,37 @@
 // Chunked-prefill paged attention on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
 // Variant: bf16 / fp16, head_dim 128, any block size, G = Hq/H_kv in {1, 2, 4, 8}.
-// One CTA (128 threads) = one (sequence, KV head, tile of 128 query rows).  The 128 rows pack
-// 128/G chunk tokens x G query heads of the KV head (row r = token r/G, head r%G), so the K/V
-// tiles staged in shared memory serve the whole GQA group.  Per 128-position KV tile:
-//   1. cp.async stages K and V rows (double-buffered, the next tile streams in during this one):
-//      positions < start come from the pool through the block table, the rest from the chunk's
-//      own K/V; rows past the causal end are zero-filled;
-//   2. one thread issues S = Q K^T as 8 tcgen05.mma (M=128, N=128, K=16, kind::f16, fp32 accum)
-//      into TMEM columns [0, 128); tcgen05.commit signals an mbarrier;
-//   3. each thread owns one row (its TMEM lane): tcgen05.ld of the row, causal/length mask, online
-//      softmax in the exp2 domain; the running O in TMEM is rescaled (tcgen05.ld/st) only when the
-//      row maximum grew by more than 2^8 since the last rescale (otherwise p <= 2^8 stays exact
-//      in fp32 and the final 1/l normalisation absorbs it); P is written as bf16 into shared
-//      memory in the 128-byte-swizzled K-major layout;
-//   4. one thread issues O += P V as 8 tcgen05.mma (V read MN-major) into TMEM columns [128, 256).
-// Epilogue: tcgen05.ld of O, divide by l, store bf16 rows.  Padding positions get zeros.
+// One CTA (128 threads, two CTAs per SM) = one (sequence, KV head, tile of 128 query rows, KV
+// split).  The 128 rows pack 128/G chunk tokens x G query heads of the KV head (row r = token r/G,
+// head r%G), so the K/V tiles staged in shared memory serve the whole GQA group.  The KV range of
+// a row tile (history + causal chunk) is cut into splits of kTilesPerSplit 64-position tiles so
+// that long histories spread over many CTAs; a tile with one split writes its output directly,
+// otherwise each split writes an unnormalised partial (O, m, l) that prefill_combine_kernel merges.
+// Per 64-position KV tile:
+//   1. cp.async stages K and V rows (double-buffered: the next tile streams in during this one):
+//      positions < start come from the pool through the block table, the rest from the chunk's own
+//      K/V; rows past the causal end are zero-filled;
+//   2. one thread issues S = Q K^T as 8 tcgen05.mma (M=128, N=64, K=16, kind::f16, fp32 accum) into
+//      TMEM columns [0, 64); tcgen05.commit signals an mbarrier;
+//   3. each thread owns one row (its TMEM lane): tcgen05.ld of the row (twice: max, then exp),
+//      causal/length mask only on tiles that cross a row's causal end, online softmax in the exp2
+//      domain; the running O in TMEM is rescaled (tcgen05.ld/st, warp-wide) only when a row maximum
+//      grew by more than 2^8 since its last rescale (p <= 2^8 stays exact in fp32 and the final 1/l
+//      absorbs it); P is written as 16-bit values into the now-dead K buffer of this tile, in the
+//      128-byte-swizzled K-major layout;
+//   4. one thread issues O += P V as 4 tcgen05.mma (M=128, N=128, V read MN-major) into TMEM
+//      columns [128, 256).
+// Epilogue: tcgen05.ld of O, divide by l (or store the partial), 16-byte stores.  Padding
+// positions get zeros.
 //
-// Shared-memory operand layout ("SW128"): a 128 x 128 tile of 16-bit elements is two 16 KiB
-// regions (columns 0-63 and 64-127); row r of a region is 128 bytes at r*128, and its 16-byte unit
-// u lives at unit u ^ (r % 8).  Every region starts 1024-byte aligned.  Descriptors:
-//   K-major (Q, K, P):  start, LBO = 16 B (unused), SBO = 1024 B (8-row groups), swizzle 128B;
-//                       k-step s (16 columns) starts at region(s/4) + (s%4)*32 B.
-//   MN-major (V as the B operand of PV, N = head_dim):  LBO = 16 KiB (next 64 columns of N),
-//                       SBO = 1024 B (next 8 K-rows); k-step s starts at s*16 rows = s*2048 B.
+// Shared-memory operand layout ("SW128"): an operand of R rows x 128 two-byte columns is two
+// regions of R*128 bytes (columns 0-63 and 64-127); row r of a region is 128 bytes at r*128 and
+// its 16-byte unit u lives at unit u ^ (r % 8).  Every region starts 1024-byte aligned.
+// Descriptors:
+//   K-major (Q: R=128, K: R=64, P: 128 rows x 64 columns = one region):  LBO = 16 B (unused),
+//     SBO = 1024 B (8-row groups), swizzle 128B; k-step s starts at region(s/4) + (s%4)*32 B.
+//   MN-major (V as the B operand of PV, N = head_dim):  LBO = 8 KiB (next 64 columns of N),
+//     SBO = 1024 B (next 8 K-rows); k-step s starts at s*16 rows = s*2048 B.
 #include <type_traits>
 
 #include "common.cuh"
@@ -32,24 +40,27 @@
 namespace mi {
 namespace {
 
-constexpr int kTcRows = 128;       // query rows per CTA (MMA M)
-constexpr int kTcKv = 128;         // KV positions per tile (MMA N of QK^T, K of PV)
-constexpr int kTcDim = 128;        // head_dim
+constexpr int kTcRows = 128;                        // query rows per CTA (MMA M)
+constexpr int kTcKv = 64;                           // KV positions per tile
+constexpr int kTcDim = 128;                         // head_dim
 constexpr int kTcThreads = 128;
-constexpr int kTileBytes = kTcRows * kTcDim * 2;  // 32 KiB per 128 x 128 operand
-constexpr int kRegionBytes = kTileBytes / 2;      // 16 KiB per 64-column region
+constexpr int kTilesPerSplit = 32;                  // 2048 KV positions per CTA at most
+constexpr int kQRegion = kTcRows * 128;             // 16 KiB: one 64-column half of Q
+constexpr int kKvRegion = kTcKv * 128;              // 8 KiB: one 64-column half of a K or V tile
+constexpr int kQBytes = 2 * kQRegion;               // 32 KiB
+constexpr int kKvBytes = 2 * kKvRegion;             // 16 KiB (also holds P: 128 rows x 64 columns)
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;          // two buffers
-constexpr int kOffV = kOffK + 2 * kTileBytes;      // two buffers
-constexpr int kOffP = kOffV + 2 * kTileBytes;
-constexpr int kOffBar = kOffP + kTileBytes;
-constexpr int kTcSmemBytes = kOffBar + 64 + 1024;  // + barriers/TMEM slot + alignment slack
-constexpr uint32_t kTmemCols = 256;                // S: [0,128), O: [128,256)
+constexpr int kOffK = kOffQ + kQBytes;              // two buffers
+constexpr int kOffV = kOffK + 2 * kKvBytes;         // two buffers
+constexpr int kOffBar = kOffV + 2 * kKvBytes;
+constexpr int kTcSmemBytes = kOffBar + 64 + 1024;   // barriers + TMEM slot + alignment slack (~97 KiB)
+constexpr uint32_t kTmemCols = 256;                 // S: [0, 64), O: [128, 256)
+constexpr uint32_t kTmemO = 128;
 constexpr float kRescaleLog2 = 8.0f;
 
-__device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t unit16) {
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t unit16, uint32_t region) {
   // unit16 in [0, 16): 16-byte unit of a 256-byte row (128 two-byte columns)
-  return (unit16 >> 3) * kRegionBytes + row * 128 + (((unit16 & 7) ^ (row & 7)) << 4);
+  return (unit16 >> 3) * region + row * 128 + (((unit16 & 7) ^ (row & 7)) << 4);
 }
 
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
@@ -57,7 +68,7 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | (uint64_t(kRegionBytes >> 4) << 16) | (uint64_t(1024 >> 4) << 32) |
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (uint64_t(kKvRegion >> 4) << 16) | (uint64_t(1024 >> 4) << 32) |
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 // kind::f16 instruction descriptor: fp32 accumulate, A/B format, A K-major, B K- or MN-major, N, M.
@@ -65,7 +76,6 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, bool b_mn_major, int
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
-
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -119,50 +129,93 @@ __device__ __forceinline__ void cp_async16(uint32_t sdst, const void* gsrc, bool
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-struct TcRowMap {
-  int groups;
-  int64_t tok0;  // first chunk token of this tile
+
+// Block-table position -> pool row: shift/mask when the block size is a power of two.
+struct BlockAddr {
+  int shift;  // log2(block_size), or -1
+  uint32_t bs;
+  __device__ __forceinline__ void split(uint32_t pos, uint32_t& blk_idx, uint32_t& off) const {
+    if (shift >= 0) {
+      blk_idx = pos >> shift;
+      off = pos & (bs - 1);
+    } else {
+      blk_idx = pos / bs;
+      off = pos - blk_idx * bs;
+    }
+  }
 };
 
-// Stage one 128-position KV tile (K and V) for KV head h: positions [j0, j0 + 128).  Thread t
-// moves 16-byte unit (t % 16) of rows t/16, t/16 + 8, ...: 16 threads cover one 256-byte row.
+// Stage one 64-position KV tile (K and V) of KV head h: positions [j0, j0 + 64).  Thread t moves
+// 16-byte unit (t % 16) of rows t/16, t/16 + 8, ...: 16 threads cover one 256-byte row.
 template <typename T>
-__device__ __forceinline__ void stage_kv(const PrefillArgs& a, int64_t b, int h, int64_t start, int64_t kv_end,
-                                         int64_t first, int64_t j0, uint32_t k_dst, uint32_t v_dst) {
+__device__ __forceinline__ void stage_kv(const PrefillArgs& a, const BlockAddr& ba, int64_t b, int h, int start,
+                                         int kv_end, int64_t first, int j0, uint32_t k_dst, uint32_t v_dst) {
   const int unit = threadIdx.x & 15;
   const int64_t* table = a.block_tables + b * a.table_stride;
   const char* kc = a.k_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2];
   const char* vc = a.v_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2];
   const int64_t pool_row = (int64_t)a.hkv * kTcDim * sizeof(T);
-#pragma unroll 4
+  const int64_t head_off = (int64_t)h * kTcDim * sizeof(T) + unit * 16;
+#pragma unroll
   for (int rr = threadIdx.x >> 4; rr < kTcKv; rr += kTcThreads / 16) {
-    const int64_t j = j0 + rr;
-    const char* ksrc = a.k_chunk;  // any valid address for zero-fill
+    const int j = j0 + rr;
+    const char* ksrc = a.k_chunk;  // any valid address when zero-filling
     const char* vsrc = a.k_chunk;
     bool valid = j < kv_end;
     if (valid && j < start) {
-      const int64_t blk = table[j / a.block_size];
+      uint32_t bi, off;
+      ba.split((uint32_t)j, bi, off);
+      const int64_t blk = table[bi];
       if (blk < 0 || blk >= a.num_blocks) {
         if (unit == 0) record_status(MI_STATUS_BAD_BLOCK);
         valid = false;
       } else {
-        const int64_t off = (blk * a.block_size + j % a.block_size) * pool_row + (int64_t)h * kTcDim * sizeof(T);
-        ksrc = a.k_pool + off;
-        vsrc = a.v_pool + off;
+        const int64_t o = (blk * a.block_size + off) * pool_row + head_off;
+        ksrc = a.k_pool + o;
+        vsrc = a.v_pool + o;
       }
     } else if (valid) {
       const int64_t p = first + (j - start);
-      ksrc = kc + p * a.kv_sb[1];
-      vsrc = vc + p * a.kv_sb[1];
+      ksrc = kc + p * a.kv_sb[1] + unit * 16;
+      vsrc = vc + p * a.kv_sb[1] + unit * 16;
     }
-    const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit);
-    cp_async16(k_dst + o, ksrc + (valid ? unit * 16 : 0), valid);
-    cp_async16(v_dst + o, vsrc + (valid ? unit * 16 : 0), valid);
+    const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion);
+    cp_async16(k_dst + o, ksrc, valid);
+    cp_async16(v_dst + o, vsrc, valid);
   }
 }
 
+struct TcGeometry {
+  int64_t len, first;
+  int start;
+  int n_tiles;  // KV tiles of this row tile (causal end of its last token)
+};
+
+__device__ __forceinline__ TcGeometry tc_geometry(const PrefillArgs& a, int64_t b, int64_t tok0, int tokens_per_tile,
+                                                  bool report) {
+  TcGeometry g;
+  int64_t len = a.chunk_lens[b];
+  if (len > a.padded_len) {
+    if (report) record_status(MI_STATUS_BAD_LENGTH);
+    len = a.padded_len;
+  }
+  g.len = len < 0 ? 0 : len;
+  g.first = a.padded_len - g.len;
+  int64_t start = a.starts[b];
+  if (start < 0) start = 0;
+  if (start > a.table_stride * a.block_size) {
+    if (report) record_status(MI_STATUS_BAD_LENGTH);
+    start = a.table_stride * a.block_size;
+  }
+  g.start = (int)start;
+  const int64_t tok_end = min(g.len, tok0 + tokens_per_tile);
+  g.n_tiles = tok0 < g.len ? (int)((start + tok_end + kTcKv - 1) / kTcKv) : 0;
+  return g;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const PrefillArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const PrefillArgs a, float* ws_o, float* ws_ml,
+                                                                    int max_splits, int shift) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -170,48 +223,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   uint64_t* bar_o = bar_s + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
 
-  const int qtile = blockIdx.x;
+  const int qtile = blockIdx.x / max_splits;
+  const int split = blockIdx.x % max_splits;
   const int h = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int G = a.groups;
   const int tokens_per_tile = kTcRows / G;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-
-  int64_t len = a.chunk_lens[b];
-  if (len > a.padded_len) {
-    if (tid == 0 && qtile == 0 && h == 0) record_status(MI_STATUS_BAD_LENGTH);
-    len = a.padded_len;
-  }
-  if (len < 0) len = 0;
-  const int64_t first = a.padded_len - len;
-  int64_t start = a.starts[b];
-  if (start < 0) start = 0;
-  if (start > a.table_stride * a.block_size) {
-    if (tid == 0 && qtile == 0 && h == 0) record_status(MI_STATUS_BAD_LENGTH);
-    start = a.table_stride * a.block_size;
-  }
-  const int row_bytes_out = a.hq * kTcDim;  // elements per output position
+  const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
+  const TcGeometry geo = tc_geometry(a, b, tok0, tokens_per_tile, tid == 0 && blockIdx.x == 0 && h == 0);
+  const int64_t first = geo.first;
+  const int start = geo.start;
+  const int row_elems = a.hq * kTcDim;  // elements per output position
   T* out = reinterpret_cast<T*>(a.out);
 
-  // Padding positions of this KV head's query heads are zeros (the CTA of tile 0 writes them).
-  if (qtile == 0) {
-    for (int64_t i = tid; i < first * G * (kTcDim / 8); i += kTcThreads) {
-      const int64_t p = i / (G * (kTcDim / 8));
-      const int rem = (int)(i % (G * (kTcDim / 8)));
-      const int g = rem / (kTcDim / 8);
-      const int u = rem % (kTcDim / 8);
-      *reinterpret_cast<uint4*>(out + (b * a.padded_len + p) * row_bytes_out + (int64_t)(h * G + g) * kTcDim + u * 8) =
+  // Padding positions of this KV head's query heads are zeros (written by tile 0, split 0).
+  if (blockIdx.x == 0) {
+    const int per_pos = G * (kTcDim / 8);
+    for (int64_t i = tid; i < first * per_pos; i += kTcThreads) {
+      const int64_t p = i / per_pos;
+      const int rem = (int)(i - p * per_pos);
+      *reinterpret_cast<uint4*>(out + (b * a.padded_len + p) * row_elems + (int64_t)(h * G) * kTcDim + rem * 8) =
           make_uint4(0, 0, 0, 0);
     }
   }
-  const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
-  if (tok0 >= len) return;  // uniform for the CTA
-  const int64_t tok_end = min(len, tok0 + tokens_per_tile);
-  const int64_t kv_end = start + tok_end;  // causal end of the last token of the tile
-  const int n_tiles = (int)((kv_end + kTcKv - 1) / kTcKv);
+  const int t_begin = split * kTilesPerSplit;
+  if (t_begin >= geo.n_tiles) return;  // uniform for the CTA
+  const int t_end = min(geo.n_tiles, t_begin + kTilesPerSplit);
+  const int n_splits = (geo.n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
+  const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
+  const int kv_end = start + (int)tok_end;  // causal end of the tile's last token
+  const BlockAddr ba{shift, (uint32_t)a.block_size};
 
-  // ---- setup: barriers, TMEM ----
   if (tid == 0) {
     mbar_init(bar_s, 1);
     mbar_init(bar_o, 1);
@@ -230,20 +274,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
       const bool valid = tok < tok_end;
       const char* src = a.q;
       if (valid) src = a.q + b * a.q_sb[0] + (first + tok) * a.q_sb[1] + (int64_t)(h * G + r % G) * a.q_sb[2] + unit * 16;
-      cp_async16(sbase + kOffQ + sw128_offset((uint32_t)r, (uint32_t)unit), src, valid);
+      cp_async16(sbase + kOffQ + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
     }
   }
-  stage_kv<T>(a, b, h, start, kv_end, first, 0, sbase + kOffK, sbase + kOffV);
+  stage_kv<T>(a, ba, b, h, start, kv_end, first, t_begin * kTcKv, sbase + kOffK, sbase + kOffV);
   cp_async_commit();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem;
-  const uint32_t tmem_o = tmem + kTcKv;
   const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t tmem_s = tmem;
+  const uint32_t tmem_o = tmem + kTmemO;
 
-  constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+  constexpr bool kBf16 = !std::is_same<T, __half>::value;
   const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
   const uint32_t idesc_pv = idesc_f16(kBf16, true, kTcRows, kTcDim);
 
@@ -251,52 +295,64 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   const int r = tid;
   const int64_t my_tok = tok0 + r / G;
   const bool row_valid = my_tok < tok_end;
-  const int64_t my_kv_end = row_valid ? start + my_tok + 1 : 0;  // keys [0, my_kv_end) are visible
+  const int my_kv_end = row_valid ? start + (int)my_tok + 1 : 0;  // keys [0, my_kv_end) are visible
+  const int cta_min_kv_end = start + (int)tok0 + 1;                // smallest causal end of a valid row
   float m_ref = -INFINITY, l_run = 0.f;
   bool aborted = false;
   const float scale = a.scale_log2;
 
-  for (int j = 0; j < n_tiles; ++j) {
-    const int buf = j & 1;
-    cp_async_wait_all();  // tile j (and Q) landed
+  for (int t = t_begin; t < t_end; ++t) {
+    const int i = t - t_begin;
+    const int buf = i & 1;
+    const uint32_t kbuf = sbase + kOffK + buf * kKvBytes;
+    const uint32_t vbuf = sbase + kOffV + buf * kKvBytes;
+    cp_async_wait_all();  // tile t (and Q) landed
     fence_async_smem();
     __syncthreads();
-    if (j > 0) {
-      mbar_wait(bar_o, (j - 1) & 1, aborted);  // PV of tile j-1 finished: its V buffer and P are free
+    if (i > 0) {
+      mbar_wait(bar_o, (i - 1) & 1, aborted);  // PV of tile t-1 done: its K (P) and V buffers are free
       tc_fence_after();
     }
-    if (j + 1 < n_tiles) {
-      stage_kv<T>(a, b, h, start, kv_end, first, (int64_t)(j + 1) * kTcKv, sbase + kOffK + (buf ^ 1) * kTileBytes,
-                  sbase + kOffV + (buf ^ 1) * kTileBytes);
+    if (t + 1 < t_end) {
+      stage_kv<T>(a, ba, b, h, start, kv_end, first, (t + 1) * kTcKv, sbase + kOffK + (buf ^ 1) * kKvBytes,
+                  sbase + kOffV + (buf ^ 1) * kKvBytes);
       cp_async_commit();
     }
     // ---- S = Q K^T ----
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t q0 = sbase + kOffQ, k0 = sbase + kOffK + buf * kTileBytes;
+      const uint32_t q0 = sbase + kOffQ;
 #pragma unroll
       for (int s = 0; s < kTcDim / 16; ++s) {
-        const uint32_t off = (s >> 2) * kRegionBytes + (s & 3) * 32;
-        umma_f16(tmem_s, desc_kmajor(q0 + off), desc_kmajor(k0 + off), idesc_qk, s > 0 ? 1u : 0u);
+        umma_f16(tmem_s, desc_kmajor(q0 + (s >> 2) * kQRegion + (s & 3) * 32),
+                 desc_kmajor(kbuf + (s >> 2) * kKvRegion + (s & 3) * 32), idesc_qk, s > 0 ? 1u : 0u);
       }
       umma_commit(bar_s);
     }
-    mbar_wait(bar_s, j & 1, aborted);
+    mbar_wait(bar_s, i & 1, aborted);
     tc_fence_after();
-    // ---- online softmax of this row: pass 1 (row max) and pass 2 (exp, sum, P) over TMEM ----
-    const int64_t j0 = (int64_t)j * kTcKv;
+    // ---- online softmax of this row: pass 1 (row max), pass 2 (exp, sum, P) over TMEM ----
+    const int j0 = t * kTcKv;
+    const bool full = j0 + kTcKv <= cta_min_kv_end;  // no valid row masks anything in this tile
+    const int lim = my_kv_end - j0;                  // keys j0 + c < my_kv_end are visible
     float tile_max = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       float sv[32];
       tmem_ld32(tmem_s + lane_base + c * 32, sv);
+      if (full) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (j0 + c * 32 + i < my_kv_end) tile_max = fmaxf(tile_max, sv[i] * scale);
+        for (int e = 0; e < 32; ++e) tile_max = fmaxf(tile_max, sv[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (c * 32 + e < lim) tile_max = fmaxf(tile_max, sv[e]);
+      }
     }
+    tile_max *= scale;  // scale > 0 commutes with max
     const float m_new = fmaxf(m_ref, tile_max);
     // tcgen05.ld/st are warp-collective: the warp rescales together if any of its rows must.
-    const bool need = j > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
+    const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
     if (__any_sync(0xffffffffu, need)) {
       const float alpha = need ? exp2f(m_ref - m_new) : 1.f;
 #pragma unroll
@@ -304,7 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         float ov[32];
         tmem_ld32(tmem_o + lane_base + c * 32, ov);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+        for (int e = 0; e < 32; ++e) ov[e] *= alpha;
         tmem_st32(tmem_o + lane_base + c * 32, ov);
       }
     }
@@ -314,11 +370,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     } else if (m_ref == -INFINITY) {
       m_ref = m_new;
     }
-    float psum = 0.f;
-    uint8_t* p_tile = smem + kOffP;
     const bool live = m_ref != -INFINITY;
+    const float neg_m = -m_ref;
+    float psum = 0.f;
+    uint8_t* p_tile = smem + kOffK + buf * kKvBytes;  // K of this tile is dead: P goes there
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       float sv[32];
       tmem_ld32(tmem_s + lane_base + c * 32, sv);
 #pragma unroll
@@ -326,15 +383,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int i0 = u * 8 + 2 * e;
-          const bool v0 = live && j0 + c * 32 + i0 < my_kv_end;
-          const bool v1 = live && j0 + c * 32 + i0 + 1 < my_kv_end;
-          const float p0 = v0 ? exp2f(sv[i0] * scale - m_ref) : 0.f;
-          const float p1 = v1 ? exp2f(sv[i0 + 1] * scale - m_ref) : 0.f;
+          const int k0 = c * 32 + u * 8 + 2 * e;
+          const bool v0 = live && (full || k0 < lim);
+          const bool v1 = live && (full || k0 + 1 < lim);
+          const float p0 = v0 ? exp2f(fmaf(sv[u * 8 + 2 * e], scale, neg_m)) : 0.f;
+          const float p1 = v1 ? exp2f(fmaf(sv[u * 8 + 2 * e + 1], scale, neg_m)) : 0.f;
           psum += p0 + p1;
           w[e] = pack2<T>(p0, p1);
         }
-        *reinterpret_cast<uint4*>(p_tile + sw128_offset((uint32_t)r, (uint32_t)(c * 4 + u))) =
+        // P: 128 rows x 64 columns = one 16 KiB region of 128-byte rows
+        *reinterpret_cast<uint4*>(p_tile + sw128_offset((uint32_t)r, (uint32_t)(c * 4 + u), kQRegion)) =
             make_uint4(w[0], w[1], w[2], w[3]);
       }
     }
@@ -345,21 +403,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     // ---- O += P V ----
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t p0 = sbase + kOffP, v0 = sbase + kOffV + buf * kTileBytes;
 #pragma unroll
       for (int s = 0; s < kTcKv / 16; ++s) {
-        const uint32_t poff = (s >> 2) * kRegionBytes + (s & 3) * 32;
-        umma_f16(tmem_o, desc_kmajor(p0 + poff), desc_mnmajor(v0 + s * 2048), idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
+        umma_f16(tmem_o, desc_kmajor(kbuf + s * 32), desc_mnmajor(vbuf + s * 2048), idesc_pv,
+                 (i > 0 || s > 0) ? 1u : 0u);
       }
       umma_commit(bar_o);
     }
   }
-  mbar_wait(bar_o, (n_tiles - 1) & 1, aborted);
+  mbar_wait(bar_o, (t_end - t_begin - 1) & 1, aborted);
   tc_fence_after();
-  // ---- epilogue: O / l -> output row ----
-  {
+  // ---- epilogue ----
+  if (n_splits == 1) {
     const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    T* dst = out + (b * a.padded_len + first + my_tok) * row_bytes_out + (int64_t)(h * G + r % G) * kTcDim;
+    T* dst = out + (b * a.padded_len + first + my_tok) * row_elems + (int64_t)(h * G + r % G) * kTcDim;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       float ov[32];
@@ -376,6 +433,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         }
       }
     }
+  } else {
+    // unnormalised partial of this split: O row (fp32), m and l
+    const int64_t part = ((b * a.hkv + h) * gridDim.x + blockIdx.x);
+    float* po = ws_o + (part * kTcRows + r) * kTcDim;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float ov[32];
+      tmem_ld32(tmem_o + lane_base + c * 32, ov);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<float4*>(po + c * 32 + u * 4) = make_float4(ov[u * 4], ov[u * 4 + 1], ov[u * 4 + 2], ov[u * 4 + 3]);
+    }
+    *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_run);
   }
   tc_fence_before();
   __syncthreads();
@@ -385,25 +455,112 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   }
 }
 
+// Merge the split partials of row tiles that needed more than one split: one warp per row.
 template <typename T>
-cudaError_t launch_tc(const PrefillArgs& a, cudaStream_t s) {
+__global__ void __launch_bounds__(128) prefill_combine_kernel(const PrefillArgs a, const float* ws_o,
+                                                              const float* ws_ml, int max_splits) {
+  const int qtile = blockIdx.x;
+  const int h = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int G = a.groups;
+  const int tokens_per_tile = kTcRows / G;
+  const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
+  const TcGeometry geo = tc_geometry(a, b, tok0, tokens_per_tile, false);
+  const int n_splits = (geo.n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
+  if (n_splits <= 1) return;
+  const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t grid_x = (int64_t)gridDim.x * max_splits;
+  T* out = reinterpret_cast<T*>(a.out);
+  for (int r = warp; r < kTcRows; r += 4) {
+    const int64_t tok = tok0 + r / G;
+    if (tok >= tok_end) continue;
+    float m_all = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) {
+      const int64_t part = (b * a.hkv + h) * grid_x + (int64_t)qtile * max_splits + s;
+      m_all = fmaxf(m_all, ws_ml[(part * kTcRows + r) * 2]);
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l_all = 0.f;
+    for (int s = 0; s < n_splits; ++s) {
+      const int64_t part = (b * a.hkv + h) * grid_x + (int64_t)qtile * max_splits + s;
+      const float2 ml = *reinterpret_cast<const float2*>(ws_ml + (part * kTcRows + r) * 2);
+      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m_all);
+      l_all += w * ml.y;
+      const float4 o = *reinterpret_cast<const float4*>(ws_o + (part * kTcRows + r) * kTcDim + lane * 4);
+      acc.x += w * o.x;
+      acc.y += w * o.y;
+      acc.z += w * o.z;
+      acc.w += w * o.w;
+    }
+    const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
+    T* dst = out + (b * a.padded_len + geo.first + tok) * (int64_t)(a.hq * kTcDim) +
+             (int64_t)(h * G + r % G) * kTcDim + lane * 4;
+    uint2 pk;
+    pk.x = pack2<T>(acc.x * inv, acc.y * inv);
+    pk.y = pack2<T>(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(dst) = pk;
+  }
+}
+
+struct TcPlan {
+  int64_t qtiles;
+  int max_splits;
+  size_t ws_o_bytes, ws_ml_bytes;
+};
+
+TcPlan tc_plan(const PrefillArgs& a) {
+  TcPlan p;
+  const int tokens_per_tile = kTcRows / a.groups;
+  p.qtiles = (a.padded_len + tokens_per_tile - 1) / tokens_per_tile;
+  const int64_t max_kv = a.table_stride * a.block_size + a.padded_len;
+  const int64_t max_tiles = (max_kv + kTcKv - 1) / kTcKv;
+  p.max_splits = (int)std::max<int64_t>(1, (max_tiles + kTilesPerSplit - 1) / kTilesPerSplit);
+  const int64_t parts = p.max_splits > 1 ? a.batch * a.hkv * p.qtiles * p.max_splits : 0;
+  p.ws_o_bytes = (size_t)parts * kTcRows * kTcDim * sizeof(float);
+  p.ws_ml_bytes = (size_t)parts * kTcRows * 2 * sizeof(float);
+  return p;
+}
+
+int log2_if_pow2(int x) {
+  if (x <= 0 || (x & (x - 1))) return -1;
+  int s = 0;
+  while ((1 << s) < x) ++s;
+  return s;
+}
+
+template <typename T>
+cudaError_t launch_tc(const PrefillArgs& a, float* ws, cudaStream_t s) {
   auto kern = prefill_tc_kernel<T>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
   if (e != cudaSuccess) return e;
-  const int tokens_per_tile = kTcRows / a.groups;
-  const int64_t qtiles = (a.padded_len + tokens_per_tile - 1) / tokens_per_tile;
-  dim3 grid((unsigned)qtiles, (unsigned)a.hkv, (unsigned)a.batch);
-  kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a);
+  const TcPlan p = tc_plan(a);
+  float* ws_o = ws;
+  float* ws_ml = ws ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ((p.ws_o_bytes + 255) & ~size_t(255)))
+                    : nullptr;
+  dim3 grid((unsigned)(p.qtiles * p.max_splits), (unsigned)a.hkv, (unsigned)a.batch);
+  kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a, ws_o, ws_ml, p.max_splits, log2_if_pow2(a.block_size));
+  e = cudaGetLastError();
+  if (e != cudaSuccess || p.max_splits == 1) return e;
+  dim3 cgrid((unsigned)p.qtiles, (unsigned)a.hkv, (unsigned)a.batch);
+  prefill_combine_kernel<T><<<cgrid, 128, 0, s>>>(a, ws_o, ws_ml, p.max_splits);
   return cudaGetLastError();
 }
 
 }  // namespace
+
+size_t prefill_tc_workspace_bytes(const PrefillArgs& a) {
+  const TcPlan p = tc_plan(a);
+  if (p.max_splits == 1) return 0;
+  return ((p.ws_o_bytes + 255) & ~size_t(255)) + ((p.ws_ml_bytes + 255) & ~size_t(255));
+}
 
 bool prefill_tc_supported(const PrefillArgs& a, int dtype) {
   if (dtype != MI_BF16 && dtype != MI_F16) return false;
   if (a.head_dim != kTcDim) return false;
   if (!(a.groups == 1 || a.groups == 2 || a.groups == 4 || a.groups == 8)) return false;
   if (a.batch > 65535 || a.hkv > 65535) return false;
+  if (a.table_stride * a.block_size + a.padded_len >= (int64_t(1) << 30)) return false;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!al16(a.q) || !al16(a.k_chunk) || !al16(a.v_chunk) || !al16(a.out)) return false;
   if (a.table_stride > 0 && (!al16(a.k_pool) || !al16(a.v_pool))) return false;
@@ -412,9 +569,9 @@ bool prefill_tc_supported(const PrefillArgs& a, int dtype) {
   return true;
 }
 
-cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, int dtype, cudaStream_t s) {
-  if (dtype == MI_BF16) return launch_tc<__nv_bfloat16>(a, s);
-  return launch_tc<__half>(a, s);
+cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, int dtype, cudaStream_t s) {
+  if (dtype == MI_BF16) return launch_tc<__nv_bfloat16>(a, ws, s);
+  return launch_tc<__half>(a, ws, s);
 }
 
 }  // namespace mi

@@ -15,7 +15,7 @@ import torch
 from mini_infra_b200 import _native as nat
 
 _DTYPES = {torch.float32: nat.MI_F32, torch.bfloat16: nat.MI_BF16, torch.float16: nat.MI_F16}
-_workspaces: dict[int, torch.Tensor] = {}
+_workspaces: dict[tuple[int, str], torch.Tensor] = {}
 
 
 def dtype_code(dtype: torch.dtype) -> int:
@@ -65,9 +65,9 @@ def _check_pool(k_pool: torch.Tensor, v_pool: torch.Tensor) -> tuple[int, int, i
     return int(n), int(bs), int(h), int(d)
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A per-device byte buffer of at least nbytes (reused across calls on the same stream)."""
-    key = device.index if device.index is not None else torch.cuda.current_device()
+def workspace(device: torch.device, nbytes: int, slot: str = "decode") -> torch.Tensor:
+    """A per-device, per-purpose byte buffer of at least nbytes (reused across calls on the same stream)."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), slot)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         size = max(nbytes, 1 << 20)
@@ -290,11 +290,18 @@ def paged_prefill(
     code = dtype_code(query.dtype)
     table_stride = tables.stride(0) if tables.ndim == 2 and tables.shape[1] > 0 else 0
     lib = nat.load()
+    need = int(lib.mi_paged_prefill_workspace_size(b, length, hq, h, d, table_stride, bs, code))
+    ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+    if need:
+        ws = workspace(device, need, slot="prefill")
+        base = ws.data_ptr()
+        ws_ptr = ctypes.c_void_p((base + 255) & ~255)
+        ws_bytes = ws.numel() - ((base + 255) & ~255) + base
     rc = lib.mi_paged_prefill(
         _ptr(query), nat.i64_array([query.stride(0), query.stride(1), query.stride(2)]), _ptr(key_chunk),
         _ptr(value_chunk), nat.i64_array([key_chunk.stride(0), key_chunk.stride(1), key_chunk.stride(2)]),
         _ptr(k_pool), _ptr(v_pool), n, bs, h, d, _ptr(tables) if table_stride else ctypes.c_void_p(0), table_stride,
-        _ptr(starts), _ptr(lens), b, length, hq, float(scale), _ptr(out), code, _stream(device),
+        _ptr(starts), _ptr(lens), b, length, hq, float(scale), _ptr(out), ws_ptr, ws_bytes, code, _stream(device),
     )
     nat.check(rc, "mi_paged_prefill")
     return out

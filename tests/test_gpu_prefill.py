@@ -88,6 +88,8 @@ TC_SHAPES = [
     (16, 8, 128, 16, [3000, 129, 0], [128, 128, 128]),  # long history, several KV tiles
     (16, 8, 128, 32, [257], [300]),                     # chunk spans several q-tiles; block size 32
     (32, 8, 128, 1, [33, 7], [9, 64]),                  # block size 1
+    (16, 8, 128, 24, [500, 60], [70, 128]),             # block size not a power of two
+    (16, 8, 128, 16, [9000, 2100, 0], [33, 128, 5]),    # history split over several CTAs + combine
 ]
 
 

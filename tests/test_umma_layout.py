@@ -15,17 +15,18 @@ and checks that every element each of the 8 + 8 MMAs of a tile reads sits exactl
 writer put it, and that no read leaves the operand's 32 KiB buffer.
 """
 
-REGION = 16384
-TILE = 32768
+Q_REGION = 128 * 128  # Q: 128 rows x 128 columns -> two 16 KiB regions
+KV_REGION = 64 * 128  # K, V: 64 rows x 128 columns -> two 8 KiB regions
+P_REGION = 128 * 128  # P: 128 rows x 64 columns -> one 16 KiB region (written into the K buffer)
 
 
-def sw128_offset(row, unit16):
-    return (unit16 >> 3) * REGION + row * 128 + (((unit16 & 7) ^ (row & 7)) << 4)
+def sw128_offset(row, unit16, region):
+    return (unit16 >> 3) * region + row * 128 + (((unit16 & 7) ^ (row & 7)) << 4)
 
 
-def writer_addr(row, col):
-    """Byte offset of element (row, col) of a 128 x 128 16-bit operand as the kernel writes it."""
-    return sw128_offset(row, col // 8) + (col % 8) * 2
+def writer_addr(row, col, region):
+    """Byte offset of element (row, col) of a 16-bit operand as the kernel writes it."""
+    return sw128_offset(row, col // 8, region) + (col % 8) * 2
 
 
 def swizzle(addr):
@@ -60,44 +61,50 @@ def idesc(bf16, b_mn, m, n):
 def test_descriptor_fields():
     f = decode(desc(0x1A400, 16, 1024))
     assert f == dict(start=0x1A400, lbo=16, sbo=1024, version=1, layout=2)
-    f = decode(desc(0x28000, REGION, 1024))
-    assert f["lbo"] == REGION and f["sbo"] == 1024
+    f = decode(desc(0x8000, KV_REGION, 1024))
+    assert f["lbo"] == KV_REGION and f["sbo"] == 1024
     i = idesc(1, 1, 128, 128)
     assert (i >> 4) & 3 == 1 and (i >> 7) & 7 == 1 and (i >> 10) & 7 == 1
     assert (i >> 15) & 1 == 0 and (i >> 16) & 1 == 1
     assert (i >> 17) & 0x3F == 16 and (i >> 24) & 0x1F == 8
+    assert (idesc(1, 0, 128, 64) >> 17) & 0x3F == 8
 
 
 def test_qk_operands_read_what_the_writer_stored():
-    base_q, base_k = 0, 1024 * 64  # any 1024-aligned buffers
+    base_q, base_k = 0, 32768  # Q at 0, first K buffer right after (both 1024-aligned)
     for s in range(8):  # k-steps over head_dim
-        off = (s >> 2) * REGION + (s & 3) * 32
-        dq, dk = desc(base_q + off, 16, 1024), desc(base_k + off, 16, 1024)
-        for m in range(128):
-            for k in range(16):
-                col = s * 16 + k
+        dq = desc(base_q + (s >> 2) * Q_REGION + (s & 3) * 32, 16, 1024)
+        dk = desc(base_k + (s >> 2) * KV_REGION + (s & 3) * 32, 16, 1024)
+        for k in range(16):
+            col = s * 16 + k
+            for m in range(128):  # M = 128 query rows
                 a = kmajor_read(dq, m, k)
-                assert a == base_q + writer_addr(m, col)
-                assert base_q <= a < base_q + TILE
-                assert kmajor_read(dk, m, k) == base_k + writer_addr(m, col)
+                assert a == base_q + writer_addr(m, col, Q_REGION)
+                assert base_q <= a < base_q + 2 * Q_REGION
+            for n in range(64):  # N = 64 KV rows
+                a = kmajor_read(dk, n, k)
+                assert a == base_k + writer_addr(n, col, KV_REGION)
+                assert base_k <= a < base_k + 2 * KV_REGION
 
 
 def test_pv_operands_read_what_the_writer_stored():
-    base_p, base_v = 4 * TILE, 5 * TILE
-    for s in range(8):  # k-steps over the 128 KV positions of the tile
-        poff = (s >> 2) * REGION + (s & 3) * 32
-        dp = desc(base_p + poff, 16, 1024)
-        dv = desc(base_v + s * 2048, REGION, 1024)
+    base_p, base_v = 32768, 65536  # P lives in the tile's K buffer; V in its own buffer
+    for s in range(4):  # k-steps over the 64 KV positions of the tile
+        dp = desc(base_p + s * 32, 16, 1024)
+        dv = desc(base_v + s * 2048, KV_REGION, 1024)
         for k in range(16):
             kv = s * 16 + k
             for m in range(128):
-                assert kmajor_read(dp, m, k) == base_p + writer_addr(m, kv)
+                a = kmajor_read(dp, m, k)
+                assert a == base_p + writer_addr(m, kv, P_REGION)
+                assert base_p <= a < base_p + P_REGION  # P fits the 16 KiB K buffer
             for n in range(128):  # N = head_dim column of V
                 a = mnmajor_read(dv, n, k)
-                assert a == base_v + writer_addr(kv, n)
-                assert base_v <= a < base_v + TILE
+                assert a == base_v + writer_addr(kv, n, KV_REGION)
+                assert base_v <= a < base_v + 2 * KV_REGION
 
 
-def test_smem_budget():
-    # Q + 2 K + 2 V + P tiles + barriers + alignment slack must fit the 227 KiB opt-in limit
-    assert 6 * TILE + 64 + 1024 <= 227 * 1024
+def test_smem_budget_two_ctas_per_sm():
+    per_cta = 2 * Q_REGION + 2 * (2 * KV_REGION) + 2 * (2 * KV_REGION) + 64 + 1024
+    assert per_cta <= 227 * 1024
+    assert 2 * (per_cta + 1024) <= 228 * 1024  # two CTAs (+1 KiB reserved each) share an SM
