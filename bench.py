@@ -328,15 +328,100 @@ def run_c4(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def c3_requests(num: int, seed: int, max_new: int, rate_per_s: float = 32.0, lo: int = 32, hi: int = 2048):
+    """Config 3 workload: Poisson arrivals (rate 32/s on the logical clock), prompt lengths
+    log-uniform in [32, 2048], token ids uniform in [1000, 100000), greedy max_new tokens."""
+    from mini_infra_b200.core import make_requests
+
+    rng = np.random.RandomState(seed)
+    gaps = rng.exponential(1000.0 / rate_per_s, size=num)
+    arrivals = np.cumsum(gaps) - gaps[0]
+    lens = np.exp(rng.uniform(np.log(lo), np.log(hi), size=num)).astype(int)
+    prompts = [rng.randint(1000, 100000, size=int(n)).tolist() for n in lens]
+    return make_requests(prompts, max_new, arrivals.tolist())
+
+
+def run_c3(args) -> None:
+    """Config 3: the full paged engine on random-init Qwen3-0.6B (bf16), 128 requests.
+
+    Warm-up = `warmup` small engine runs; each timed step = one full run of the 128-request workload
+    through ``run_scheduler`` (paged-kv-cache + continuous batching).  ``value`` = decode tokens /
+    decode-step time (ms summed over decode events, rank 0's clock, which all ranks share);
+    with N ranks the model is KV-head partitioned (strong scaling: same requests)."""
+    import datetime
+
+    from mini_infra_b200.core import BatchingMethod, PagedCacheConfig, SchedulerConfig
+    from mini_infra_b200.engine import EngineConfig, run_scheduler
+    from mini_infra_b200.model import QWEN3_0_6B, HeadPartition, Qwen3Config, build_model
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        group = dist.group.WORLD
+    cfg = Qwen3Config(**QWEN3_0_6B, torch_dtype="bfloat16")
+    model = build_model(cfg, seed=0, device=device, dtype=torch.bfloat16, partition=HeadPartition(rank, world, group),
+                        generator_device="cuda")
+    engine = EngineConfig(PagedCacheConfig(block_size=16), BatchingMethod.CONTINUOUS,
+                          scheduler_config=SchedulerConfig(None))
+    for i in range(args.warmup):
+        run_scheduler(engine, model, c3_requests(8, 100 + i, 8), None, stop_on_eos=False)
+    results = []
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            torch.cuda.synchronize(device)
+            results.append(run_scheduler(engine, model, c3_requests(128, SEED + i, 128), None, stop_on_eos=False))
+    if rank == 0:
+        dec_tokens = sum(r.schedule_metrics.decode_tokens for r in results)
+        dec_ms = sum(r.schedule_metrics.decode_ms for r in results)
+        out_tokens = sum(r.schedule_metrics.num_output_tokens for r in results)
+        busy_ms = sum(r.schedule_metrics.busy_ms for r in results)
+        steps = sum(len(r.events) for r in results)
+        line = {
+            "metric": "engine decode tok/s", "value": dec_tokens * 1000.0 / dec_ms, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": busy_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, uniform token ids)",
+            "config": {"workload": "config3_engine_qwen3_0.6b", "model": "Qwen3-0.6B shape (28L, 16q/8kv, d128)",
+                       "requests": 128, "arrivals": "Poisson 32/s", "prompt_len": "log-uniform[32,2048]",
+                       "max_new_tokens": 128, "engine": str(engine), "engine_steps": steps,
+                       "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU"},
+            "engine": {"decode_tokens": dec_tokens, "decode_ms": dec_ms, "throughput_tok_s": out_tokens * 1000.0 / busy_ms,
+                       "busy_ms": busy_ms, "prefill_steps": sum(r.schedule_metrics.num_prefill_steps for r in results),
+                       "decode_steps": sum(r.schedule_metrics.num_decode_steps for r in results)},
+            "e2e": {"value": out_tokens * 1000.0 / sum(r.e2e_wall_ms for r in results),
+                    "unit": "tok/s (all generated tokens over the engine's wall clock)",
+                    "h2d_bytes_per_step": sum(r.extra["h2d_bytes"] for r in results) / steps,
+                    "d2h_bytes_per_step": sum(r.extra["d2h_bytes"] for r in results) / steps},
+            "clocks": clocks.summary(),
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default 3000 for c2, 20 for c5)")
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 20 for c2, 3 for c5)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c4"], default="c2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c3", "c4"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.workload == "c3":
+        args.steps = args.steps or 1
+        args.warmup = args.warmup or 3
+        run_c3(args)
+        return
     if args.workload == "c4":
         args.steps = args.steps or 200
         args.warmup = args.warmup or 5

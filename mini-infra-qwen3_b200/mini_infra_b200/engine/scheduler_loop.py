@@ -76,7 +76,9 @@ def _run_loop(backend: PagedScheduleBackend, requests: Sequence[Request], max_ru
         ))
     synchronize(backend.device)
     wall_ms = (time.perf_counter() - wall0) * 1000.0
-    return summarize_schedule(states, events, max_running_requests, wall_ms, backend.collect_paged_cache_profile())
+    result = summarize_schedule(states, events, max_running_requests, wall_ms, backend.collect_paged_cache_profile())
+    result.extra.update(h2d_bytes=backend.runner.h2d_bytes, d2h_bytes=backend.runner.d2h_bytes)
+    return result
 
 
 @torch.inference_mode()

@@ -45,6 +45,15 @@ def _to_device(values: list[int], device: torch.device) -> torch.Tensor:
 
 
 class PagedRunner(BaseModelRunner):
+    """Counters ``h2d_bytes`` / ``d2h_bytes`` accumulate the host<->device traffic of its steps."""
+
+    h2d_bytes = 0
+    d2h_bytes = 0
+
+    def _upload(self, values: list[int]) -> torch.Tensor:
+        self.h2d_bytes += 8 * len(values)
+        return _to_device(values, self.device)
+
     def run_prefill_chunk_step(
         self,
         chunk_token_ids: Sequence[Sequence[int]],
@@ -72,7 +81,7 @@ class PagedRunner(BaseModelRunner):
             if len(table) < h:
                 raise ValueError(f"block table {list(table)} does not cover {h} history blocks")
             flat += [int(x) for x in table[:h]] + [_NULL_BLOCK_ID] * (nb - h)
-        packed = _to_device(flat, self.device)
+        packed = self._upload(flat)
         o = b * width
         input_ids = packed[:o].view(b, width)
         position_ids = packed[o : 2 * o].view(b, width)
@@ -86,6 +95,7 @@ class PagedRunner(BaseModelRunner):
         with StepTimer(self.device) as timer:
             logits, presents = self.model(input_ids, position_ids=position_ids, attn_metadata=metadata, last_only=True)
             next_token, _ = greedy_sample(logits)
+        self.d2h_bytes += 8 * b
         return PrefillOutput(next_token.squeeze(-1).tolist(), KVCache(presents), timer.elapsed_ms)
 
     def store_prefill(
@@ -107,7 +117,7 @@ class PagedRunner(BaseModelRunner):
         flat = [int(n) for n in chunk_lens] + [int(s) for s in start_positions]
         for table, k in zip(block_tables, need):
             flat += [int(x) for x in table[:k]] + [_NULL_BLOCK_ID] * (width - k)
-        packed = _to_device(flat, self.device)
+        packed = self._upload(flat)
         pool.store_chunks(prefill_cache, packed[:b], packed[b : 2 * b], packed[2 * b :].view(b, width))
 
     def prepare_decode_inputs(
@@ -124,7 +134,7 @@ class PagedRunner(BaseModelRunner):
         flat = [int(x) for x in last_tokens] + [int(p) for p in positions] + slots + [int(p) + 1 for p in positions]
         for t in block_tables:
             flat += [int(x) for x in t] + [_NULL_BLOCK_ID] * (max_blocks - len(t))
-        packed = _to_device(flat, self.device)
+        packed = self._upload(flat)
         metadata = PagedAttentionMetadata(
             slot_mapping=packed[2 * b : 3 * b],
             block_tables=packed[4 * b :].view(b, max_blocks),
@@ -144,6 +154,7 @@ class PagedRunner(BaseModelRunner):
                 input_ids, position_ids=position_ids, attn_metadata=metadata._replace(kv_pools=tuple(pool.kv_pools))
             )
             next_token, _ = greedy_sample(logits)
+        self.d2h_bytes += 8 * input_ids.shape[0]
         return PagedDecodeOutput(next_token.squeeze(-1).tolist(), timer.elapsed_ms)
 
 
