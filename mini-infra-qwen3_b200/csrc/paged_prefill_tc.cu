@@ -43,7 +43,11 @@ namespace {
 constexpr int kTcRows = 128;                        // query rows per CTA (MMA M)
 constexpr int kTcKv = 64;                           // KV positions per tile
 constexpr int kTcDim = 128;                         // head_dim
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 192;                    // warp 0 loader, warp 1 MMA, warps 2-5 softmax
+constexpr int kLoaderWarp = 0;
+constexpr int kMmaWarp = 1;
+constexpr int kLoaderThreads = 32;
+constexpr int kSoftmaxThreads = 128;
 constexpr int kTilesPerSplit = 32;                  // 2048 KV positions per CTA at most
 constexpr int kQRegion = kTcRows * 128;             // 16 KiB: one 64-column half of Q
 constexpr int kKvRegion = kTcKv * 128;              // 8 KiB: one 64-column half of a K or V tile
@@ -53,8 +57,8 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;              // two buffers
 constexpr int kOffV = kOffK + 2 * kKvBytes;         // two buffers
 constexpr int kOffBar = kOffV + 2 * kKvBytes;
-constexpr int kTcSmemBytes = kOffBar + 64 + 1024;   // barriers + TMEM slot + alignment slack (~97 KiB)
-constexpr uint32_t kTmemCols = 256;                 // S: [0, 64), O: [128, 256)
+constexpr int kTcSmemBytes = kOffBar + 128 + 1024;  // barriers + TMEM slot + alignment slack (~97 KiB)
+constexpr uint32_t kTmemCols = 256;                 // S tiles: [0, 64) and [64, 128); O: [128, 256)
 constexpr uint32_t kTmemO = 128;
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -145,19 +149,20 @@ struct BlockAddr {
   }
 };
 
-// Stage one 64-position KV tile (K and V) of KV head h: positions [j0, j0 + 64).  Thread t moves
-// 16-byte unit (t % 16) of rows t/16, t/16 + 8, ...: 16 threads cover one 256-byte row.
+// Stage one 64-position KV tile (K and V) of KV head h, positions [j0, j0 + 64), by `nthreads`
+// threads (thread `ti`): 16 threads cover one 256-byte row, 16-byte unit (ti % 16) each.
 template <typename T>
 __device__ __forceinline__ void stage_kv(const PrefillArgs& a, const BlockAddr& ba, int64_t b, int h, int start,
-                                         int kv_end, int64_t first, int j0, uint32_t k_dst, uint32_t v_dst) {
-  const int unit = threadIdx.x & 15;
+                                         int kv_end, int64_t first, int j0, uint32_t k_dst, uint32_t v_dst, int ti,
+                                         int nthreads) {
+  const int unit = ti & 15;
   const int64_t* table = a.block_tables + b * a.table_stride;
-  const char* kc = a.k_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2];
-  const char* vc = a.v_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2];
+  const char* kc = a.k_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
+  const char* vc = a.v_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
   const int64_t pool_row = (int64_t)a.hkv * kTcDim * sizeof(T);
   const int64_t head_off = (int64_t)h * kTcDim * sizeof(T) + unit * 16;
-#pragma unroll
-  for (int rr = threadIdx.x >> 4; rr < kTcKv; rr += kTcThreads / 16) {
+#pragma unroll 4
+  for (int rr = ti >> 4; rr < kTcKv; rr += nthreads / 16) {
     const int j = j0 + rr;
     const char* ksrc = a.k_chunk;  // any valid address when zero-filling
     const char* vsrc = a.k_chunk;
@@ -175,14 +180,23 @@ __device__ __forceinline__ void stage_kv(const PrefillArgs& a, const BlockAddr& 
         vsrc = a.v_pool + o;
       }
     } else if (valid) {
-      const int64_t p = first + (j - start);
-      ksrc = kc + p * a.kv_sb[1] + unit * 16;
-      vsrc = vc + p * a.kv_sb[1] + unit * 16;
+      const int64_t pos = first + (j - start);
+      ksrc = kc + pos * a.kv_sb[1];
+      vsrc = vc + pos * a.kv_sb[1];
     }
     const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion);
     cp_async16(k_dst + o, ksrc, valid);
     cp_async16(v_dst + o, vsrc, valid);
   }
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 struct TcGeometry {
@@ -219,9 +233,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* bar_o = bar_s + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2] loader -> MMA: stage landed
+  uint64_t* kv_empty = bars + 3;  // [2] MMA -> loader: PV of the stage done
+  uint64_t* s_full = bars + 5;    // [2] MMA -> softmax: S tile ready
+  uint64_t* p_full = bars + 7;    // [2] softmax -> MMA: P written (and S consumed)
+  uint64_t* o_done = bars + 9;    // MMA -> softmax: one phase per PV (rescale waits)
+  uint64_t* o_final = bars + 10;  // MMA -> softmax: the last PV is done (epilogue)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
 
   const int qtile = blockIdx.x / max_splits;
   const int split = blockIdx.x % max_splits;
@@ -231,6 +251,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   const int tokens_per_tile = kTcRows / G;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const int lane = tid & 31;
   const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
   const TcGeometry geo = tc_geometry(a, b, tok0, tokens_per_tile, tid == 0 && blockIdx.x == 0 && h == 0);
   const int64_t first = geo.first;
@@ -251,205 +272,212 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   const int t_begin = split * kTilesPerSplit;
   if (t_begin >= geo.n_tiles) return;  // uniform for the CTA
   const int t_end = min(geo.n_tiles, t_begin + kTilesPerSplit);
+  const int n = t_end - t_begin;
   const int n_splits = (geo.n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
   const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
   const int kv_end = start + (int)tok_end;  // causal end of the tile's last token
-  const BlockAddr ba{shift, (uint32_t)a.block_size};
 
   if (tid == 0) {
-    mbar_init(bar_s, 1);
-    mbar_init(bar_o, 1);
+    mbar_init(q_full, kLoaderThreads);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], kLoaderThreads);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], kSoftmaxThreads);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  // ---- stage Q (row r = token r/G, head r%G) and the first KV tile ----
-  {
-    const int unit = tid & 15;
-    for (int r = tid >> 4; r < kTcRows; r += kTcThreads / 16) {
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool aborted = false;
+
+  if (warp == kLoaderWarp) {
+    // ---------------- loader: Q once, then K/V tiles into a 2-stage ring ----------------
+    const BlockAddr ba{shift, (uint32_t)a.block_size};
+    const int unit = lane & 15;
+    for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
       const int64_t tok = tok0 + r / G;
       const bool valid = tok < tok_end;
       const char* src = a.q;
       if (valid) src = a.q + b * a.q_sb[0] + (first + tok) * a.q_sb[1] + (int64_t)(h * G + r % G) * a.q_sb[2] + unit * 16;
       cp_async16(sbase + kOffQ + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
     }
-  }
-  stage_kv<T>(a, ba, b, h, start, kv_end, first, t_begin * kTcKv, sbase + kOffK, sbase + kOffV);
-  cp_async_commit();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  const uint32_t tmem_s = tmem;
-  const uint32_t tmem_o = tmem + kTmemO;
-
-  constexpr bool kBf16 = !std::is_same<T, __half>::value;
-  const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
-  const uint32_t idesc_pv = idesc_f16(kBf16, true, kTcRows, kTcDim);
-
-  // this thread's row
-  const int r = tid;
-  const int64_t my_tok = tok0 + r / G;
-  const bool row_valid = my_tok < tok_end;
-  const int my_kv_end = row_valid ? start + (int)my_tok + 1 : 0;  // keys [0, my_kv_end) are visible
-  const int cta_min_kv_end = start + (int)tok0 + 1;                // smallest causal end of a valid row
-  float m_ref = -INFINITY, l_run = 0.f;
-  bool aborted = false;
-  const float scale = a.scale_log2;
-
-  for (int t = t_begin; t < t_end; ++t) {
-    const int i = t - t_begin;
-    const int buf = i & 1;
-    const uint32_t kbuf = sbase + kOffK + buf * kKvBytes;
-    const uint32_t vbuf = sbase + kOffV + buf * kKvBytes;
-    cp_async_wait_all();  // tile t (and Q) landed
-    fence_async_smem();
-    __syncthreads();
-    if (i > 0) {
-      mbar_wait(bar_o, (i - 1) & 1, aborted);  // PV of tile t-1 done: its K (P) and V buffers are free
-      tc_fence_after();
+    cp_async_arrive_noinc(q_full);
+    for (int i = 0; i < n; ++i) {
+      const int st = i & 1;
+      if (i >= 2) mbar_wait(&kv_empty[st], ((i - 2) >> 1) & 1, aborted);
+      stage_kv<T>(a, ba, b, h, start, kv_end, first, (t_begin + i) * kTcKv, sbase + kOffK + st * kKvBytes,
+                  sbase + kOffV + st * kKvBytes, lane, kLoaderThreads);
+      cp_async_arrive_noinc(&kv_full[st]);
     }
-    if (t + 1 < t_end) {
-      stage_kv<T>(a, ba, b, h, start, kv_end, first, (t + 1) * kTcKv, sbase + kOffK + (buf ^ 1) * kKvBytes,
-                  sbase + kOffV + (buf ^ 1) * kKvBytes);
-      cp_async_commit();
-    }
-    // ---- S = Q K^T ----
-    if (tid == 0) {
-      tc_fence_after();
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer: S(i+1) overlaps softmax(i); PV(i) after P(i) ----------------
+    if (lane == 0) {
+      constexpr bool kBf16 = !std::is_same<T, __half>::value;
+      const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
+      const uint32_t idesc_pv = idesc_f16(kBf16, true, kTcRows, kTcDim);
       const uint32_t q0 = sbase + kOffQ;
+      auto issue_s = [&](int i) {
+        const int st = i & 1;
+        mbar_wait(&kv_full[st], (i >> 1) & 1, aborted);
+        fence_async_smem();
+        tc_fence_after();
+        const uint32_t kb = sbase + kOffK + st * kKvBytes;
 #pragma unroll
-      for (int s = 0; s < kTcDim / 16; ++s) {
-        umma_f16(tmem_s, desc_kmajor(q0 + (s >> 2) * kQRegion + (s & 3) * 32),
-                 desc_kmajor(kbuf + (s >> 2) * kKvRegion + (s & 3) * 32), idesc_qk, s > 0 ? 1u : 0u);
+        for (int s = 0; s < kTcDim / 16; ++s)
+          umma_f16(tmem + st * kTcKv, desc_kmajor(q0 + (s >> 2) * kQRegion + (s & 3) * 32),
+                   desc_kmajor(kb + (s >> 2) * kKvRegion + (s & 3) * 32), idesc_qk, s > 0 ? 1u : 0u);
+        umma_commit(&s_full[st]);
+      };
+      mbar_wait(q_full, 0, aborted);
+      issue_s(0);
+      for (int i = 0; i < n; ++i) {
+        const int st = i & 1;
+        if (i + 1 < n) issue_s(i + 1);  // its S buffer was consumed by softmax(i-1) (waited below last round)
+        mbar_wait(&p_full[st], (i >> 1) & 1, aborted);  // P(i) written, S(i) consumed
+        fence_async_smem();
+        tc_fence_after();
+        const uint32_t kb = sbase + kOffK + st * kKvBytes;  // holds P(i)
+        const uint32_t vb = sbase + kOffV + st * kKvBytes;
+#pragma unroll
+        for (int s = 0; s < kTcKv / 16; ++s)
+          umma_f16(tmem + kTmemO, desc_kmajor(kb + s * 32), desc_mnmajor(vb + s * 2048), idesc_pv,
+                   (i > 0 || s > 0) ? 1u : 0u);
+        umma_commit(&kv_empty[st]);
+        umma_commit(o_done);
       }
-      umma_commit(bar_s);
+      umma_commit(o_final);
     }
-    mbar_wait(bar_s, i & 1, aborted);
+  } else {
+    // ---------------- softmax warpgroup: thread <-> row <-> TMEM lane ----------------
+    const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;            // row of the tile
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int64_t my_tok = tok0 + r / G;
+    const bool row_valid = my_tok < tok_end;
+    const int my_kv_end = row_valid ? start + (int)my_tok + 1 : 0;
+    const int cta_min_kv_end = start + (int)tok0 + 1;
+    const float scale = a.scale_log2;
+    float m_ref = -INFINITY, l_run = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const int st = i & 1;
+      const int j0 = (t_begin + i) * kTcKv;
+      const bool full = j0 + kTcKv <= cta_min_kv_end;
+      const int lim = my_kv_end - j0;
+      mbar_wait(&s_full[st], (i >> 1) & 1, aborted);
+      tc_fence_after();
+      const uint32_t s_addr = tmem + st * kTcKv + lane_base;
+      // pass 1: row maximum (four independent accumulators)
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float sv[32];
+        tmem_ld32(s_addr + c * 32, sv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float x = (full || c * 32 + e < lim) ? sv[e] : -INFINITY;
+          mx[e & 3] = fmaxf(mx[e & 3], x);
+        }
+      }
+      const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
+      const float m_new = fmaxf(m_ref, tile_max);
+      const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
+      if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access
+        mbar_wait(o_done, (i - 1) & 1, aborted);  // PV(i-1) finished writing O
+        tc_fence_after();
+        const float alpha = need ? fast_exp2(m_ref - m_new) : 1.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tmem + kTmemO + lane_base + c * 32, ov);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+          tmem_st32(tmem + kTmemO + lane_base + c * 32, ov);
+        }
+      }
+      if (need) {
+        l_run *= fast_exp2(m_ref - m_new);
+        m_ref = m_new;
+      } else if (m_ref == -INFINITY) {
+        m_ref = m_new;
+      }
+      // pass 2: p = 2^(s*scale - m), row sum, P (16-bit) into the tile's dead K buffer
+      const bool live = m_ref != -INFINITY;
+      const float neg_m = -m_ref;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      uint8_t* p_tile = smem + kOffK + st * kKvBytes;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float sv[32];
+        tmem_ld32(s_addr + c * 32, sv);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k0 = c * 32 + u * 8 + 2 * e;
+            const float p0 = (live && (full || k0 < lim)) ? fast_exp2(fmaf(sv[u * 8 + 2 * e], scale, neg_m)) : 0.f;
+            const float p1 = (live && (full || k0 + 1 < lim)) ? fast_exp2(fmaf(sv[u * 8 + 2 * e + 1], scale, neg_m)) : 0.f;
+            ps[e] += p0 + p1;
+            w[e] = pack2<T>(p0, p1);
+          }
+          *reinterpret_cast<uint4*>(p_tile + sw128_offset((uint32_t)r, (uint32_t)(c * 4 + u), kQRegion)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      fence_async_smem();  // P (generic writes) before the tensor core reads it
+      tc_fence_before();   // our tcgen05.ld of S / st of O before the next MMAs
+      mbar_arrive(&p_full[st]);
+    }
+    // ---- epilogue ----
+    mbar_wait(o_final, 0, aborted);
     tc_fence_after();
-    // ---- online softmax of this row: pass 1 (row max), pass 2 (exp, sum, P) over TMEM ----
-    const int j0 = t * kTcKv;
-    const bool full = j0 + kTcKv <= cta_min_kv_end;  // no valid row masks anything in this tile
-    const int lim = my_kv_end - j0;                  // keys j0 + c < my_kv_end are visible
-    float tile_max = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      float sv[32];
-      tmem_ld32(tmem_s + lane_base + c * 32, sv);
-      if (full) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) tile_max = fmaxf(tile_max, sv[e]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (c * 32 + e < lim) tile_max = fmaxf(tile_max, sv[e]);
-      }
-    }
-    tile_max *= scale;  // scale > 0 commutes with max
-    const float m_new = fmaxf(m_ref, tile_max);
-    // tcgen05.ld/st are warp-collective: the warp rescales together if any of its rows must.
-    const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
-    if (__any_sync(0xffffffffu, need)) {
-      const float alpha = need ? exp2f(m_ref - m_new) : 1.f;
+    if (n_splits == 1) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      T* dst = out + (b * a.padded_len + first + my_tok) * row_elems + (int64_t)(h * G + r % G) * kTcDim;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float ov[32];
-        tmem_ld32(tmem_o + lane_base + c * 32, ov);
+        tmem_ld32(tmem + kTmemO + lane_base + c * 32, ov);
+        if (row_valid) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-        tmem_st32(tmem_o + lane_base + c * 32, ov);
-      }
-    }
-    if (need) {
-      l_run *= exp2f(m_ref - m_new);
-      m_ref = m_new;
-    } else if (m_ref == -INFINITY) {
-      m_ref = m_new;
-    }
-    const bool live = m_ref != -INFINITY;
-    const float neg_m = -m_ref;
-    float psum = 0.f;
-    uint8_t* p_tile = smem + kOffK + buf * kKvBytes;  // K of this tile is dead: P goes there
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      float sv[32];
-      tmem_ld32(tmem_s + lane_base + c * 32, sv);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {  // 4 units of 8 columns per 32-column chunk
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int k0 = c * 32 + u * 8 + 2 * e;
-          const bool v0 = live && (full || k0 < lim);
-          const bool v1 = live && (full || k0 + 1 < lim);
-          const float p0 = v0 ? exp2f(fmaf(sv[u * 8 + 2 * e], scale, neg_m)) : 0.f;
-          const float p1 = v1 ? exp2f(fmaf(sv[u * 8 + 2 * e + 1], scale, neg_m)) : 0.f;
-          psum += p0 + p1;
-          w[e] = pack2<T>(p0, p1);
+          for (int u = 0; u < 4; ++u) {
+            uint4 pk;
+            pk.x = pack2<T>(ov[u * 8 + 0] * inv, ov[u * 8 + 1] * inv);
+            pk.y = pack2<T>(ov[u * 8 + 2] * inv, ov[u * 8 + 3] * inv);
+            pk.z = pack2<T>(ov[u * 8 + 4] * inv, ov[u * 8 + 5] * inv);
+            pk.w = pack2<T>(ov[u * 8 + 6] * inv, ov[u * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pk;
+          }
         }
-        // P: 128 rows x 64 columns = one 16 KiB region of 128-byte rows
-        *reinterpret_cast<uint4*>(p_tile + sw128_offset((uint32_t)r, (uint32_t)(c * 4 + u), kQRegion)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
       }
+    } else {
+      const int64_t part = ((b * a.hkv + h) * gridDim.x + blockIdx.x);
+      float* po = ws_o + (part * kTcRows + r) * kTcDim;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float ov[32];
+        tmem_ld32(tmem + kTmemO + lane_base + c * 32, ov);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(po + c * 32 + u * 4) = make_float4(ov[u * 4], ov[u * 4 + 1], ov[u * 4 + 2], ov[u * 4 + 3]);
+      }
+      *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_run);
     }
-    l_run += psum;
     tc_fence_before();
-    fence_async_smem();
-    __syncthreads();
-    // ---- O += P V ----
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int s = 0; s < kTcKv / 16; ++s) {
-        umma_f16(tmem_o, desc_kmajor(kbuf + s * 32), desc_mnmajor(vbuf + s * 2048), idesc_pv,
-                 (i > 0 || s > 0) ? 1u : 0u);
-      }
-      umma_commit(bar_o);
-    }
   }
-  mbar_wait(bar_o, (t_end - t_begin - 1) & 1, aborted);
-  tc_fence_after();
-  // ---- epilogue ----
-  if (n_splits == 1) {
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    T* dst = out + (b * a.padded_len + first + my_tok) * row_elems + (int64_t)(h * G + r % G) * kTcDim;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float ov[32];
-      tmem_ld32(tmem_o + lane_base + c * 32, ov);
-      if (row_valid) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint4 pk;
-          pk.x = pack2<T>(ov[u * 8 + 0] * inv, ov[u * 8 + 1] * inv);
-          pk.y = pack2<T>(ov[u * 8 + 2] * inv, ov[u * 8 + 3] * inv);
-          pk.z = pack2<T>(ov[u * 8 + 4] * inv, ov[u * 8 + 5] * inv);
-          pk.w = pack2<T>(ov[u * 8 + 6] * inv, ov[u * 8 + 7] * inv);
-          *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pk;
-        }
-      }
-    }
-  } else {
-    // unnormalised partial of this split: O row (fp32), m and l
-    const int64_t part = ((b * a.hkv + h) * gridDim.x + blockIdx.x);
-    float* po = ws_o + (part * kTcRows + r) * kTcDim;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float ov[32];
-      tmem_ld32(tmem_o + lane_base + c * 32, ov);
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        *reinterpret_cast<float4*>(po + c * 32 + u * 4) = make_float4(ov[u * 4], ov[u * 4 + 1], ov[u * 4 + 2], ov[u * 4 + 3]);
-    }
-    *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_run);
-  }
-  tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
