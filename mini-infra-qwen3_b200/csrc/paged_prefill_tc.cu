@@ -57,7 +57,8 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;              // two buffers
 constexpr int kOffV = kOffK + 2 * kKvBytes;         // two buffers
 constexpr int kOffBar = kOffV + 2 * kKvBytes;
-constexpr int kTcSmemBytes = kOffBar + 128 + 1024;  // barriers + TMEM slot + alignment slack (~97 KiB)
+constexpr int kOffPages = kOffBar + 128;             // 65 block ids of the tile being loaded
+constexpr int kTcSmemBytes = kOffPages + 65 * 8 + 1024;  // + alignment slack (~98 KiB)
 constexpr uint32_t kTmemCols = 256;                 // S tiles: [0, 64) and [64, 128); O: [128, 256)
 constexpr uint32_t kTmemO = 128;
 constexpr float kRescaleLog2 = 8.0f;
@@ -149,28 +150,41 @@ struct BlockAddr {
   }
 };
 
-// Stage one 64-position KV tile (K and V) of KV head h, positions [j0, j0 + 64), by `nthreads`
-// threads (thread `ti`): 16 threads cover one 256-byte row, 16-byte unit (ti % 16) each.
+// Stage one 64-position KV tile (K and V) of KV head h, positions [j0, j0 + 64), by the 32 loader
+// threads.  First the block ids of every page the tile's history rows touch (at most 64) are read
+// once, coalesced, into `pages` (shared memory); then 16 threads cover one 256-byte row (16-byte
+// unit lane % 16 each), two rows per pass: history rows address the pool through `pages`, chunk
+// rows are consecutive rows of the chunk tensor, rows past the causal end are zero-filled.
 template <typename T>
 __device__ __forceinline__ void stage_kv(const PrefillArgs& a, const BlockAddr& ba, int64_t b, int h, int start,
-                                         int kv_end, int64_t first, int j0, uint32_t k_dst, uint32_t v_dst, int ti,
-                                         int nthreads) {
-  const int unit = ti & 15;
-  const int64_t* table = a.block_tables + b * a.table_stride;
+                                         int kv_end, int64_t first, int j0, uint32_t k_dst, uint32_t v_dst,
+                                         int lane, int64_t* pages) {
+  const int unit = lane & 15;
+  const int hist_rows = max(0, min(kTcKv, start - j0));
+  if (hist_rows > 0) {
+    uint32_t p0, off0, p1, off1;
+    ba.split((uint32_t)j0, p0, off0);
+    ba.split((uint32_t)(j0 + hist_rows - 1), p1, off1);
+    const int64_t* table = a.block_tables + b * a.table_stride;
+    for (int k = lane; k <= (int)(p1 - p0); k += 32) pages[k] = table[p0 + k];
+    __syncwarp();
+  }
   const char* kc = a.k_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
   const char* vc = a.v_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
   const int64_t pool_row = (int64_t)a.hkv * kTcDim * sizeof(T);
   const int64_t head_off = (int64_t)h * kTcDim * sizeof(T) + unit * 16;
+  uint32_t pbase, poff;
+  ba.split((uint32_t)j0, pbase, poff);
 #pragma unroll 4
-  for (int rr = ti >> 4; rr < kTcKv; rr += nthreads / 16) {
+  for (int rr = lane >> 4; rr < kTcKv; rr += 2) {
     const int j = j0 + rr;
     const char* ksrc = a.k_chunk;  // any valid address when zero-filling
     const char* vsrc = a.k_chunk;
     bool valid = j < kv_end;
-    if (valid && j < start) {
+    if (rr < hist_rows) {
       uint32_t bi, off;
       ba.split((uint32_t)j, bi, off);
-      const int64_t blk = table[bi];
+      const int64_t blk = pages[bi - pbase];
       if (blk < 0 || blk >= a.num_blocks) {
         if (unit == 0) record_status(MI_STATUS_BAD_BLOCK);
         valid = false;
@@ -188,6 +202,7 @@ __device__ __forceinline__ void stage_kv(const PrefillArgs& a, const BlockAddr& 
     cp_async16(k_dst + o, ksrc, valid);
     cp_async16(v_dst + o, vsrc, valid);
   }
+  __syncwarp();  // `pages` is rewritten for the next tile
 }
 
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
@@ -242,6 +257,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   uint64_t* o_done = bars + 9;    // MMA -> softmax: one phase per PV (rescale waits)
   uint64_t* o_final = bars + 10;  // MMA -> softmax: the last PV is done (epilogue)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // loader: block ids of one KV tile
 
   const int qtile = blockIdx.x / max_splits;
   const int split = blockIdx.x % max_splits;
@@ -316,7 +332,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       const int st = i & 1;
       if (i >= 2) mbar_wait(&kv_empty[st], ((i - 2) >> 1) & 1, aborted);
       stage_kv<T>(a, ba, b, h, start, kv_end, first, (t_begin + i) * kTcKv, sbase + kOffK + st * kKvBytes,
-                  sbase + kOffV + st * kKvBytes, lane, kLoaderThreads);
+                  sbase + kOffV + st * kKvBytes, lane, pages);
       cp_async_arrive_noinc(&kv_full[st]);
     }
   } else if (warp == kMmaWarp) {

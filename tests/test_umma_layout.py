@@ -105,6 +105,6 @@ def test_pv_operands_read_what_the_writer_stored():
 
 
 def test_smem_budget_two_ctas_per_sm():
-    per_cta = 2 * Q_REGION + 2 * (2 * KV_REGION) + 2 * (2 * KV_REGION) + 64 + 1024
+    per_cta = 2 * Q_REGION + 2 * (2 * KV_REGION) + 2 * (2 * KV_REGION) + 128 + 65 * 8 + 1024  # + barriers, page ids
     assert per_cta <= 227 * 1024
     assert 2 * (per_cta + 1024) <= 228 * 1024  # two CTAs (+1 KiB reserved each) share an SM
