@@ -94,6 +94,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of an mbarrier phase (for loops that poll several barriers).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Deadline for one wait.  A correct kernel never comes near it; a wrong one records
 // MI_STATUS_TIMEOUT and continues (results are then garbage, the status word says so).
 constexpr uint64_t kWaitLimitNs = 200ull * 1000ull * 1000ull;  // 200 ms

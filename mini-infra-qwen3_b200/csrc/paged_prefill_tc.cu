@@ -109,6 +109,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// tcgen05.ld of 32 columns without the wait: issue several, then one tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
@@ -344,7 +357,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       const uint32_t q0 = sbase + kOffQ;
       auto issue_s = [&](int i) {
         const int st = i & 1;
-        mbar_wait(&kv_full[st], (i >> 1) & 1, aborted);
         fence_async_smem();
         tc_fence_after();
         const uint32_t kb = sbase + kOffK + st * kKvBytes;
@@ -354,12 +366,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
                    desc_kmajor(kb + (s >> 2) * kKvRegion + (s & 3) * 32), idesc_qk, s > 0 ? 1u : 0u);
         umma_commit(&s_full[st]);
       };
-      mbar_wait(q_full, 0, aborted);
-      issue_s(0);
-      for (int i = 0; i < n; ++i) {
+      auto issue_pv = [&](int i) {
         const int st = i & 1;
-        if (i + 1 < n) issue_s(i + 1);  // its S buffer was consumed by softmax(i-1) (waited below last round)
-        mbar_wait(&p_full[st], (i >> 1) & 1, aborted);  // P(i) written, S(i) consumed
         fence_async_smem();
         tc_fence_after();
         const uint32_t kb = sbase + kOffK + st * kKvBytes;  // holds P(i)
@@ -370,6 +378,32 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
                    (i > 0 || s > 0) ? 1u : 0u);
         umma_commit(&kv_empty[st]);
         umma_commit(o_done);
+      };
+      mbar_wait(q_full, 0, aborted);
+      // Issue S(ns) as soon as its tile has landed and its TMEM buffer is free (softmax(ns-2) done,
+      // i.e. ns <= npv + 1), and PV(npv) as soon as P(npv) is written; whichever is ready first.
+      int ns = 0, npv = 0;
+      uint64_t t_last = globaltimer_ns();
+      while (npv < n) {
+        bool progressed = false;
+        if (ns < n && ns <= npv + 1 && mbar_test_wait(&kv_full[ns & 1], (ns >> 1) & 1)) {
+          issue_s(ns++);
+          progressed = true;
+        }
+        if (npv < ns && mbar_test_wait(&p_full[npv & 1], (npv >> 1) & 1)) {
+          issue_pv(npv++);
+          progressed = true;
+        }
+        if (progressed) {
+          t_last = globaltimer_ns();
+        } else if (!aborted && globaltimer_ns() - t_last > kWaitLimitNs) {
+          record_status(MI_STATUS_TIMEOUT);
+          aborted = true;
+        }
+        if (aborted && !progressed) {  // give up: let the other roles time out and finish
+          if (ns < n && ns <= npv + 1) issue_s(ns++);
+          else issue_pv(npv++);
+        }
       }
       umma_commit(o_final);
     }
@@ -392,15 +426,18 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       mbar_wait(&s_full[st], (i >> 1) & 1, aborted);
       tc_fence_after();
       const uint32_t s_addr = tmem + st * kTcKv + lane_base;
+      // the whole 64-column S row in registers: two loads, one wait
+      uint32_t sr[2][32];
+      tmem_ld32_async(s_addr, sr[0]);
+      tmem_ld32_async(s_addr + 32, sr[1]);
+      tmem_wait_ld();
       // pass 1: row maximum (four independent accumulators)
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        float sv[32];
-        tmem_ld32(s_addr + c * 32, sv);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float x = (full || c * 32 + e < lim) ? sv[e] : -INFINITY;
+          const float x = (full || c * 32 + e < lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
           mx[e & 3] = fmaxf(mx[e & 3], x);
         }
       }
@@ -433,16 +470,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       uint8_t* p_tile = smem + kOffK + st * kKvBytes;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        float sv[32];
-        tmem_ld32(s_addr + c * 32, sv);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int k0 = c * 32 + u * 8 + 2 * e;
-            const float p0 = (live && (full || k0 < lim)) ? fast_exp2(fmaf(sv[u * 8 + 2 * e], scale, neg_m)) : 0.f;
-            const float p1 = (live && (full || k0 + 1 < lim)) ? fast_exp2(fmaf(sv[u * 8 + 2 * e + 1], scale, neg_m)) : 0.f;
+            const float s0 = __uint_as_float(sr[c][u * 8 + 2 * e]), s1 = __uint_as_float(sr[c][u * 8 + 2 * e + 1]);
+            const float p0 = (live && (full || k0 < lim)) ? fast_exp2(fmaf(s0, scale, neg_m)) : 0.f;
+            const float p1 = (live && (full || k0 + 1 < lim)) ? fast_exp2(fmaf(s1, scale, neg_m)) : 0.f;
             ps[e] += p0 + p1;
             w[e] = pack2<T>(p0, p1);
           }
