@@ -114,6 +114,44 @@ int pool_tensor_map(const void* pool, int64_t num_blocks, int bs, int hkv, int d
   return MI_OK;
 }
 
+// Tiled, 128-byte-swizzled tensor map of a 16-bit tensor (cached by every encoding argument).
+std::unordered_map<std::string, CUtensorMap> g_generic_maps;
+
+bool encode_map(const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                int dtype, CUtensorMap* out) {
+  std::string key(reinterpret_cast<const char*>(&base), sizeof(base));
+  key.append(reinterpret_cast<const char*>(&rank), sizeof(rank));
+  key.append(reinterpret_cast<const char*>(dims), sizeof(cuuint64_t) * rank);
+  key.append(reinterpret_cast<const char*>(strides), sizeof(cuuint64_t) * (rank - 1));
+  key.append(reinterpret_cast<const char*>(box), sizeof(cuuint32_t) * rank);
+  key.append(reinterpret_cast<const char*>(&dtype), sizeof(dtype));
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    auto it = g_generic_maps.find(key);
+    if (it != g_generic_maps.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapDataType ty =
+      dtype == MI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap m;
+  if (fn(&m, ty, rank, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+      CUDA_SUCCESS)
+    return false;
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    if (g_generic_maps.size() > 4096) g_generic_maps.clear();
+    g_generic_maps[key] = m;
+  }
+  *out = m;
+  return true;
+}
+
 int check_pool_geometry(int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, int dtype) {
   if (elem_size(dtype) == 0) return fail(MI_ERR_INVALID, "unknown dtype %d", dtype);
   if (num_blocks < 1 || block_size < 1 || num_kv_heads < 1 || head_dim < 1)
@@ -380,6 +418,8 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
   a.scale_log2 = scale * 1.4426950408889634f;
   a.out = static_cast<char*>(out);
   float* ws = nullptr;
+  mi::PrefillMaps maps;
+  bool use_maps = false;
   if (mi::prefill_tc_supported(a, dtype)) {
     const size_t need = mi::prefill_tc_workspace_bytes(a);
     if (need > 0) {
@@ -388,8 +428,28 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
                     workspace_bytes);
       ws = static_cast<float*>(workspace);
     }
+    // TMA staging when every operand has a tensor map; otherwise the kernel uses cp.async.
+    if (mi::prefill_tc_tma_block_size(block_size) && padded_len < (int64_t(1) << 31)) {
+      const int G = a.groups;
+      const cuuint64_t qd[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)padded_len,
+                                (cuuint64_t)batch};
+      const cuuint64_t qs[3] = {(cuuint64_t)a.q_sb[2], (cuuint64_t)a.q_sb[1], (cuuint64_t)a.q_sb[0]};
+      const cuuint32_t qb[4] = {64, (cuuint32_t)G, (cuuint32_t)(128 / G), 1};
+      const cuuint64_t kd[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_kv_heads, (cuuint64_t)padded_len,
+                                (cuuint64_t)batch};
+      const cuuint64_t ks[3] = {(cuuint64_t)a.kv_sb[2], (cuuint64_t)a.kv_sb[1], (cuuint64_t)a.kv_sb[0]};
+      const cuuint32_t kb[4] = {64, 1, 64, 1};
+      use_maps = encode_map(q, 4, qd, qs, qb, dtype, &maps.q) && encode_map(k_chunk, 4, kd, ks, kb, dtype, &maps.k_chunk) &&
+                 encode_map(v_chunk, 4, kd, ks, kb, dtype, &maps.v_chunk);
+      if (use_maps && table_stride > 0) {
+        use_maps = pool_tensor_map(k_pool, num_blocks, block_size, num_kv_heads, head_dim, dtype, &maps.k_pool) ==
+                       MI_OK &&
+                   pool_tensor_map(v_pool, num_blocks, block_size, num_kv_heads, head_dim, dtype, &maps.v_pool) ==
+                       MI_OK;
+      }
+    }
   }
-  cudaError_t e = mi::launch_paged_prefill(a, ws, dtype, static_cast<cudaStream_t>(stream));
+  cudaError_t e = mi::launch_paged_prefill(a, ws, use_maps ? &maps : nullptr, dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MI_OK : cuda_fail(e, "mi_paged_prefill launch");
 }
 

@@ -125,11 +125,19 @@ struct PrefillArgs {
   char* out;  // [batch, padded_len, hq*head_dim] contiguous
 };
 
-cudaError_t launch_paged_prefill(const PrefillArgs& a, float* ws, int dtype, cudaStream_t s);
+// TMA descriptors of the prefill operands (Q box [64, G, 128/G, 1]; chunk K/V boxes [64, 1, 64, 1];
+// pool boxes [64, 1, block_size]).  With maps == nullptr the kernel stages K/V with cp.async.
+struct PrefillMaps {
+  CUtensorMap q, k_chunk, v_chunk, k_pool, v_pool;
+};
+cudaError_t launch_paged_prefill(const PrefillArgs& a, float* ws, const PrefillMaps* maps, int dtype,
+                                 cudaStream_t s);
 // tcgen05 variant (bf16/fp16, head_dim 128, G in {1,2,4,8}, 16-byte aligned operands); its split-KV
 // partials need prefill_tc_workspace_bytes(a) bytes of workspace (0 when no row tile splits)
 bool prefill_tc_supported(const PrefillArgs& a, int dtype);
 size_t prefill_tc_workspace_bytes(const PrefillArgs& a);
-cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, int dtype, cudaStream_t s);
+bool prefill_tc_tma_block_size(int block_size);
+cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, const PrefillMaps* maps, int dtype,
+                                    cudaStream_t s);
 
 }  // namespace mi

@@ -96,10 +96,11 @@ __global__ void __launch_bounds__(128) prefill_scalar_kernel(const PrefillArgs a
 
 }  // namespace
 
-cudaError_t launch_paged_prefill(const PrefillArgs& a, float* ws, int dtype, cudaStream_t s) {
+cudaError_t launch_paged_prefill(const PrefillArgs& a, float* ws, const PrefillMaps* maps, int dtype,
+                                 cudaStream_t s) {
   const int64_t warps = a.batch * a.padded_len * a.hq;
   if (warps == 0) return cudaSuccess;
-  if (prefill_tc_supported(a, dtype)) return launch_paged_prefill_tc(a, ws, dtype, s);
+  if (prefill_tc_supported(a, dtype)) return launch_paged_prefill_tc(a, ws, maps, dtype, s);
   const unsigned blocks = (unsigned)((warps + 3) / 4);
   switch (dtype) {
     case MI_BF16: prefill_scalar_kernel<__nv_bfloat16><<<blocks, 128, 0, s>>>(a); break;

@@ -163,74 +163,15 @@ struct BlockAddr {
   }
 };
 
-// Stage one 64-position KV tile (K and V) of KV head h, positions [j0, j0 + 64), by the 32 loader
-// threads.  First the block ids of every page the tile's history rows touch (at most 64) are read
-// once, coalesced, into `pages` (shared memory); then 16 threads cover one 256-byte row (16-byte
-// unit lane % 16 each), two rows per pass: history rows address the pool through `pages`, chunk
-// rows are consecutive rows of the chunk tensor, rows past the causal end are zero-filled.
-template <typename T>
-__device__ __forceinline__ void stage_kv(const PrefillArgs& a, const BlockAddr& ba, int64_t b, int h, int start,
-                                         int kv_end, int64_t first, int j0, uint32_t k_dst, uint32_t v_dst,
-                                         int lane, int64_t* pages) {
-  const int unit = lane & 15;
-  const int hist_rows = max(0, min(kTcKv, start - j0));
-  if (hist_rows > 0) {
-    uint32_t p0, off0, p1, off1;
-    ba.split((uint32_t)j0, p0, off0);
-    ba.split((uint32_t)(j0 + hist_rows - 1), p1, off1);
-    const int64_t* table = a.block_tables + b * a.table_stride;
-    for (int k = lane; k <= (int)(p1 - p0); k += 32) pages[k] = table[p0 + k];
-    __syncwarp();
-  }
-  const char* kc = a.k_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
-  const char* vc = a.v_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
-  const int64_t pool_row = (int64_t)a.hkv * kTcDim * sizeof(T);
-  const int64_t head_off = (int64_t)h * kTcDim * sizeof(T) + unit * 16;
-  uint32_t pbase, poff;
-  ba.split((uint32_t)j0, pbase, poff);
-#pragma unroll 4
-  for (int rr = lane >> 4; rr < kTcKv; rr += 2) {
-    const int j = j0 + rr;
-    const char* ksrc = a.k_chunk;  // any valid address when zero-filling
-    const char* vsrc = a.k_chunk;
-    bool valid = j < kv_end;
-    if (rr < hist_rows) {
-      uint32_t bi, off;
-      ba.split((uint32_t)j, bi, off);
-      const int64_t blk = pages[bi - pbase];
-      if (blk < 0 || blk >= a.num_blocks) {
-        if (unit == 0) record_status(MI_STATUS_BAD_BLOCK);
-        valid = false;
-      } else {
-        const int64_t o = (blk * a.block_size + off) * pool_row + head_off;
-        ksrc = a.k_pool + o;
-        vsrc = a.v_pool + o;
-      }
-    } else if (valid) {
-      const int64_t pos = first + (j - start);
-      ksrc = kc + pos * a.kv_sb[1];
-      vsrc = vc + pos * a.kv_sb[1];
-    }
-    const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion);
-    cp_async16(k_dst + o, ksrc, valid);
-    cp_async16(v_dst + o, vsrc, valid);
-  }
-  __syncwarp();  // `pages` is rewritten for the next tile
-}
-
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
+// KV tiles of a row tile: first the history tiles (positions [64k, 64k + 64) of [0, start), read
+// from the pool), then the chunk tiles (chunk tokens [64k, 64k + 64) of [0, tok_end), read from the
+// chunk's own K/V).  Keeping the two apart aligns every tile to its source, so each one is a few
+// whole TMA boxes: pool pages [64 x 1 x block_size] or a [64 x 1 x 64 x 1] chunk box.
 struct TcGeometry {
   int64_t len, first;
   int start;
-  int n_tiles;  // KV tiles of this row tile (causal end of its last token)
+  int hist_tiles;  // ceil(start / 64)
+  int n_tiles;     // history tiles + chunk tiles up to the causal end of the tile's last token
 };
 
 __device__ __forceinline__ TcGeometry tc_geometry(const PrefillArgs& a, int64_t b, int64_t tok0, int tokens_per_tile,
@@ -250,14 +191,84 @@ __device__ __forceinline__ TcGeometry tc_geometry(const PrefillArgs& a, int64_t 
     start = a.table_stride * a.block_size;
   }
   g.start = (int)start;
+  g.hist_tiles = (int)((start + kTcKv - 1) / kTcKv);
   const int64_t tok_end = min(g.len, tok0 + tokens_per_tile);
-  g.n_tiles = tok0 < g.len ? (int)((start + tok_end + kTcKv - 1) / kTcKv) : 0;
+  g.n_tiles = tok0 < g.len ? g.hist_tiles + (int)((tok_end + kTcKv - 1) / kTcKv) : 0;
   return g;
 }
 
+// cp.async staging (block sizes without a TMA box): history tile k = positions [64k, 64k + 64),
+// rows at or past `start` zero-filled; block ids of the tile's pages are read once into `pages`.
 template <typename T>
-__global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const PrefillArgs a, float* ws_o, float* ws_ml,
-                                                                    int max_splits, int shift) {
+__device__ __forceinline__ void stage_hist_cp(const PrefillArgs& a, const BlockAddr& ba, int64_t b, int h, int start,
+                                              int k, uint32_t k_dst, uint32_t v_dst, int lane, int64_t* pages) {
+  const int unit = lane & 15;
+  const int j0 = k * kTcKv;
+  const int hist_rows = max(0, min(kTcKv, start - j0));
+  uint32_t p0, off0, p1, off1;
+  ba.split((uint32_t)j0, p0, off0);
+  ba.split((uint32_t)(j0 + max(hist_rows, 1) - 1), p1, off1);
+  const int64_t* table = a.block_tables + b * a.table_stride;
+  for (int q = lane; q <= (int)(p1 - p0); q += 32) pages[q] = table[p0 + q];
+  __syncwarp();
+  const int64_t pool_row = (int64_t)a.hkv * kTcDim * sizeof(T);
+  const int64_t head_off = (int64_t)h * kTcDim * sizeof(T) + unit * 16;
+#pragma unroll 4
+  for (int rr = lane >> 4; rr < kTcKv; rr += 2) {
+    const char* ksrc = a.k_chunk;  // any valid address when zero-filling
+    const char* vsrc = a.k_chunk;
+    bool valid = rr < hist_rows;
+    if (valid) {
+      uint32_t bi, off;
+      ba.split((uint32_t)(j0 + rr), bi, off);
+      const int64_t blk = pages[bi - p0];
+      if (blk < 0 || blk >= a.num_blocks) {
+        if (unit == 0) record_status(MI_STATUS_BAD_BLOCK);
+        valid = false;
+      } else {
+        const int64_t o = (blk * a.block_size + off) * pool_row + head_off;
+        ksrc = a.k_pool + o;
+        vsrc = a.v_pool + o;
+      }
+    }
+    const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion);
+    cp_async16(k_dst + o, ksrc, valid);
+    cp_async16(v_dst + o, vsrc, valid);
+  }
+  __syncwarp();  // `pages` is rewritten for the next tile
+}
+
+// cp.async staging of chunk tile k = chunk tokens [64k, 64k + 64); rows at or past `rows_end` zero.
+__device__ __forceinline__ void stage_chunk_cp(const PrefillArgs& a, int64_t b, int h, int64_t first, int k,
+                                               int rows_end, uint32_t k_dst, uint32_t v_dst, int lane) {
+  const int unit = lane & 15;
+  const char* kc = a.k_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
+  const char* vc = a.v_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
+#pragma unroll 4
+  for (int rr = lane >> 4; rr < kTcKv; rr += 2) {
+    const int jc = k * kTcKv + rr;
+    const bool valid = jc < rows_end;
+    const int64_t pos = first + jc;
+    const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion);
+    cp_async16(k_dst + o, valid ? kc + pos * a.kv_sb[1] : a.k_chunk, valid);
+    cp_async16(v_dst + o, valid ? vc + pos * a.kv_sb[1] : a.k_chunk, valid);
+  }
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T, bool kTma>
+__global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const PrefillArgs a,
+                                                                    const __grid_constant__ PrefillMaps maps,
+                                                                    float* ws_o, float* ws_ml, int max_splits,
+                                                                    int shift) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -270,7 +281,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   uint64_t* o_done = bars + 9;    // MMA -> softmax: one phase per PV (rescale waits)
   uint64_t* o_final = bars + 10;  // MMA -> softmax: the last PV is done (epilogue)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
-  int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // loader: block ids of one KV tile
+  int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async loader: block ids of one tile
 
   const int qtile = blockIdx.x / max_splits;
   const int split = blockIdx.x % max_splits;
@@ -304,12 +315,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   const int n = t_end - t_begin;
   const int n_splits = (geo.n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
   const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
-  const int kv_end = start + (int)tok_end;  // causal end of the tile's last token
+  const int hist_tiles = geo.hist_tiles;
 
   if (tid == 0) {
-    mbar_init(q_full, kLoaderThreads);
+    mbar_init(q_full, kTma ? 1 : kLoaderThreads);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], kLoaderThreads);
+      mbar_init(&kv_full[i], kTma ? 1 : kLoaderThreads);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kSoftmaxThreads);
@@ -331,25 +342,72 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
 
   if (warp == kLoaderWarp) {
     // ---------------- loader: Q once, then K/V tiles into a 2-stage ring ----------------
-    const BlockAddr ba{shift, (uint32_t)a.block_size};
-    const int unit = lane & 15;
-    for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
-      const int64_t tok = tok0 + r / G;
-      const bool valid = tok < tok_end;
-      const char* src = a.q;
-      if (valid) src = a.q + b * a.q_sb[0] + (first + tok) * a.q_sb[1] + (int64_t)(h * G + r % G) * a.q_sb[2] + unit * 16;
-      cp_async16(sbase + kOffQ + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
-    }
-    cp_async_arrive_noinc(q_full);
-    for (int i = 0; i < n; ++i) {
-      const int st = i & 1;
-      if (i >= 2) mbar_wait(&kv_empty[st], ((i - 2) >> 1) & 1, aborted);
-      stage_kv<T>(a, ba, b, h, start, kv_end, first, (t_begin + i) * kTcKv, sbase + kOffK + st * kKvBytes,
-                  sbase + kOffV + st * kKvBytes, lane, pages);
-      cp_async_arrive_noinc(&kv_full[st]);
+    if constexpr (kTma) {
+      if (lane == 0) {
+        tma_prefetch_desc(&maps.q);
+        tma_prefetch_desc(&maps.k_chunk);
+        tma_prefetch_desc(&maps.v_chunk);
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        for (int c = 0; c < 2; ++c)  // box [64 d, G heads, 128/G tokens]: row = token * G + head
+          tma_load_4d(smem + kOffQ + c * kQRegion, &maps.q, q_full, c * 64, h * G, (int)(first + tok0), (int)b);
+        const int64_t* table = a.block_tables + b * a.table_stride;
+        const int pages_per_tile = kTcKv / a.block_size;
+        const int page_bytes = a.block_size * 128;
+        const int num_slots = (int)(a.num_blocks * a.block_size);
+        for (int i = 0; i < n; ++i) {
+          const int st = i & 1;
+          if (i >= 2) mbar_wait(&kv_empty[st], ((i - 2) >> 1) & 1, aborted);
+          uint8_t* kd = smem + kOffK + st * kKvBytes;
+          uint8_t* vd = smem + kOffV + st * kKvBytes;
+          mbar_arrive_expect_tx(&kv_full[st], 2 * kKvBytes);
+          const int t = t_begin + i;
+          if (t < hist_tiles) {
+            for (int pg = 0; pg < pages_per_tile; ++pg) {
+              const int pos0 = t * kTcKv + pg * a.block_size;
+              int row0 = num_slots;  // past the tensor: TMA fills zeros
+              if (pos0 < start) {
+                const int64_t blk = table[pos0 >> shift];
+                if (blk < 0 || blk >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
+                else row0 = (int)(blk * a.block_size);
+              }
+              for (int c = 0; c < 2; ++c) {
+                tma_load_3d(kd + c * kKvRegion + pg * page_bytes, &maps.k_pool, &kv_full[st], c * 64, h, row0);
+                tma_load_3d(vd + c * kKvRegion + pg * page_bytes, &maps.v_pool, &kv_full[st], c * 64, h, row0);
+              }
+            }
+          } else {
+            const int pos = (int)first + (t - hist_tiles) * kTcKv;
+            for (int c = 0; c < 2; ++c) {
+              tma_load_4d(kd + c * kKvRegion, &maps.k_chunk, &kv_full[st], c * 64, h, pos, (int)b);
+              tma_load_4d(vd + c * kKvRegion, &maps.v_chunk, &kv_full[st], c * 64, h, pos, (int)b);
+            }
+          }
+        }
+      }
+    } else {
+      const BlockAddr ba{shift, (uint32_t)a.block_size};
+      const int unit = lane & 15;
+      for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
+        const int64_t tok = tok0 + r / G;
+        const bool valid = tok < tok_end;
+        const char* src = a.q;
+        if (valid)
+          src = a.q + b * a.q_sb[0] + (first + tok) * a.q_sb[1] + (int64_t)(h * G + r % G) * a.q_sb[2] + unit * 16;
+        cp_async16(sbase + kOffQ + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
+      }
+      cp_async_arrive_noinc(q_full);
+      for (int i = 0; i < n; ++i) {
+        const int st = i & 1;
+        if (i >= 2) mbar_wait(&kv_empty[st], ((i - 2) >> 1) & 1, aborted);
+        const int t = t_begin + i;
+        const uint32_t kd = sbase + kOffK + st * kKvBytes, vd = sbase + kOffV + st * kKvBytes;
+        if (t < hist_tiles) stage_hist_cp<T>(a, ba, b, h, start, t, kd, vd, lane, pages);
+        else stage_chunk_cp(a, b, h, first, t - hist_tiles, (int)tok_end, kd, vd, lane);
+        cp_async_arrive_noinc(&kv_full[st]);
+      }
     }
   } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer: S(i+1) overlaps softmax(i); PV(i) after P(i) ----------------
+    // ---------------- MMA issuer: S and PV in readiness order ----------------
     if (lane == 0) {
       constexpr bool kBf16 = !std::is_same<T, __half>::value;
       const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
@@ -380,8 +438,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
         umma_commit(o_done);
       };
       mbar_wait(q_full, 0, aborted);
-      // Issue S(ns) as soon as its tile has landed and its TMEM buffer is free (softmax(ns-2) done,
-      // i.e. ns <= npv + 1), and PV(npv) as soon as P(npv) is written; whichever is ready first.
+      // S(ns) as soon as its tile landed and its TMEM buffer is free (softmax(ns-2) done, i.e.
+      // ns <= npv + 1); PV(npv) as soon as P(npv) is written; whichever is ready first.
       int ns = 0, npv = 0;
       uint64_t t_last = globaltimer_ns();
       while (npv < n) {
@@ -414,24 +472,29 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const int64_t my_tok = tok0 + r / G;
     const bool row_valid = my_tok < tok_end;
-    const int my_kv_end = row_valid ? start + (int)my_tok + 1 : 0;
-    const int cta_min_kv_end = start + (int)tok0 + 1;
     const float scale = a.scale_log2;
     float m_ref = -INFINITY, l_run = 0.f;
     for (int i = 0; i < n; ++i) {
       const int st = i & 1;
-      const int j0 = (t_begin + i) * kTcKv;
-      const bool full = j0 + kTcKv <= cta_min_kv_end;
-      const int lim = my_kv_end - j0;
+      const int t = t_begin + i;
+      // visible columns of this tile: history keys below `start`; chunk keys up to the row's token
+      bool full;
+      int lim;
+      if (t < hist_tiles) {
+        lim = row_valid ? start - t * kTcKv : 0;
+        full = (t + 1) * kTcKv <= start;
+      } else {
+        const int k0 = (t - hist_tiles) * kTcKv;
+        lim = row_valid ? (int)my_tok + 1 - k0 : 0;
+        full = k0 + kTcKv <= (int)tok0 + 1;
+      }
       mbar_wait(&s_full[st], (i >> 1) & 1, aborted);
       tc_fence_after();
       const uint32_t s_addr = tmem + st * kTcKv + lane_base;
-      // the whole 64-column S row in registers: two loads, one wait
       uint32_t sr[2][32];
       tmem_ld32_async(s_addr, sr[0]);
       tmem_ld32_async(s_addr + 32, sr[1]);
       tmem_wait_ld();
-      // pass 1: row maximum (four independent accumulators)
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -463,7 +526,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       } else if (m_ref == -INFINITY) {
         m_ref = m_new;
       }
-      // pass 2: p = 2^(s*scale - m), row sum, P (16-bit) into the tile's dead K buffer
       const bool live = m_ref != -INFINITY;
       const float neg_m = -m_ref;
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
@@ -593,8 +655,7 @@ TcPlan tc_plan(const PrefillArgs& a) {
   TcPlan p;
   const int tokens_per_tile = kTcRows / a.groups;
   p.qtiles = (a.padded_len + tokens_per_tile - 1) / tokens_per_tile;
-  const int64_t max_kv = a.table_stride * a.block_size + a.padded_len;
-  const int64_t max_tiles = (max_kv + kTcKv - 1) / kTcKv;
+  const int64_t max_tiles = (a.table_stride * a.block_size + kTcKv - 1) / kTcKv + (a.padded_len + kTcKv - 1) / kTcKv;
   p.max_splits = (int)std::max<int64_t>(1, (max_tiles + kTilesPerSplit - 1) / kTilesPerSplit);
   const int64_t parts = p.max_splits > 1 ? a.batch * a.hkv * p.qtiles * p.max_splits : 0;
   p.ws_o_bytes = (size_t)parts * kTcRows * kTcDim * sizeof(float);
@@ -609,9 +670,9 @@ int log2_if_pow2(int x) {
   return s;
 }
 
-template <typename T>
-cudaError_t launch_tc(const PrefillArgs& a, float* ws, cudaStream_t s) {
-  auto kern = prefill_tc_kernel<T>;
+template <typename T, bool kTma>
+cudaError_t launch_tc(const PrefillArgs& a, float* ws, const PrefillMaps& maps, cudaStream_t s) {
+  auto kern = prefill_tc_kernel<T, kTma>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
   if (e != cudaSuccess) return e;
   const TcPlan p = tc_plan(a);
@@ -619,7 +680,7 @@ cudaError_t launch_tc(const PrefillArgs& a, float* ws, cudaStream_t s) {
   float* ws_ml = ws ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ((p.ws_o_bytes + 255) & ~size_t(255)))
                     : nullptr;
   dim3 grid((unsigned)(p.qtiles * p.max_splits), (unsigned)a.hkv, (unsigned)a.batch);
-  kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a, ws_o, ws_ml, p.max_splits, log2_if_pow2(a.block_size));
+  kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, p.max_splits, log2_if_pow2(a.block_size));
   e = cudaGetLastError();
   if (e != cudaSuccess || p.max_splits == 1) return e;
   dim3 cgrid((unsigned)p.qtiles, (unsigned)a.hkv, (unsigned)a.batch);
@@ -649,9 +710,19 @@ bool prefill_tc_supported(const PrefillArgs& a, int dtype) {
   return true;
 }
 
-cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, int dtype, cudaStream_t s) {
-  if (dtype == MI_BF16) return launch_tc<__nv_bfloat16>(a, ws, s);
-  return launch_tc<__half>(a, ws, s);
+bool prefill_tc_tma_block_size(int block_size) {
+  return block_size == 16 || block_size == 32 || block_size == 64;
+}
+
+cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, const PrefillMaps* maps, int dtype,
+                                    cudaStream_t s) {
+  static const PrefillMaps kNoMaps{};
+  if (maps) {
+    if (dtype == MI_BF16) return launch_tc<__nv_bfloat16, true>(a, ws, *maps, s);
+    return launch_tc<__half, true>(a, ws, *maps, s);
+  }
+  if (dtype == MI_BF16) return launch_tc<__nv_bfloat16, false>(a, ws, kNoMaps, s);
+  return launch_tc<__half, false>(a, ws, kNoMaps, s);
 }
 
 }  // namespace mi
