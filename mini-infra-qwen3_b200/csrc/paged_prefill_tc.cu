@@ -1,26 +1,27 @@
 // Chunked-prefill paged attention on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
 // Variant: bf16 / fp16, head_dim 128, any block size, G = Hq/H_kv in {1, 2, 4, 8}.
-// One CTA (128 threads, two CTAs per SM) = one (sequence, KV head, tile of 128 query rows, KV
+// One CTA (192 threads, two CTAs per SM) = one (sequence, KV head, tile of 128 query rows, KV
 // split).  The 128 rows pack 128/G chunk tokens x G query heads of the KV head (row r = token r/G,
 // head r%G), so the K/V tiles staged in shared memory serve the whole GQA group.  The KV range of
-// a row tile (history + causal chunk) is cut into splits of kTilesPerSplit 64-position tiles so
-// that long histories spread over many CTAs; a tile with one split writes its output directly,
-// otherwise each split writes an unnormalised partial (O, m, l) that prefill_combine_kernel merges.
-// Per 64-position KV tile:
-//   1. cp.async stages K and V rows (double-buffered: the next tile streams in during this one):
-//      positions < start come from the pool through the block table, the rest from the chunk's own
-//      K/V; rows past the causal end are zero-filled;
-//   2. one thread issues S = Q K^T as 8 tcgen05.mma (M=128, N=64, K=16, kind::f16, fp32 accum) into
-//      TMEM columns [0, 64); tcgen05.commit signals an mbarrier;
-//   3. each thread owns one row (its TMEM lane): tcgen05.ld of the row (twice: max, then exp),
-//      causal/length mask only on tiles that cross a row's causal end, online softmax in the exp2
-//      domain; the running O in TMEM is rescaled (tcgen05.ld/st, warp-wide) only when a row maximum
-//      grew by more than 2^8 since its last rescale (p <= 2^8 stays exact in fp32 and the final 1/l
-//      absorbs it); P is written as 16-bit values into the now-dead K buffer of this tile, in the
-//      128-byte-swizzled K-major layout;
-//   4. one thread issues O += P V as 4 tcgen05.mma (M=128, N=128, V read MN-major) into TMEM
-//      columns [128, 256).
+// a row tile (history tiles, then causal chunk tiles) is cut into splits of kTilesPerSplit
+// 64-position tiles so that long histories spread over many CTAs; a tile with one split writes its
+// output directly, otherwise each split writes an unnormalised partial (O, m, l) that
+// prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
+//   warp 0 (loader): Q once, then K and V tiles into a 2-stage ring.  With tensor maps (block size
+//      16/32/64) one thread issues TMA copies: one 3D box per pool page of a history tile (a page
+//      past `start` reads rows past the pool, which TMA fills with zeros) and one 4D box per half of
+//      a chunk tile; otherwise the warp stages rows with cp.async through the block table;
+//   warp 1 (MMA, one thread): S = Q K^T as 8 tcgen05.mma (M=128, N=64, K=16, kind::f16, fp32
+//      accumulate) into one of two TMEM S buffers (columns [0, 64) / [64, 128)), and O += P V as 4
+//      tcgen05.mma (M=128, N=128, V read MN-major) into TMEM columns [128, 256), issued in
+//      readiness order so S(i+1) runs under softmax(i); tcgen05.commit signals the mbarriers;
+//   warps 2-5 (softmax): each thread owns one row (its TMEM lane): one tcgen05.ld of the row's 64
+//      scores, causal / length mask (set to -inf) only on tiles that cross a row's causal end or
+//      the history end, online softmax in the exp2 domain; the running O in TMEM is rescaled
+//      (tcgen05.ld/st, warp-wide) only when a row maximum grew by more than 2^8 since its last
+//      rescale (p <= 2^8 stays exact in fp32 and the final 1/l absorbs it); P is written as 16-bit
+//      values into the tile's K buffer (dead once S is done), in the 128-byte-swizzled K-major layout.
 // Epilogue: tcgen05.ld of O, divide by l (or store the partial), 16-byte stores.  Padding
 // positions get zeros.
 //
@@ -495,14 +496,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       tmem_ld32_async(s_addr, sr[0]);
       tmem_ld32_async(s_addr + 32, sr[1]);
       tmem_wait_ld();
+      if (!full) {  // uniform for the CTA: only tiles that cross a causal or history end are masked
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e >= lim) sr[c][e] = 0xff800000u;  // -inf: exp2 gives 0 below
+        }
+      }
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float x = (full || c * 32 + e < lim) ? __uint_as_float(sr[c][e]) : -INFINITY;
-          mx[e & 3] = fmaxf(mx[e & 3], x);
-        }
+        for (int e = 0; e < 32; ++e) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[c][e]));
       }
       const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
       const float m_new = fmaxf(m_ref, tile_max);
@@ -526,8 +532,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       } else if (m_ref == -INFINITY) {
         m_ref = m_new;
       }
-      const bool live = m_ref != -INFINITY;
-      const float neg_m = -m_ref;
+      const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;  // a row with nothing visible yet: all -inf
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
       uint8_t* p_tile = smem + kOffK + st * kKvBytes;
 #pragma unroll
@@ -537,10 +542,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int k0 = c * 32 + u * 8 + 2 * e;
-            const float s0 = __uint_as_float(sr[c][u * 8 + 2 * e]), s1 = __uint_as_float(sr[c][u * 8 + 2 * e + 1]);
-            const float p0 = (live && (full || k0 < lim)) ? fast_exp2(fmaf(s0, scale, neg_m)) : 0.f;
-            const float p1 = (live && (full || k0 + 1 < lim)) ? fast_exp2(fmaf(s1, scale, neg_m)) : 0.f;
+            // branch-free: every exponent is independent, so the ex2 issue overlaps
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][u * 8 + 2 * e]), scale, neg_m));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][u * 8 + 2 * e + 1]), scale, neg_m));
             ps[e] += p0 + p1;
             w[e] = pack2<T>(p0, p1);
           }
