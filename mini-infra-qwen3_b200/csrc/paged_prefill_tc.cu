@@ -8,20 +8,21 @@
 // 64-position tiles so that long histories spread over many CTAs; a tile with one split writes its
 // output directly, otherwise each split writes an unnormalised partial (O, m, l) that
 // prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
-//   warp 0 (loader): Q once, then K and V tiles into a 2-stage ring.  With tensor maps (block size
-//      16/32/64) one thread issues TMA copies: one 3D box per pool page of a history tile (a page
-//      past `start` reads rows past the pool, which TMA fills with zeros) and one 4D box per half of
-//      a chunk tile; otherwise the warp stages rows with cp.async through the block table;
+//   warp 0 (loader): Q once, then K and V tiles into two 2-stage rings (K is free once S is done,
+//      V once PV is done).  With tensor maps (block size 16/32/64) the split's block ids are first
+//      resolved into shared memory, then one thread issues TMA copies: one 3D box per pool page of a
+//      history tile (a page past `start` reads rows past the pool, which TMA fills with zeros) and
+//      one 4D box per half of a chunk tile; otherwise the warp stages rows with cp.async;
 //   warp 1 (MMA, one thread): S = Q K^T as 8 tcgen05.mma (M=128, N=64, K=16, kind::f16, fp32
 //      accumulate) into one of two TMEM S buffers (columns [0, 64) / [64, 128)), and O += P V as 4
-//      tcgen05.mma (M=128, N=128, V read MN-major) into TMEM columns [128, 256), issued in
-//      readiness order so S(i+1) runs under softmax(i); tcgen05.commit signals the mbarriers;
+//      tcgen05.mma (M=128, N=128, P read from TMEM, V read MN-major) into TMEM columns [128, 256),
+//      issued in readiness order so S(i+1) runs under softmax(i); tcgen05.commit signals mbarriers;
 //   warps 2-5 (softmax): each thread owns one row (its TMEM lane): one tcgen05.ld of the row's 64
 //      scores, causal / length mask (set to -inf) only on tiles that cross a row's causal end or
 //      the history end, online softmax in the exp2 domain; the running O in TMEM is rescaled
 //      (tcgen05.ld/st, warp-wide) only when a row maximum grew by more than 2^8 since its last
-//      rescale (p <= 2^8 stays exact in fp32 and the final 1/l absorbs it); P is written as 16-bit
-//      values into the tile's K buffer (dead once S is done), in the 128-byte-swizzled K-major layout.
+//      rescale (p <= 2^8 stays exact in fp32 and the final 1/l absorbs it); P is written back with
+//      tcgen05.st as 16-bit pairs into the first 32 columns of the tile's S buffer.
 // Epilogue: tcgen05.ld of O, divide by l (or store the partial), 16-byte stores.  Padding
 // positions get zeros.
 //
@@ -29,7 +30,7 @@
 // regions of R*128 bytes (columns 0-63 and 64-127); row r of a region is 128 bytes at r*128 and
 // its 16-byte unit u lives at unit u ^ (r % 8).  Every region starts 1024-byte aligned.
 // Descriptors:
-//   K-major (Q: R=128, K: R=64, P: 128 rows x 64 columns = one region):  LBO = 16 B (unused),
+//   K-major (Q: R=128, K: R=64):  LBO = 16 B (unused),
 //     SBO = 1024 B (8-row groups), swizzle 128B; k-step s starts at region(s/4) + (s%4)*32 B.
 //   MN-major (V as the B operand of PV, N = head_dim):  LBO = 8 KiB (next 64 columns of N),
 //     SBO = 1024 B (next 8 K-rows); k-step s starts at s*16 rows = s*2048 B.
@@ -88,6 +89,14 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
+// Same, with A (M=128 rows x 16 K elements, two 16-bit values per 32-bit column) read from TMEM.
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                                uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -137,6 +146,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
       "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -198,11 +219,12 @@ __device__ __forceinline__ TcGeometry tc_geometry(const PrefillArgs& a, int64_t 
   return g;
 }
 
-// cp.async staging (block sizes without a TMA box): history tile k = positions [64k, 64k + 64),
-// rows at or past `start` zero-filled; block ids of the tile's pages are read once into `pages`.
+// cp.async staging (block sizes without a TMA box) of the K or the V rows of history tile k =
+// positions [64k, 64k + 64) from `pool`; rows at or past `start` zero-filled; block ids of the
+// tile's pages are read once into `pages`.
 template <typename T>
 __device__ __forceinline__ void stage_hist_cp(const PrefillArgs& a, const BlockAddr& ba, int64_t b, int h, int start,
-                                              int k, uint32_t k_dst, uint32_t v_dst, int lane, int64_t* pages) {
+                                              int k, const char* pool, uint32_t dst, int lane, int64_t* pages) {
   const int unit = lane & 15;
   const int j0 = k * kTcKv;
   const int hist_rows = max(0, min(kTcKv, start - j0));
@@ -216,8 +238,7 @@ __device__ __forceinline__ void stage_hist_cp(const PrefillArgs& a, const BlockA
   const int64_t head_off = (int64_t)h * kTcDim * sizeof(T) + unit * 16;
 #pragma unroll 4
   for (int rr = lane >> 4; rr < kTcKv; rr += 2) {
-    const char* ksrc = a.k_chunk;  // any valid address when zero-filling
-    const char* vsrc = a.k_chunk;
+    const char* src = pool;  // any valid address when zero-filling
     bool valid = rr < hist_rows;
     if (valid) {
       uint32_t bi, off;
@@ -227,32 +248,26 @@ __device__ __forceinline__ void stage_hist_cp(const PrefillArgs& a, const BlockA
         if (unit == 0) record_status(MI_STATUS_BAD_BLOCK);
         valid = false;
       } else {
-        const int64_t o = (blk * a.block_size + off) * pool_row + head_off;
-        ksrc = a.k_pool + o;
-        vsrc = a.v_pool + o;
+        src = pool + (blk * a.block_size + off) * pool_row + head_off;
       }
     }
-    const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion);
-    cp_async16(k_dst + o, ksrc, valid);
-    cp_async16(v_dst + o, vsrc, valid);
+    cp_async16(dst + sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion), src, valid);
   }
   __syncwarp();  // `pages` is rewritten for the next tile
 }
 
-// cp.async staging of chunk tile k = chunk tokens [64k, 64k + 64); rows at or past `rows_end` zero.
+// cp.async staging of the K or V rows (`chunk` = k_chunk or v_chunk) of chunk tile k = chunk
+// tokens [64k, 64k + 64); rows at or past `rows_end` zero.
 __device__ __forceinline__ void stage_chunk_cp(const PrefillArgs& a, int64_t b, int h, int64_t first, int k,
-                                               int rows_end, uint32_t k_dst, uint32_t v_dst, int lane) {
+                                               int rows_end, const char* chunk, uint32_t dst, int lane) {
   const int unit = lane & 15;
-  const char* kc = a.k_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
-  const char* vc = a.v_chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
+  const char* src = chunk + b * a.kv_sb[0] + (int64_t)h * a.kv_sb[2] + unit * 16;
 #pragma unroll 4
   for (int rr = lane >> 4; rr < kTcKv; rr += 2) {
     const int jc = k * kTcKv + rr;
     const bool valid = jc < rows_end;
-    const int64_t pos = first + jc;
-    const uint32_t o = sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion);
-    cp_async16(k_dst + o, valid ? kc + pos * a.kv_sb[1] : a.k_chunk, valid);
-    cp_async16(v_dst + o, valid ? vc + pos * a.kv_sb[1] : a.k_chunk, valid);
+    cp_async16(dst + sw128_offset((uint32_t)rr, (uint32_t)unit, kKvRegion),
+               valid ? src + (first + jc) * a.kv_sb[1] : chunk, valid);
   }
 }
 
@@ -275,13 +290,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2] loader -> MMA: stage landed
-  uint64_t* kv_empty = bars + 3;  // [2] MMA -> loader: PV of the stage done
-  uint64_t* s_full = bars + 5;    // [2] MMA -> softmax: S tile ready
-  uint64_t* p_full = bars + 7;    // [2] softmax -> MMA: P written (and S consumed)
-  uint64_t* o_done = bars + 9;    // MMA -> softmax: one phase per PV (rescale waits)
-  uint64_t* o_final = bars + 10;  // MMA -> softmax: the last PV is done (epilogue)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* k_full = bars + 1;    // [2] loader -> MMA: K stage landed
+  uint64_t* k_empty = bars + 3;   // [2] MMA -> loader: S of the stage done (K free)
+  uint64_t* v_full = bars + 5;    // [2] loader -> MMA: V stage landed
+  uint64_t* v_empty = bars + 7;   // [2] MMA -> loader: PV of the stage done (V free)
+  uint64_t* s_full = bars + 9;    // [2] MMA -> softmax: S tile ready
+  uint64_t* p_full = bars + 11;   // [2] softmax -> MMA: P written into TMEM (and S consumed)
+  uint64_t* o_done = bars + 13;   // MMA -> softmax: one phase per PV (rescale waits)
+  uint64_t* o_final = bars + 14;  // MMA -> softmax: the last PV is done (epilogue)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async loader: block ids of one tile
 
   const int qtile = blockIdx.x / max_splits;
@@ -321,8 +338,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   if (tid == 0) {
     mbar_init(q_full, kTma ? 1 : kLoaderThreads);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], kTma ? 1 : kLoaderThreads);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], kTma ? 1 : kLoaderThreads);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], kTma ? 1 : kLoaderThreads);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kSoftmaxThreads);
     }
@@ -342,8 +361,28 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   bool aborted = false;
 
   if (warp == kLoaderWarp) {
-    // ---------------- loader: Q once, then K/V tiles into a 2-stage ring ----------------
+    // ---------------- loader: Q once, then K and V tiles into two 2-stage rings ----------------
+    // Order K0 K1 V0 K2 V1 K3 ...: K(i+2) waits for S(i), V(i) for PV(i-2), and the MMA thread
+    // issues ... PV(i-2) S(i) PV(i-1) S(i+1) ..., so each wait ends in the order the loads are issued.
     if constexpr (kTma) {
+      // Block ids of the split's history pages, resolved once: the pool row of each page's first
+      // slot, or a row past the pool for a page at or past `start` (TMA fills it with zeros).
+      int* page_rows = reinterpret_cast<int*>(pages);
+      const int pages_per_tile = kTcKv / a.block_size;
+      const int num_slots = (int)(a.num_blocks * a.block_size);
+      const int n_pages = max(0, min(t_end, hist_tiles) - t_begin) * pages_per_tile;
+      const int64_t* table = a.block_tables + b * a.table_stride;
+      for (int j = lane; j < n_pages; j += 32) {
+        const int pos0 = t_begin * kTcKv + j * a.block_size;
+        int row0 = num_slots;
+        if (pos0 < start) {
+          const int64_t blk = table[pos0 >> shift];
+          if (blk < 0 || blk >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
+          else row0 = (int)(blk * a.block_size);
+        }
+        page_rows[j] = row0;
+      }
+      __syncwarp();
       if (lane == 0) {
         tma_prefetch_desc(&maps.q);
         tma_prefetch_desc(&maps.k_chunk);
@@ -351,38 +390,31 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
         mbar_arrive_expect_tx(q_full, kQBytes);
         for (int c = 0; c < 2; ++c)  // box [64 d, G heads, 128/G tokens]: row = token * G + head
           tma_load_4d(smem + kOffQ + c * kQRegion, &maps.q, q_full, c * 64, h * G, (int)(first + tok0), (int)b);
-        const int64_t* table = a.block_tables + b * a.table_stride;
-        const int pages_per_tile = kTcKv / a.block_size;
         const int page_bytes = a.block_size * 128;
-        const int num_slots = (int)(a.num_blocks * a.block_size);
-        for (int i = 0; i < n; ++i) {
+        auto load = [&](int i, bool is_v) {
           const int st = i & 1;
-          if (i >= 2) mbar_wait(&kv_empty[st], ((i - 2) >> 1) & 1, aborted);
-          uint8_t* kd = smem + kOffK + st * kKvBytes;
-          uint8_t* vd = smem + kOffV + st * kKvBytes;
-          mbar_arrive_expect_tx(&kv_full[st], 2 * kKvBytes);
+          uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+          if (i >= 2) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i - 2) >> 1) & 1, aborted);
+          uint8_t* dst = smem + (is_v ? kOffV : kOffK) + st * kKvBytes;
+          mbar_arrive_expect_tx(full, kKvBytes);
           const int t = t_begin + i;
           if (t < hist_tiles) {
+            const CUtensorMap* map = is_v ? &maps.v_pool : &maps.k_pool;
             for (int pg = 0; pg < pages_per_tile; ++pg) {
-              const int pos0 = t * kTcKv + pg * a.block_size;
-              int row0 = num_slots;  // past the tensor: TMA fills zeros
-              if (pos0 < start) {
-                const int64_t blk = table[pos0 >> shift];
-                if (blk < 0 || blk >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
-                else row0 = (int)(blk * a.block_size);
-              }
-              for (int c = 0; c < 2; ++c) {
-                tma_load_3d(kd + c * kKvRegion + pg * page_bytes, &maps.k_pool, &kv_full[st], c * 64, h, row0);
-                tma_load_3d(vd + c * kKvRegion + pg * page_bytes, &maps.v_pool, &kv_full[st], c * 64, h, row0);
-              }
+              const int row0 = page_rows[i * pages_per_tile + pg];
+              for (int c = 0; c < 2; ++c) tma_load_3d(dst + c * kKvRegion + pg * page_bytes, map, full, c * 64, h, row0);
             }
           } else {
+            const CUtensorMap* map = is_v ? &maps.v_chunk : &maps.k_chunk;
             const int pos = (int)first + (t - hist_tiles) * kTcKv;
-            for (int c = 0; c < 2; ++c) {
-              tma_load_4d(kd + c * kKvRegion, &maps.k_chunk, &kv_full[st], c * 64, h, pos, (int)b);
-              tma_load_4d(vd + c * kKvRegion, &maps.v_chunk, &kv_full[st], c * 64, h, pos, (int)b);
-            }
+            for (int c = 0; c < 2; ++c) tma_load_4d(dst + c * kKvRegion, map, full, c * 64, h, pos, (int)b);
           }
+        };
+        load(0, false);
+        if (n > 1) load(1, false);
+        for (int i = 0; i < n; ++i) {
+          load(i, true);
+          if (i + 2 < n) load(i + 2, false);
         }
       }
     } else {
@@ -397,14 +429,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
         cp_async16(sbase + kOffQ + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
       }
       cp_async_arrive_noinc(q_full);
-      for (int i = 0; i < n; ++i) {
+      auto load = [&](int i, bool is_v) {
         const int st = i & 1;
-        if (i >= 2) mbar_wait(&kv_empty[st], ((i - 2) >> 1) & 1, aborted);
+        if (i >= 2) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i - 2) >> 1) & 1, aborted);
         const int t = t_begin + i;
-        const uint32_t kd = sbase + kOffK + st * kKvBytes, vd = sbase + kOffV + st * kKvBytes;
-        if (t < hist_tiles) stage_hist_cp<T>(a, ba, b, h, start, t, kd, vd, lane, pages);
-        else stage_chunk_cp(a, b, h, first, t - hist_tiles, (int)tok_end, kd, vd, lane);
-        cp_async_arrive_noinc(&kv_full[st]);
+        const uint32_t dst = sbase + (is_v ? kOffV : kOffK) + st * kKvBytes;
+        if (t < hist_tiles) stage_hist_cp<T>(a, ba, b, h, start, t, is_v ? a.v_pool : a.k_pool, dst, lane, pages);
+        else stage_chunk_cp(a, b, h, first, t - hist_tiles, (int)tok_end, is_v ? a.v_chunk : a.k_chunk, dst, lane);
+        cp_async_arrive_noinc(is_v ? &v_full[st] : &k_full[st]);
+      };
+      load(0, false);
+      if (n > 1) load(1, false);
+      for (int i = 0; i < n; ++i) {
+        load(i, true);
+        if (i + 2 < n) load(i + 2, false);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -423,19 +461,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
         for (int s = 0; s < kTcDim / 16; ++s)
           umma_f16(tmem + st * kTcKv, desc_kmajor(q0 + (s >> 2) * kQRegion + (s & 3) * 32),
                    desc_kmajor(kb + (s >> 2) * kKvRegion + (s & 3) * 32), idesc_qk, s > 0 ? 1u : 0u);
+        umma_commit(&k_empty[st]);
         umma_commit(&s_full[st]);
       };
       auto issue_pv = [&](int i) {
         const int st = i & 1;
         fence_async_smem();
         tc_fence_after();
-        const uint32_t kb = sbase + kOffK + st * kKvBytes;  // holds P(i)
         const uint32_t vb = sbase + kOffV + st * kKvBytes;
 #pragma unroll
-        for (int s = 0; s < kTcKv / 16; ++s)
-          umma_f16(tmem + kTmemO, desc_kmajor(kb + s * 32), desc_mnmajor(vb + s * 2048), idesc_pv,
-                   (i > 0 || s > 0) ? 1u : 0u);
-        umma_commit(&kv_empty[st]);
+        for (int s = 0; s < kTcKv / 16; ++s)  // P(i): 16-bit pairs in the S buffer's first 32 columns
+          umma_f16_tmem_a(tmem + kTmemO, tmem + st * kTcKv + s * 8, desc_mnmajor(vb + s * 2048), idesc_pv,
+                          (i > 0 || s > 0) ? 1u : 0u);
+        umma_commit(&v_empty[st]);
         umma_commit(o_done);
       };
       mbar_wait(q_full, 0, aborted);
@@ -445,11 +483,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       uint64_t t_last = globaltimer_ns();
       while (npv < n) {
         bool progressed = false;
-        if (ns < n && ns <= npv + 1 && mbar_test_wait(&kv_full[ns & 1], (ns >> 1) & 1)) {
+        if (ns < n && ns <= npv + 1 && mbar_test_wait(&k_full[ns & 1], (ns >> 1) & 1)) {
           issue_s(ns++);
           progressed = true;
         }
-        if (npv < ns && mbar_test_wait(&p_full[npv & 1], (npv >> 1) & 1)) {
+        if (npv < ns && mbar_test_wait(&p_full[npv & 1], (npv >> 1) & 1) &&
+            mbar_test_wait(&v_full[npv & 1], (npv >> 1) & 1)) {
           issue_pv(npv++);
           progressed = true;
         }
@@ -534,27 +573,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       }
       const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;  // a row with nothing visible yet: all -inf
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
-      uint8_t* p_tile = smem + kOffK + st * kKvBytes;
+      uint32_t pw[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            // branch-free: every exponent is independent, so the ex2 issue overlaps
-            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][u * 8 + 2 * e]), scale, neg_m));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][u * 8 + 2 * e + 1]), scale, neg_m));
-            ps[e] += p0 + p1;
-            w[e] = pack2<T>(p0, p1);
-          }
-          *reinterpret_cast<uint4*>(p_tile + sw128_offset((uint32_t)r, (uint32_t)(c * 4 + u), kQRegion)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
-        }
+      for (int j = 0; j < 32; ++j) {
+        // branch-free: every exponent is independent, so the ex2 issue overlaps
+        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[j >> 4][(2 * j) & 31]), scale, neg_m));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[j >> 4][(2 * j + 1) & 31]), scale, neg_m));
+        ps[j & 3] += p0 + p1;
+        pw[j] = pack2<T>(p0, p1);
       }
       l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      fence_async_smem();  // P (generic writes) before the tensor core reads it
-      tc_fence_before();   // our tcgen05.ld of S / st of O before the next MMAs
+      // P(i) as the A operand of PV: 16-bit pairs over the S buffer's first 32 columns (S(i) is in
+      // registers already; S(i+2) overwrites them only after PV(i), issued before it, has read them)
+      tmem_st32(s_addr, pw);
+      tc_fence_before();  // our tcgen05.ld of S / st of P and O before the next MMAs
       mbar_arrive(&p_full[st]);
     }
     // ---- epilogue ----
