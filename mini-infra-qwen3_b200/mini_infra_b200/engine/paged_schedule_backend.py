@@ -2,7 +2,8 @@
 
 Per prefill step: chunk forward (model_ms, StepTimer), then ``store_prefill`` timed as cache_ms
 (host wall clock between two synchronisations).  Per decode step: host packing + H2D timed as
-cache_ms, then the decode forward (model_ms).  ``accessed_kv_cache_tokens`` counts history tokens
+cache_ms, then the decode forward (model_ms) — a CUDA-graph replay per batch bucket unless
+``cuda_graphs=False`` (a bucket's first step captures its graph before the timing starts).  ``accessed_kv_cache_tokens`` counts history tokens
 read: sum of chunk starts (prefill) and sum of context lengths (decode).
 """
 
@@ -32,6 +33,7 @@ class PagedScheduleBackend:
         paged_cache_config: PagedCacheConfig,
         batching_method: BatchingMethod = BatchingMethod.CONTINUOUS,
         pad_token_id: int = 0,
+        cuda_graphs: bool = True,
     ) -> None:
         self.model = model
         self.device = next(model.parameters()).device
@@ -57,6 +59,13 @@ class PagedScheduleBackend:
             device=self.device,
         )
         self.kv_cache_manager = KVCacheManager(self.block_size, num_blocks)
+        if cuda_graphs and self.device.type == "cuda":
+            # decode tables never exceed the largest request; round the graphs' width up to a power of two
+            self.runner.enable_decode_graphs(self.pool.kv_pools, 1 << max(4, (largest - 1).bit_length()))
+
+    def close(self) -> None:
+        """Drop the decode graphs (they may hold NCCL calls: before the process group goes)."""
+        self.runner.release_decode_graphs()
 
     @property
     def kv_cache_config(self) -> PagedCacheConfig:
@@ -83,10 +92,12 @@ class PagedScheduleBackend:
         )
 
     def execute_decode(self, scheduled: Sequence[RequestState]) -> ScheduleStepOutput:
+        tables = [self.kv_cache_manager.block_table(s.request.request_idx) for s in scheduled]
+        self.runner.warm_decode_graph(len(tables), max(len(t) for t in tables))  # first use of a bucket: capture
         synchronize(self.device)
         t0 = time.perf_counter()
         ids, pos, md = self.runner.prepare_decode_inputs(
-            [self.kv_cache_manager.block_table(s.request.request_idx) for s in scheduled],
+            tables,
             last_tokens=[s.generated[-1] for s in scheduled],
             positions=[s.cache_length for s in scheduled],
             block_size=self.block_size,

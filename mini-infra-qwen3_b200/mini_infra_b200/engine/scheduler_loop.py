@@ -77,7 +77,8 @@ def _run_loop(backend: PagedScheduleBackend, requests: Sequence[Request], max_ru
     synchronize(backend.device)
     wall_ms = (time.perf_counter() - wall0) * 1000.0
     result = summarize_schedule(states, events, max_running_requests, wall_ms, backend.collect_paged_cache_profile())
-    result.extra.update(h2d_bytes=backend.runner.h2d_bytes, d2h_bytes=backend.runner.d2h_bytes)
+    result.extra.update(h2d_bytes=backend.runner.h2d_bytes, d2h_bytes=backend.runner.d2h_bytes,
+                        decode_graph_replays=backend.runner.graph_replays)
     return result
 
 
@@ -90,8 +91,11 @@ def run_scheduler(
     *,
     pad_token_id: int = 0,
     stop_on_eos: bool = True,
+    cuda_graphs: bool = True,
 ) -> ScheduleResult:
-    """Run the requests through the paged engine; returns sequences, events and metrics."""
+    """Run the requests through the paged engine; returns sequences, events and metrics.
+
+    ``cuda_graphs`` replays decode steps from per-batch-bucket CUDA graphs (False: eager)."""
     if not requests:
         raise ValueError("requests must not be empty")
     mrr = config.scheduler_config.max_running_requests or len(requests)
@@ -102,5 +106,9 @@ def run_scheduler(
         raise NotImplementedError("only caching-method=paged-kv-cache is implemented in this package")
     if config.batching_method not in (BatchingMethod.CONTINUOUS, BatchingMethod.FIXED):
         raise ValueError(f"paged-kv-cache supports continuous or fixed batching, got {config.batching_method.value}")
-    backend = PagedScheduleBackend(model, requests, mrr, config.kv_cache_config, config.batching_method, pad_token_id)
-    return _run_loop(backend, requests, mrr, config, eos_token_id, stop_on_eos)
+    backend = PagedScheduleBackend(model, requests, mrr, config.kv_cache_config, config.batching_method, pad_token_id,
+                                   cuda_graphs=cuda_graphs)
+    try:
+        return _run_loop(backend, requests, mrr, config, eos_token_id, stop_on_eos)
+    finally:
+        backend.close()

@@ -16,6 +16,7 @@ from mini_infra_b200 import _native as nat
 
 _DTYPES = {torch.float32: nat.MI_F32, torch.bfloat16: nat.MI_BF16, torch.float16: nat.MI_F16}
 _workspaces: dict[tuple[int, str], torch.Tensor] = {}
+_retired_workspaces: list[torch.Tensor] = []
 
 
 def dtype_code(dtype: torch.dtype) -> int:
@@ -66,10 +67,15 @@ def _check_pool(k_pool: torch.Tensor, v_pool: torch.Tensor) -> tuple[int, int, i
 
 
 def workspace(device: torch.device, nbytes: int, slot: str = "decode") -> torch.Tensor:
-    """A per-device, per-purpose byte buffer of at least nbytes (reused across calls on the same stream)."""
+    """A per-device, per-purpose byte buffer of at least nbytes (reused across calls on the same stream).
+
+    A buffer that grows is replaced, but the old one is kept alive: a captured CUDA graph may
+    still hold its address."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), slot)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            _retired_workspaces.append(buf)
         size = max(nbytes, 1 << 20)
         buf = torch.empty(size + 256, dtype=torch.uint8, device=device)
         _workspaces[key] = buf

@@ -12,6 +12,9 @@ tables).  Attention reads history in place from the pools; nothing gathers the h
 * ``store_prefill`` — writes those tokens to their slots; the slot arithmetic
   (table[pos // bs] * bs + pos % bs) runs on the device;
 * ``prepare_decode_inputs`` / ``run_decode_step`` — decode step, append fused in the attention op.
+  With ``enable_decode_graphs`` the packed rows are padded to a batch bucket and copied into
+  that bucket's static input buffer, and the step replays the bucket's CUDA graph
+  (``worker/decode_graphs.py``); otherwise it runs eagerly.
 """
 
 from __future__ import annotations
@@ -19,11 +22,13 @@ from __future__ import annotations
 from collections.abc import Sequence
 from typing import NamedTuple
 
+import numpy as np
 import torch
 
 from mini_infra_b200.device import StepTimer
 from mini_infra_b200.model.qwen3 import ChunkPrefillMetadata, PagedAttentionMetadata
 from mini_infra_b200.worker.base_runner import BaseModelRunner, PrefillOutput
+from mini_infra_b200.worker.decode_graphs import DecodeGraphSet, packed_length
 from mini_infra_b200.worker.kv_cache import KVCache
 from mini_infra_b200.worker.paged_kv_cache import PagedKVCachePool
 from mini_infra_b200.worker.sampler import greedy_sample
@@ -49,6 +54,27 @@ class PagedRunner(BaseModelRunner):
 
     h2d_bytes = 0
     d2h_bytes = 0
+    graph_replays = 0  # decode steps served by a CUDA-graph replay
+    decode_graphs: DecodeGraphSet | None = None
+    _graph_step: tuple[int, int, int] | None = None  # (bucket, batch, static buffer address)
+
+    def enable_decode_graphs(self, kv_pools, width: int) -> None:
+        """Replay decode steps of at most `width` table blocks from CUDA graphs over `kv_pools`."""
+        self.release_decode_graphs()
+        self.decode_graphs = DecodeGraphSet(self.model, kv_pools, width)
+
+    def release_decode_graphs(self) -> None:
+        if self.decode_graphs is not None:
+            self.decode_graphs.release()
+        self.decode_graphs = None
+        self._graph_step = None
+
+    def warm_decode_graph(self, batch: int, max_blocks: int) -> None:
+        """Capture the graph a step of this shape will replay (outside any step timing)."""
+        g = self.decode_graphs
+        bucket = g.bucket_for(batch, max_blocks) if g is not None else None
+        if bucket is not None:
+            g.static_inputs(bucket)
 
     def _upload(self, values: list[int]) -> torch.Tensor:
         self.h2d_bytes += 8 * len(values)
@@ -131,6 +157,10 @@ class PagedRunner(BaseModelRunner):
         b = len(block_tables)
         max_blocks = max(len(t) for t in block_tables)
         slots = [int(t[p // block_size]) * block_size + p % block_size for t, p in zip(block_tables, positions)]
+        g = self.decode_graphs
+        bucket = g.bucket_for(b, max_blocks) if g is not None else None
+        if bucket is not None:
+            return self._prepare_graph_inputs(g, bucket, block_tables, last_tokens, positions, slots)
         flat = [int(x) for x in last_tokens] + [int(p) for p in positions] + slots + [int(p) + 1 for p in positions]
         for t in block_tables:
             flat += [int(x) for x in t] + [_NULL_BLOCK_ID] * (max_blocks - len(t))
@@ -142,6 +172,29 @@ class PagedRunner(BaseModelRunner):
         )
         return packed[:b].view(b, 1), packed[b : 2 * b].view(b, 1), metadata
 
+    def _prepare_graph_inputs(self, g: DecodeGraphSet, n: int, block_tables, last_tokens, positions, slots):
+        """Packed rows padded to bucket n, copied into the bucket's static buffer; views of its first b rows."""
+        b, w = len(block_tables), g.width
+        host = np.zeros(packed_length(n, w), dtype=np.int64)
+        host[3 * n : 4 * n] = 1
+        host[:b] = last_tokens
+        host[n : n + b] = positions
+        host[2 * n : 2 * n + b] = slots
+        host[3 * n : 3 * n + b] = host[n : n + b] + 1
+        tables = host[4 * n :].reshape(n, w)
+        for i, t in enumerate(block_tables):
+            tables[i, : len(t)] = t
+        static = g.static_inputs(n)
+        self.h2d_bytes += host.nbytes
+        static.copy_(torch.from_numpy(host).pin_memory(), non_blocking=True)
+        self._graph_step = (n, b, static.data_ptr())
+        metadata = PagedAttentionMetadata(
+            slot_mapping=static[2 * n : 2 * n + b],
+            block_tables=static[4 * n : 4 * n + b * w].view(b, w),
+            context_lens=static[3 * n : 3 * n + b],
+        )
+        return static[:b].view(b, 1), static[n : n + b].view(b, 1), metadata
+
     def run_decode_step(
         self,
         input_ids: torch.Tensor,
@@ -149,11 +202,20 @@ class PagedRunner(BaseModelRunner):
         metadata: PagedAttentionMetadata,
         pool: PagedKVCachePool,
     ) -> PagedDecodeOutput:
+        step, self._graph_step = self._graph_step, None
+        g = self.decode_graphs
+        use_graph = (step is not None and g is not None and step[2] == input_ids.data_ptr()
+                     and step[1] == input_ids.shape[0] and g.kv_pools[0][0].data_ptr() == pool.kv_pools[0][0].data_ptr())
         with StepTimer(self.device) as timer:
-            logits, _ = self.model(
-                input_ids, position_ids=position_ids, attn_metadata=metadata._replace(kv_pools=tuple(pool.kv_pools))
-            )
-            next_token, _ = greedy_sample(logits)
+            if use_graph:
+                next_token = g.replay(step[0])[: step[1]]
+                self.graph_replays += 1
+            else:
+                logits, _ = self.model(
+                    input_ids, position_ids=position_ids,
+                    attn_metadata=metadata._replace(kv_pools=tuple(pool.kv_pools)),
+                )
+                next_token, _ = greedy_sample(logits)
         self.d2h_bytes += 8 * input_ids.shape[0]
         return PagedDecodeOutput(next_token.squeeze(-1).tolist(), timer.elapsed_ms)
 

@@ -2,7 +2,8 @@
 
 * C1 tiny model (fp32): greedy token ids identical to what the REFERENCE engine produced
   (tests/golden/engine.json), for 32 and 64 decode steps, tied and untied heads, prefill-first
-  and chunked-prefill — the drop-in claim for caching-method=paged-kv-cache.
+  and chunked-prefill — the drop-in claim for caching-method=paged-kv-cache — with the decode
+  steps replayed from CUDA graphs (every one of them) and run eagerly.
 * Runner-level checks mirroring the reference's own paged tests: chunked prefill in rounds
   leaves the same K/V in the pool as a one-shot prefill and yields the same first token.
 """
@@ -40,16 +41,19 @@ def no_tf32():
     torch.backends.cuda.matmul.allow_tf32 = old
 
 
+@pytest.mark.parametrize("graphs", [True, False], ids=["graphs", "eager"])
 @pytest.mark.parametrize("case", GOLDEN["cases"], ids=lambda c: c["name"])
-def test_engine_tokens_identical_to_reference(case):
+def test_engine_tokens_identical_to_reference(case, graphs):
     model = c1_model(case["tied"])
     policy = PrefillFirstConfig() if case["batching_policy"] == "prefill-first" else ChunkedPrefillConfig(
         case["token_budget"])
     cfg = EngineConfig(PagedCacheConfig(block_size=16), BatchingMethod.CONTINUOUS,
                        scheduler_config=SchedulerConfig(case["max_running_requests"], policy))
     result = run_scheduler(cfg, model, make_requests(case["prompts"], case["max_new_tokens"]), None,
-                           stop_on_eos=False)
+                           stop_on_eos=False, cuda_graphs=graphs)
     assert [s.token_ids for s in result.sequences] == case["tokens"]
+    replays = result.extra["decode_graph_replays"]
+    assert (replays == case["num_decode_steps"]) if graphs else replays == 0
     assert result.schedule_metrics.num_prefill_steps == case["num_prefill_steps"]
     assert result.schedule_metrics.num_decode_steps == case["num_decode_steps"]
     assert result.paged_cache is not None and result.paged_cache.peak_used_blocks > 0
