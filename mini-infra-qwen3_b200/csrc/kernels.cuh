@@ -140,4 +140,57 @@ bool prefill_tc_tma_block_size(int block_size);
 cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, const PrefillMaps* maps, int dtype,
                                     cudaStream_t s);
 
+// Model-side fused row operations around the attention (layer_ops.cu).
+struct RmsNormArgs {
+  const char* x;  // [rows, hidden] rows at x + row * x_rs (bytes)
+  int64_t x_rs;
+  const char* res;  // optional residual added first (same shape), or null
+  int64_t res_rs;
+  char* res_out;  // optional: receives x + res (may alias res)
+  int64_t res_out_rs;
+  const char* w;  // [hidden]
+  char* out;
+  int64_t out_rs;
+  int64_t rows;
+  int hidden;
+  float eps;
+  float inv_hidden;
+};
+cudaError_t launch_rmsnorm(const RmsNormArgs& a, bool vec16, int dtype, cudaStream_t s);
+
+struct QkNormRopeArgs {
+  const char* q;  // token t, head h at q + t * q_rs (bytes) + h * head_dim elements
+  int64_t q_rs;
+  const char* k;
+  int64_t k_rs;
+  const char* v;
+  int64_t v_rs;
+  const char* q_w;  // [head_dim] q_norm / k_norm weights
+  const char* k_w;
+  const char* cos;  // [tokens, head_dim] rows at cos + t * cs_rs
+  const char* sin;
+  int64_t cs_rs;
+  int64_t tokens;
+  int hq, hkv, head_dim;
+  float eps;
+  char* q_out;  // [tokens, hq, head_dim]
+  char* k_out;  // optional [tokens, hkv, head_dim]
+  char* v_out;  // optional [tokens, hkv, head_dim]
+  const int64_t* slots;  // optional: append K/V to the pools at these slots
+  char* k_pool;
+  char* v_pool;
+  int64_t num_slots;
+};
+cudaError_t launch_qk_norm_rope(const QkNormRopeArgs& a, int dtype, cudaStream_t s);
+
+struct SiluMulArgs {
+  const char* gate;  // [rows, cols] at gate + row * in_rs (bytes); up likewise
+  const char* up;
+  int64_t in_rs;
+  char* out;
+  int64_t out_rs;
+  int64_t rows, cols;
+};
+cudaError_t launch_silu_mul(const SiluMulArgs& a, bool vec16, int dtype, cudaStream_t s);
+
 }  // namespace mi

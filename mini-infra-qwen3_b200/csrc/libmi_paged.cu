@@ -4,5 +4,7 @@
 #include "paged_decode.cu"
 #include "paged_prefill_tc.cu"
 #include "paged_prefill.cu"
+#include "layer_ops.cu"
 #include "api.cu"
+#include "api_layers.cu"
 #include "api_static.cu"

@@ -18,7 +18,7 @@ MI_F32, MI_BF16, MI_F16 = 0, 1, 2
 MI_OK, MI_ERR_INVALID, MI_ERR_CUDA, MI_ERR_UNSUPPORTED = 0, -1, -2, -3
 MI_STATUS_BAD_BLOCK, MI_STATUS_BAD_SLOT, MI_STATUS_TIMEOUT, MI_STATUS_BAD_LENGTH, MI_STATUS_BAD_INDEX = 1, 2, 4, 8, 16
 
-# Every symbol of include/mi_paged.h with its ctypes signature (restype, argtypes).
+# Every symbol of include/*.h with its ctypes signature (restype, argtypes).
 _P = ctypes.c_void_p
 _I64P = ctypes.POINTER(ctypes.c_int64)
 _I = ctypes.c_int
@@ -46,6 +46,14 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _I64P, _P, _P, _I64P, _P, _P, _L, _I, _I, _I, _P, _L, _P, _P, _L, _L, _I, ctypes.c_float, _P, _P,
          ctypes.c_size_t, _I, _P],
     ),
+    # include/mi_layers.h
+    "mi_rmsnorm": (_I, [_P, _L, _P, _L, _P, _L, _P, _P, _L, _L, _I, ctypes.c_float, _I, _P]),
+    "mi_qk_norm_rope": (
+        _I,
+        [_P, _L, _P, _L, _P, _L, _P, _P, _P, _P, _L, _L, _I, _I, _I, ctypes.c_float, _P, _P, _P, _P, _P, _P, _L, _I,
+         _P],
+    ),
+    "mi_silu_mul": (_I, [_P, _P, _L, _P, _L, _L, _L, _I, _P]),
 }
 
 _lock = threading.Lock()

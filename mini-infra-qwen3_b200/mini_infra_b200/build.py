@@ -24,7 +24,7 @@ NVCC_FLAGS = [
 
 
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [PKG.parent.parent / "include" / "mi_paged.h"]
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted((PKG.parent.parent / "include").glob("*.h"))
 
 
 def needs_build() -> bool:

@@ -10,6 +10,7 @@ from mini_infra_b200.model.qwen3 import (
     PastKeyValue,
     Qwen3ForCausalLM,
     Qwen3Model,
+    pack_projections_,
 )
 
 __all__ = [
@@ -26,5 +27,6 @@ __all__ = [
     "build_model",
     "init_weights_",
     "model_dtype_from_config",
+    "pack_projections_",
     "untie_lm_head_",
 ]

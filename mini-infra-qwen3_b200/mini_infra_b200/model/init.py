@@ -13,7 +13,7 @@ from __future__ import annotations
 import torch
 
 from mini_infra_b200.model.config import Qwen3Config, model_dtype_from_config
-from mini_infra_b200.model.qwen3 import HeadPartition, Qwen3ForCausalLM
+from mini_infra_b200.model.qwen3 import HeadPartition, Qwen3ForCausalLM, pack_projections_
 
 _SHARDED_ROWS = ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight")
 
@@ -61,12 +61,14 @@ def build_model(
     untied_head_seed: int | None = None,
     generator_device: str = "cpu",
 ) -> Qwen3ForCausalLM:
-    """Random-init model on `device` (weights drawn by ``init_weights_``), eval mode."""
+    """Random-init model on `device` (weights drawn by ``init_weights_``, projections packed by
+    ``pack_projections_``), eval mode."""
     dtype = dtype or model_dtype_from_config(config)
     with torch.device("meta"):
         model = Qwen3ForCausalLM(config, partition)
     model = model.to_empty(device=device).to(dtype)
     model.tie_weights()
+    pack_projections_(model)  # q/k/v and gate/up as one GEMM each (weights drawn below, in place)
     model.model.rotary_emb.inv_freq = (
         1.0 / (config.rope_theta ** (torch.arange(0, config.head_dim, 2, dtype=torch.float32) / config.head_dim))
     ).to(device)

@@ -1,8 +1,17 @@
 """Qwen3 causal LM whose attention runs on the paged-KV CUDA kernels.
 
-Projections, norms, RoPE, MLP and lm_head are plain PyTorch (cuBLAS GEMMs, elementwise ops) with
-the reference's numerics (``model/qwen3.py``: fp32 RMSNorm statistics :67-78, fp32 RoPE angles
-cast to the model dtype :95-109, rotate-half RoPE :112-144).  Attention has two entry forms:
+Numerics are the reference's (``model/qwen3.py``: fp32 RMSNorm statistics :67-78, fp32 RoPE
+angles cast to the model dtype :95-109, rotate-half RoPE :112-144), with its rounding points kept
+by the fused kernels of ``include/mi_layers.h`` that replace its element-wise chains on CUDA:
+
+* RMSNorm, with the residual add before it fused in (the layer carries the residual stream
+  apart from the branch output, so the adds land in the next norm's launch);
+* per-head q_norm / k_norm + RoPE in one launch, which on decode also appends K/V to the pools;
+* SiLU(gate) * up in one launch;
+* q/k/v and gate/up projections as one GEMM each when ``pack_projections_`` has laid their
+  weights out contiguously (the parameters stay separate views; otherwise three / two GEMMs).
+
+Attention has two entry forms:
 
 * ``PagedAttentionMetadata`` (decode, one token per row, same fields as the reference :27-42):
   the new K/V are appended at ``slot_mapping`` and attention reads history in place through
@@ -70,7 +79,13 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(hidden_size))
         self.eps = eps
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """RMSNorm(x), or RMSNorm(x + residual) with the sum written back into `residual`."""
+        if x.is_cuda:
+            return ops.rmsnorm(x, self.weight, self.eps, residual)
+        if residual is not None:
+            residual.copy_(x + residual)
+            x = residual
         dtype = x.dtype
         xf = x.float()
         normed = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
@@ -90,11 +105,33 @@ class RotaryEmbedding(nn.Module):
         return emb.cos().to(dtype), emb.sin().to(dtype)
 
 
-def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x [B, L, heads, D] rotated by cos/sin [B, L, 1, D] (rotate-half form)."""
-    half = x.shape[-1] // 2
-    rotated = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
-    return x * cos + rotated * sin
+def _packed_linear(x: torch.Tensor, weights: Sequence[torch.Tensor], packed: torch.Tensor | None):
+    """x @ [W_0; W_1; ...]^T as column views of ONE GEMM when the weights are consecutive rows of
+    `packed` (``pack_projections_``), else one GEMM per weight."""
+    if packed is not None and packed.device == x.device and packed.dtype == x.dtype:
+        offset, ok = packed.data_ptr(), True
+        for w in weights:
+            ok = ok and w.data_ptr() == offset and w.is_contiguous() and w.dtype == packed.dtype
+            offset += w.numel() * w.element_size()
+        if ok and offset == packed.data_ptr() + packed.numel() * packed.element_size():
+            out = F.linear(x, packed)
+            cols, views = 0, []
+            for w in weights:
+                views.append(out[:, cols : cols + w.shape[0]])
+                cols += w.shape[0]
+            return views
+    return [F.linear(x, w) for w in weights]
+
+
+def _pack_rows_(modules: Sequence[nn.Linear]) -> torch.Tensor:
+    """Move the weights of `modules` into one contiguous buffer; each keeps a Parameter view of it."""
+    packed = torch.cat([m.weight.detach() for m in modules], dim=0).contiguous()
+    row = 0
+    for m in modules:
+        n = m.weight.shape[0]
+        m.weight = nn.Parameter(packed[row : row + n], requires_grad=m.weight.requires_grad)
+        row += n
+    return packed
 
 
 class HeadPartition(NamedTuple):
@@ -134,34 +171,36 @@ class Qwen3Attention(nn.Module):
         self.o_proj = nn.Linear(config.num_attention_heads * self.head_dim, config.hidden_size, bias=False)
         self.q_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
         self.k_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
-
-    def _project(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
-        b, length, _ = x.shape
-        q = self.q_norm(self.q_proj(x).view(b, length, self.num_heads, self.head_dim))
-        k = self.k_norm(self.k_proj(x).view(b, length, self.num_kv_heads, self.head_dim))
-        v = self.v_proj(x).view(b, length, self.num_kv_heads, self.head_dim)
-        cos, sin = cos.unsqueeze(2), sin.unsqueeze(2)
-        return _rotate(q, cos, sin), _rotate(k, cos, sin), v
+        self.packed_qkv: torch.Tensor | None = None  # set by pack_projections_
 
     def forward(self, x, cos, sin, kv_pool: PastKeyValue | None, metadata):
-        b, length, _ = x.shape
-        q, k, v = self._project(x, cos, sin)
+        """x [B, L, hidden], cos/sin [B, L, D] -> (o_proj output [B, L, hidden], present)."""
+        b, length, hidden = x.shape
+        tokens, d = b * length, self.head_dim
+        q, k, v = _packed_linear(x.reshape(tokens, hidden), (self.q_proj.weight, self.k_proj.weight,
+                                                              self.v_proj.weight), self.packed_qkv)
+        cos2, sin2 = cos.reshape(tokens, d), sin.reshape(tokens, d)
         if isinstance(metadata, PagedAttentionMetadata):
+            # decode: norm + RoPE, and the new K/V appended to the pools, in one launch
             key_pool, value_pool = kv_pool
-            attn = ops.paged_decode(
-                q.view(b, self.num_heads, self.head_dim), key_pool, value_pool, metadata.block_tables,
-                metadata.context_lens, self.scaling, key_new=k.view(b, self.num_kv_heads, self.head_dim),
-                value_new=v.view(b, self.num_kv_heads, self.head_dim), slot_mapping=metadata.slot_mapping,
-            )
+            q_out, _, _ = ops.qk_norm_rope(q, k, v, self.q_norm.weight, self.k_norm.weight, cos2, sin2, self.q_norm.eps,
+                                           self.num_heads, self.num_kv_heads, kv_out=False,
+                                           slot_mapping=metadata.slot_mapping, k_pool=key_pool, v_pool=value_pool)
+            attn = ops.paged_decode(q_out, key_pool, value_pool, metadata.block_tables, metadata.context_lens,
+                                    self.scaling)
             present = kv_pool
         else:
+            q_out, k_out, v_out = ops.qk_norm_rope(q, k, v, self.q_norm.weight, self.k_norm.weight, cos2, sin2,
+                                                   self.q_norm.eps, self.num_heads, self.num_kv_heads)
+            k4 = k_out.view(b, length, self.num_kv_heads, d)
+            v4 = v_out.view(b, length, self.num_kv_heads, d)
             key_pool, value_pool = kv_pool if kv_pool is not None else (None, None)
             attn = ops.paged_prefill(
-                q, k, v, key_pool, value_pool, metadata.block_tables, metadata.start_positions, metadata.chunk_lens,
-                self.scaling,
-            ).view(b * length, self.num_heads * self.head_dim)
-            present = (k.transpose(1, 2), v.transpose(1, 2))
-        attn = gather_heads(attn.view(b * length, -1), self.partition).view(b, length, -1)
+                q_out.view(b, length, self.num_heads, d), k4, v4, key_pool, value_pool, metadata.block_tables,
+                metadata.start_positions, metadata.chunk_lens, self.scaling,
+            )
+            present = (k4.transpose(1, 2), v4.transpose(1, 2))
+        attn = gather_heads(attn.view(tokens, -1), self.partition).view(b, length, -1)
         return self.o_proj(attn), present
 
 
@@ -171,9 +210,14 @@ class Qwen3MLP(nn.Module):
         self.gate_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
         self.up_proj = nn.Linear(config.hidden_size, config.intermediate_size, bias=False)
         self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
+        self.packed_gate_up: torch.Tensor | None = None  # set by pack_projections_
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+        if not x.is_cuda:
+            return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
+        x2 = x.reshape(-1, x.shape[-1])
+        gate, up = _packed_linear(x2, (self.gate_proj.weight, self.up_proj.weight), self.packed_gate_up)
+        return self.down_proj(ops.silu_mul(gate, up)).view(*x.shape[:-1], -1)
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -185,10 +229,22 @@ class Qwen3DecoderLayer(nn.Module):
         self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
 
     def forward(self, x, cos, sin, kv_pool, metadata):
-        attn, present = self.self_attn(self.input_layernorm(x), cos, sin, kv_pool, metadata)
-        x = x + attn
-        x = x + self.mlp(self.post_attention_layernorm(x))
-        return x, present
+        """x -> (x + attn + mlp, present), the reference's layer."""
+        out, residual, present = self.forward_residual(x.clone(), None, cos, sin, kv_pool, metadata)
+        return residual + out, present
+
+    def forward_residual(self, hidden, residual, cos, sin, kv_pool, metadata):
+        """Residual-stream form: the layer input is hidden + residual (hidden alone when residual is
+        None); returns (mlp output, residual stream after the attention add, present).  The adds
+        happen inside the norms' launches and overwrite `residual` (or `hidden`) in place."""
+        if residual is None:
+            residual = hidden
+            normed = self.input_layernorm(hidden)
+        else:
+            normed = self.input_layernorm(hidden, residual)
+        attn, present = self.self_attn(normed, cos, sin, kv_pool, metadata)
+        normed = self.post_attention_layernorm(attn, residual)
+        return self.mlp(normed), residual, present
 
 
 class Qwen3Model(nn.Module):
@@ -237,10 +293,11 @@ class Qwen3Model(nn.Module):
             pools = attn_metadata.kv_pools if attn_metadata.kv_pools else [None] * len(self.layers)
         cos, sin = self.rotary_emb(position_ids, hidden.dtype)
         presents = []
+        residual = None
         for layer, pool in zip(self.layers, pools):
-            hidden, present = layer(hidden, cos, sin, pool, attn_metadata)
+            hidden, residual, present = layer.forward_residual(hidden, residual, cos, sin, pool, attn_metadata)
             presents.append(present)
-        return self.norm(hidden), presents
+        return self.norm(hidden, residual), presents
 
 
 class Qwen3ForCausalLM(nn.Module):
@@ -263,6 +320,20 @@ class Qwen3ForCausalLM(nn.Module):
         return self.lm_head(hidden), presents
 
 
+@torch.no_grad()
+def pack_projections_(model: nn.Module) -> nn.Module:
+    """Lay each layer's q/k/v_proj and gate/up_proj weights out as consecutive rows of one buffer
+    (the parameters become views of it, names and values unchanged), so each group runs as ONE
+    GEMM.  Call after moving the model to its device and dtype; later in-place weight updates
+    (``copy_``, ``load_state_dict``) keep the packing, replacing a parameter object undoes it."""
+    for m in model.modules():
+        if isinstance(m, Qwen3Attention):
+            m.packed_qkv = _pack_rows_((m.q_proj, m.k_proj, m.v_proj))
+        elif isinstance(m, Qwen3MLP):
+            m.packed_gate_up = _pack_rows_((m.gate_proj, m.up_proj))
+    return model
+
+
 __all__ = [
     "ChunkPrefillMetadata",
     "DenseAttentionMetadata",
@@ -276,4 +347,5 @@ __all__ = [
     "Qwen3Model",
     "RMSNorm",
     "RotaryEmbedding",
+    "pack_projections_",
 ]

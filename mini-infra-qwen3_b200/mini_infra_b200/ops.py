@@ -313,6 +313,93 @@ def paged_prefill(
     return out
 
 
+def _rows(t: torch.Tensor, name: str) -> torch.Tensor:
+    """A [rows, cols] view with unit column stride (copies only when no such view exists)."""
+    t2 = t if t.ndim == 2 else t.reshape(-1, t.shape[-1])
+    if t2.stride(-1) != 1:
+        t2 = t2.contiguous()
+    return t2
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm of x (or of x + residual, which then replaces `residual` in place): a new tensor
+    shaped like x.  x, residual: [..., hidden]; residual contiguous."""
+    device = _require_cuda("rmsnorm", x, weight, residual)
+    hidden = int(x.shape[-1])
+    x2 = _rows(x, "x")
+    out = torch.empty(x.shape, dtype=x.dtype, device=device)
+    r2 = None
+    if residual is not None:
+        if residual.shape != x.shape or not residual.is_contiguous() or residual.dtype != x.dtype:
+            raise ValueError("residual must be a contiguous tensor shaped and typed like x")
+        r2 = residual.view(-1, hidden)
+    rc = nat.load().mi_rmsnorm(
+        _ptr(x2), x2.stride(0), _ptr(r2), r2.stride(0) if r2 is not None else 0, _ptr(r2),
+        r2.stride(0) if r2 is not None else 0, _ptr(weight), _ptr(out), hidden, x2.shape[0], hidden, float(eps),
+        dtype_code(x.dtype), _stream(device))
+    nat.check(rc, "mi_rmsnorm")
+    return out
+
+
+def qk_norm_rope(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    q_weight: torch.Tensor,
+    k_weight: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    eps: float,
+    num_q_heads: int,
+    num_kv_heads: int,
+    *,
+    kv_out: bool = True,
+    slot_mapping: torch.Tensor | None = None,
+    k_pool: torch.Tensor | None = None,
+    v_pool: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
+    """Per-head RMSNorm + rotate-half RoPE of q [T, Hq*D] and k [T, Hkv*D] (any row strides);
+    returns (q_out [T, Hq, D], k_out, v_out [T, Hkv, D] or None when kv_out is False).  With
+    slot_mapping [T] the roped K and V are also written into the pools at those slots."""
+    device = _require_cuda("qk_norm_rope", q, k, v, q_weight, k_weight, cos, sin, slot_mapping, k_pool, v_pool)
+    q2, k2, v2, c2, s2 = _rows(q, "q"), _rows(k, "k"), _rows(v, "v"), _rows(cos, "cos"), _rows(sin, "sin")
+    if c2.stride(0) != s2.stride(0):
+        c2, s2 = c2.contiguous(), s2.contiguous()
+    tokens = q2.shape[0]
+    d = int(q_weight.shape[0])
+    q_out = torch.empty((tokens, num_q_heads, d), dtype=q.dtype, device=device)
+    k_out = v_out = None
+    if kv_out:
+        k_out = torch.empty((tokens, num_kv_heads, d), dtype=q.dtype, device=device)
+        v_out = torch.empty_like(k_out)
+    num_slots = 0
+    if slot_mapping is not None:
+        _check_pool(k_pool, v_pool)
+        slot_mapping = _index(slot_mapping, "slot_mapping")
+        num_slots = k_pool.shape[0] * k_pool.shape[1]
+    rc = nat.load().mi_qk_norm_rope(
+        _ptr(q2), q2.stride(0), _ptr(k2), k2.stride(0), _ptr(v2), v2.stride(0), _ptr(q_weight), _ptr(k_weight),
+        _ptr(c2), _ptr(s2), c2.stride(0), tokens, num_q_heads, num_kv_heads, d, float(eps), _ptr(q_out), _ptr(k_out),
+        _ptr(v_out), _ptr(slot_mapping), _ptr(k_pool if slot_mapping is not None else None),
+        _ptr(v_pool if slot_mapping is not None else None), num_slots, dtype_code(q.dtype), _stream(device))
+    nat.check(rc, "mi_qk_norm_rope")
+    return q_out, k_out, v_out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up with the model's rounding; gate/up [T, I] sharing a row stride -> [T, I]."""
+    device = _require_cuda("silu_mul", gate, up)
+    g2, u2 = _rows(gate, "gate"), _rows(up, "up")
+    if g2.stride(0) != u2.stride(0):
+        g2, u2 = g2.contiguous(), u2.contiguous()
+    rows, cols = g2.shape
+    out = torch.empty((rows, cols), dtype=gate.dtype, device=device)
+    rc = nat.load().mi_silu_mul(_ptr(g2), _ptr(u2), g2.stride(0), _ptr(out), cols, rows, cols, dtype_code(gate.dtype),
+                                _stream(device))
+    nat.check(rc, "mi_silu_mul")
+    return out
+
+
 def read_status(device: torch.device | None = None, clear: bool = True) -> int:
     """Device status bits (MI_STATUS_*) recorded since the last clear; synchronises the stream."""
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())

@@ -1,4 +1,4 @@
-"""The C-ABI library loads on a host without a GPU, exports every symbol of include/mi_paged.h,
+"""The C-ABI library loads on a host without a GPU, exports every symbol declared in include/*.h,
 and rejects bad arguments on the host (no device call is made by these checks)."""
 
 import ctypes
@@ -9,11 +9,11 @@ import pytest
 
 from mini_infra_b200 import _native as nat
 
-HEADER = Path(__file__).resolve().parents[1] / "include" / "mi_paged.h"
+HEADERS = sorted((Path(__file__).resolve().parents[1] / "include").glob("*.h"))
 
 
 def declared_symbols():
-    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    text = "".join(re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S) for h in HEADERS)
     return sorted(set(re.findall(r"\b(mi_[a-z0-9_]+)\s*\(", text)))
 
 
