@@ -258,14 +258,24 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeArgs a)
   for (int i = 0; i < PER_LANE; ++i) acc[i] = 0.f;
   float l_all = 0.f;
   if (m_all != -INFINITY) {
-    for (int p = 0; p < n_parts; ++p) {
-      const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + (base + p) * 2);
-      const float w = exp2f(ml.x - m_all);
-      l_all += w * ml.y;
-      const float* src = a.ws_o + (base + p) * D + lane * PER_LANE;
+    // lane j weighs part p0 + j; the O rows of 32 parts are then read with independent loads
+    for (int p0 = 0; p0 < n_parts; p0 += 32) {
+      float w = 0.f;
+      if (p0 + lane < n_parts) {
+        const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + (base + p0 + lane) * 2);
+        w = exp2f(ml.x - m_all);
+        l_all += w * ml.y;
+      }
+      const int cnt = min(32, n_parts - p0);
+#pragma unroll 4
+      for (int j = 0; j < cnt; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        const float* src = a.ws_o + (base + p0 + j) * D + lane * PER_LANE;
 #pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) acc[i] += w * src[i];
+        for (int i = 0; i < PER_LANE; ++i) acc[i] += wj * src[i];
+      }
     }
+    l_all = warp_sum(l_all);
   }
   const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
   T* dst = reinterpret_cast<T*>(a.out + b * a.out_sb) + (int64_t)hq * D + lane * PER_LANE;

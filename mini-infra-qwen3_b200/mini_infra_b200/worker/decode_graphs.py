@@ -97,10 +97,15 @@ class DecodeGraphSet:
             self._graphs[bucket] = g
         return g
 
-    @torch.inference_mode()
     def _capture(self, n: int) -> _Graph:
-        static = torch.zeros(packed_length(n, self.width), dtype=torch.long, device=self.device)
-        static[3 * n : 4 * n] = 1  # padding rows: context length 1 (their own token)
+        # a normal (not inference-mode) tensor: the runner refills it in or out of inference mode
+        with torch.inference_mode(False):
+            static = torch.zeros(packed_length(n, self.width), dtype=torch.long, device=self.device)
+            static[3 * n : 4 * n] = 1  # padding rows: context length 1 (their own token)
+        with torch.inference_mode():
+            return self._record(n, static)
+
+    def _record(self, n: int, static: torch.Tensor) -> _Graph:
         ids, pos, md = self._views(static, n)
         current = torch.cuda.current_stream(self.device)
         side = torch.cuda.Stream(self.device)
