@@ -633,11 +633,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   }
 }
 
-// Merge the split partials of row tiles that needed more than one split: one warp per row.
+// Merge the split partials of row tiles that needed more than one split.  A CTA takes one group
+// of kCombineRows rows of a row tile; each thread merges (row, 16-byte column chunk) items in one
+// online pass over the splits (running max, rescaled sums), so the loads of every split are
+// independent of each other and a warp reads 512 contiguous bytes of one row per split.
+constexpr int kCombineThreads = 128;
+constexpr int kCombineRows = 16;
+
 template <typename T>
-__global__ void __launch_bounds__(128) prefill_combine_kernel(const PrefillArgs a, const float* ws_o,
-                                                              const float* ws_ml, int max_splits) {
-  const int qtile = blockIdx.x;
+__global__ void __launch_bounds__(kCombineThreads) prefill_combine_kernel(const PrefillArgs a, const float* ws_o,
+                                                                          const float* ws_ml, int max_splits) {
+  constexpr int kGroups = kTcRows / kCombineRows;
+  const int qtile = blockIdx.x / kGroups;
+  const int r0 = (blockIdx.x % kGroups) * kCombineRows;
   const int h = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int G = a.groups;
@@ -645,35 +653,39 @@ __global__ void __launch_bounds__(128) prefill_combine_kernel(const PrefillArgs 
   const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
   const TcGeometry geo = tc_geometry(a, b, tok0, tokens_per_tile, false);
   const int n_splits = (geo.n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
-  if (n_splits <= 1) return;
+  if (n_splits <= 1) return;  // uniform for the CTA
   const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t grid_x = (int64_t)gridDim.x * max_splits;
+  const int rows = (int)min((int64_t)kTcRows, (tok_end - tok0) * G);  // valid rows: a prefix of the tile
+  // partial (split s, row r) lives at row (part0 + s) * kTcRows + r
+  const int64_t part0 = (b * a.hkv + h) * ((int64_t)(gridDim.x / kGroups) * max_splits) + (int64_t)qtile * max_splits;
   T* out = reinterpret_cast<T*>(a.out);
-  for (int r = warp; r < kTcRows; r += 4) {
-    const int64_t tok = tok0 + r / G;
-    if (tok >= tok_end) continue;
-    float m_all = -INFINITY;
-    for (int s = 0; s < n_splits; ++s) {
-      const int64_t part = (b * a.hkv + h) * grid_x + (int64_t)qtile * max_splits + s;
-      m_all = fmaxf(m_all, ws_ml[(part * kTcRows + r) * 2]);
-    }
+  constexpr int kChunks = kTcDim / 4;  // float4 chunks of a row
+  for (int item = threadIdx.x; item < kCombineRows * kChunks; item += kCombineThreads) {
+    const int r = r0 + item / kChunks;
+    const int c = item % kChunks;
+    if (r >= rows) break;  // items are row-major: the rest of this thread's items are past the end too
+    float m = -INFINITY, l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float l_all = 0.f;
-    for (int s = 0; s < n_splits; ++s) {
-      const int64_t part = (b * a.hkv + h) * grid_x + (int64_t)qtile * max_splits + s;
-      const float2 ml = *reinterpret_cast<const float2*>(ws_ml + (part * kTcRows + r) * 2);
-      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m_all);
-      l_all += w * ml.y;
-      const float4 o = *reinterpret_cast<const float4*>(ws_o + (part * kTcRows + r) * kTcDim + lane * 4);
-      acc.x += w * o.x;
-      acc.y += w * o.y;
-      acc.z += w * o.z;
-      acc.w += w * o.w;
+#pragma unroll 4
+    for (int sp = 0; sp < n_splits; ++sp) {
+      const int64_t row = (part0 + sp) * kTcRows + r;
+      const float2 ml = *reinterpret_cast<const float2*>(ws_ml + row * 2);
+      const float4 o = *reinterpret_cast<const float4*>(ws_o + row * kTcDim + c * 4);
+      if (ml.x == -INFINITY) continue;  // an empty split contributes nothing
+      const float m_new = fmaxf(m, ml.x);
+      const float alpha = exp2f(m - m_new);  // 0 on the first contribution (m = -inf)
+      const float w = exp2f(ml.x - m_new);
+      l = l * alpha + w * ml.y;
+      acc.x = acc.x * alpha + w * o.x;
+      acc.y = acc.y * alpha + w * o.y;
+      acc.z = acc.z * alpha + w * o.z;
+      acc.w = acc.w * alpha + w * o.w;
+      m = m_new;
     }
-    const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int64_t tok = tok0 + r / G;
     T* dst = out + (b * a.padded_len + geo.first + tok) * (int64_t)(a.hq * kTcDim) +
-             (int64_t)(h * G + r % G) * kTcDim + lane * 4;
+             (int64_t)(h * G + r % G) * kTcDim + c * 4;
     uint2 pk;
     pk.x = pack2<T>(acc.x * inv, acc.y * inv);
     pk.y = pack2<T>(acc.z * inv, acc.w * inv);
@@ -719,8 +731,8 @@ cudaError_t launch_tc(const PrefillArgs& a, float* ws, const PrefillMaps& maps, 
   kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, p.max_splits, log2_if_pow2(a.block_size));
   e = cudaGetLastError();
   if (e != cudaSuccess || p.max_splits == 1) return e;
-  dim3 cgrid((unsigned)p.qtiles, (unsigned)a.hkv, (unsigned)a.batch);
-  prefill_combine_kernel<T><<<cgrid, 128, 0, s>>>(a, ws_o, ws_ml, p.max_splits);
+  dim3 cgrid((unsigned)(p.qtiles * (kTcRows / kCombineRows)), (unsigned)a.hkv, (unsigned)a.batch);
+  prefill_combine_kernel<T><<<cgrid, kCombineThreads, 0, s>>>(a, ws_o, ws_ml, p.max_splits);
   return cudaGetLastError();
 }
 
