@@ -1,24 +1,29 @@
 // Chunked-prefill paged attention on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
 // Variant: bf16 / fp16, head_dim 128, any block size, G = Hq/H_kv in {1, 2, 4, 8}.
-// One CTA (192 threads, two CTAs per SM) = one (sequence, KV head, tile of 128 query rows, KV
-// split).  The 128 rows pack 128/G chunk tokens x G query heads of the KV head (row r = token r/G,
-// head r%G), so the K/V tiles staged in shared memory serve the whole GQA group.  The KV range of
-// a row tile (history tiles, then causal chunk tiles) is cut into splits of kTilesPerSplit
-// 64-position tiles so that long histories spread over many CTAs; a tile with one split writes its
+// One CTA (320 threads, one CTA per SM) = one (sequence, KV head, pair of tiles of 128 query
+// rows, KV split).  A row tile packs 128/G chunk tokens x the G query heads of the KV head (row
+// r = token r/G, head r%G); the CTA's two row tiles are consecutive, so every K/V tile staged in
+// shared memory serves 2 x 128 query rows of the whole GQA group (half the L2 -> SM bytes per
+// FLOP of one row tile per CTA).  The KV range of a row tile (history tiles, then causal chunk
+// tiles) is cut into splits of kTilesPerSplit 64-position tiles so that long histories spread
+// over many CTAs; the two row tiles' ranges differ only in their last chunk tiles, so the CTA
+// stages the union and each row tile uses a prefix of it.  A row tile with one split writes its
 // output directly, otherwise each split writes an unnormalised partial (O, m, l) that
 // prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
-//   warp 0 (loader): Q once, then K and V tiles into two 2-stage rings (K is free once S is done,
-//      V once PV is done).  With tensor maps (block size 16/32/64) the split's block ids are first
-//      resolved into shared memory, then one thread issues TMA copies: one 3D box per pool page of a
-//      history tile (a page past `start` reads rows past the pool, which TMA fills with zeros) and
-//      one 4D box per half of a chunk tile; otherwise the warp stages rows with cp.async;
-//   warp 1 (MMA, one thread): S = Q K^T as 8 tcgen05.mma (M=128, N=64, K=16, kind::f16, fp32
-//      accumulate) into one of two TMEM S buffers (columns [0, 64) / [64, 128)), and O += P V as 4
-//      tcgen05.mma (M=128, N=128, P read from TMEM, V read MN-major) into TMEM columns [128, 256),
+//   warp 0 (loader): both Q tiles once, then K and V tiles into two kStages-deep rings (K is free
+//      once the S of both row tiles is done, V once both PVs are done).  With tensor maps (block
+//      size 16/32/64) the split's block ids are first resolved into shared memory, then one thread
+//      issues TMA copies: one 3D box per pool page of a history tile (a page past `start` reads
+//      rows past the pool, which TMA fills with zeros) and one 4D box per half of a chunk tile;
+//      otherwise the warp stages rows with cp.async;
+//   warp 1 (MMA, one thread): per row tile g, S = Q_g K^T as 8 tcgen05.mma (M=128, N=64, K=16,
+//      kind::f16, fp32 accumulate) into one of g's two TMEM S buffers, and O_g += P V as 4
+//      tcgen05.mma (M=128, N=128, P read from TMEM, V read MN-major) into g's TMEM O columns,
 //      issued in readiness order so S(i+1) runs under softmax(i); tcgen05.commit signals mbarriers;
-//   warps 2-5 (softmax): each thread owns one row (its TMEM lane): one tcgen05.ld of the row's 64
-//      scores, causal / length mask (set to -inf) only on tiles that cross a row's causal end or
+//   warps 2-5 / 6-9 (softmax of row tile 0 / 1): each thread owns one row (its TMEM lane): one
+//      tcgen05.ld of the row's 64 scores, causal / length mask (set to -inf) only on tiles that
+//      cross a row's causal end or
 //      the history end, online softmax in the exp2 domain; the running O in TMEM is rescaled
 //      (tcgen05.ld/st, warp-wide) only when a row maximum grew by more than 2^8 since its last
 //      rescale (p <= 2^8 stays exact in fp32 and the final 1/l absorbs it); P is written back with
@@ -42,27 +47,30 @@
 namespace mi {
 namespace {
 
-constexpr int kTcRows = 128;                        // query rows per CTA (MMA M)
+constexpr int kTcRows = 128;                        // query rows per row tile (MMA M)
+constexpr int kPair = 2;                            // row tiles per CTA, sharing every K/V tile
 constexpr int kTcKv = 64;                           // KV positions per tile
 constexpr int kTcDim = 128;                         // head_dim
-constexpr int kTcThreads = 192;                    // warp 0 loader, warp 1 MMA, warps 2-5 softmax
+constexpr int kSoftmaxThreads = 128;                // one warpgroup per row tile
+constexpr int kTcThreads = 64 + kPair * kSoftmaxThreads;  // warp 0 loader, warp 1 MMA, then the warpgroups
 constexpr int kLoaderWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kLoaderThreads = 32;
-constexpr int kSoftmaxThreads = 128;
 constexpr int kTilesPerSplit = 32;                  // 2048 KV positions per CTA at most
-constexpr int kQRegion = kTcRows * 128;             // 16 KiB: one 64-column half of Q
+constexpr int kStages = 4;                          // depth of the K ring and of the V ring
+constexpr int kQRegion = kTcRows * 128;             // 16 KiB: one 64-column half of a Q tile
 constexpr int kKvRegion = kTcKv * 128;              // 8 KiB: one 64-column half of a K or V tile
-constexpr int kQBytes = 2 * kQRegion;               // 32 KiB
-constexpr int kKvBytes = 2 * kKvRegion;             // 16 KiB (also holds P: 128 rows x 64 columns)
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;              // two buffers
-constexpr int kOffV = kOffK + 2 * kKvBytes;         // two buffers
-constexpr int kOffBar = kOffV + 2 * kKvBytes;
-constexpr int kOffPages = kOffBar + 128;             // 65 block ids of the tile being loaded
-constexpr int kTcSmemBytes = kOffPages + 65 * 8 + 1024;  // + alignment slack (~98 KiB)
-constexpr uint32_t kTmemCols = 256;                 // S tiles: [0, 64) and [64, 128); O: [128, 256)
-constexpr uint32_t kTmemO = 128;
+constexpr int kQBytes = 2 * kQRegion;               // 32 KiB per row tile
+constexpr int kKvBytes = 2 * kKvRegion;             // 16 KiB
+constexpr int kOffQ = 0;                            // kPair Q tiles
+constexpr int kOffK = kOffQ + kPair * kQBytes;      // kStages K buffers
+constexpr int kOffV = kOffK + kStages * kKvBytes;   // kStages V buffers
+constexpr int kOffBar = kOffV + kStages * kKvBytes;
+constexpr int kOffPages = kOffBar + 256;            // block ids (cp.async: 65 int64 of one tile; TMA: 128 int32)
+constexpr int kTcSmemBytes = kOffPages + 65 * 8 + 1024;  // + alignment slack (~194 KiB: one CTA per SM)
+// TMEM (512 columns): S buffers of row tile g at g*128 + {0, 64}; O of row tile g at 256 + g*128.
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = 256;
 constexpr float kRescaleLog2 = 8.0f;
 
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t unit16, uint32_t region) {
@@ -83,23 +91,55 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, bool b_mn_major, int
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
+// The tcgen05 / TMA issue helpers below are executed by a whole converged warp (so their operands
+// are warp-uniform and live in uniform registers); the lane chosen by elect.sync issues.
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 // Same, with A (M=128 rows x 16 K elements, two 16-bit values per 32-bit column) read from TMEM.
 __device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
                                                 uint32_t acc) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
       "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_e(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];\n\t}" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_e(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                              int c3) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];\n\t}" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx_e(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(smem_u32(bar)), "r"(bytes)
+      : "memory");
+}
+// Bounded wait by a whole warp; leaves the warp converged with a warp-uniform `aborted`.
+__device__ __forceinline__ void mbar_wait_warp(uint64_t* bar, uint32_t parity, bool& aborted) {
+  mbar_wait(bar, parity, aborted);
+  aborted = __any_sync(0xffffffffu, aborted);
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -281,27 +321,27 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 template <typename T, bool kTma>
-__global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const PrefillArgs a,
+__global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const PrefillArgs a,
                                                                     const __grid_constant__ PrefillMaps maps,
                                                                     float* ws_o, float* ws_ml, int max_splits,
-                                                                    int shift) {
+                                                                    int qtiles, int shift) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2] loader -> MMA: K stage landed
-  uint64_t* k_empty = bars + 3;   // [2] MMA -> loader: S of the stage done (K free)
-  uint64_t* v_full = bars + 5;    // [2] loader -> MMA: V stage landed
-  uint64_t* v_empty = bars + 7;   // [2] MMA -> loader: PV of the stage done (V free)
-  uint64_t* s_full = bars + 9;    // [2] MMA -> softmax: S tile ready
-  uint64_t* p_full = bars + 11;   // [2] softmax -> MMA: P written into TMEM (and S consumed)
-  uint64_t* o_done = bars + 13;   // MMA -> softmax: one phase per PV (rescale waits)
-  uint64_t* o_final = bars + 14;  // MMA -> softmax: the last PV is done (epilogue)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* q_full = bars + 0;                    // loader -> MMA: both Q tiles landed
+  uint64_t* k_full = bars + 1;                    // [kStages] loader -> MMA: K stage landed
+  uint64_t* k_empty = k_full + kStages;           // [kStages] MMA -> loader: the S of the stage done
+  uint64_t* v_full = k_empty + kStages;           // [kStages] loader -> MMA: V stage landed
+  uint64_t* v_empty = v_full + kStages;           // [kStages] MMA -> loader: the PVs of the stage done
+  uint64_t* s_full = v_empty + kStages;           // [kPair][2] MMA -> softmax g: S tile ready
+  uint64_t* p_full = s_full + 2 * kPair;          // [kPair][2] softmax g -> MMA: P written into TMEM
+  uint64_t* o_done = p_full + 2 * kPair;          // [kPair] MMA -> softmax g: one phase per PV
+  uint64_t* o_final = o_done + kPair;             // [kPair] MMA -> softmax g: its last PV is done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + kPair);
   int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async loader: block ids of one tile
 
-  const int qtile = blockIdx.x / max_splits;
+  const int pair = blockIdx.x / max_splits;
   const int split = blockIdx.x % max_splits;
   const int h = blockIdx.y;
   const int64_t b = blockIdx.z;
@@ -310,14 +350,26 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
-  const TcGeometry geo = tc_geometry(a, b, tok0, tokens_per_tile, tid == 0 && blockIdx.x == 0 && h == 0);
+  // row tile g of this CTA = q-tile 2*pair + g; both share the row's history and chunk geometry
+  int64_t tok0[kPair], tok_end[kPair];
+  int n_tiles[kPair], ng[kPair];
+  TcGeometry geo{};
+  const int t_begin = split * kTilesPerSplit;
+#pragma unroll
+  for (int g = 0; g < kPair; ++g) {
+    tok0[g] = (int64_t)(pair * kPair + g) * tokens_per_tile;
+    geo = tc_geometry(a, b, tok0[g], tokens_per_tile, g == 0 && tid == 0 && blockIdx.x == 0 && h == 0);
+    n_tiles[g] = geo.n_tiles;
+    tok_end[g] = min(geo.len, tok0[g] + tokens_per_tile);
+    ng[g] = max(0, min(n_tiles[g], t_begin + kTilesPerSplit) - t_begin);  // this split's tiles of row tile g
+  }
   const int64_t first = geo.first;
   const int start = geo.start;
+  const int hist_tiles = geo.hist_tiles;
   const int row_elems = a.hq * kTcDim;  // elements per output position
   T* out = reinterpret_cast<T*>(a.out);
 
-  // Padding positions of this KV head's query heads are zeros (written by tile 0, split 0).
+  // Padding positions of this KV head's query heads are zeros (written by pair 0, split 0).
   if (blockIdx.x == 0) {
     const int per_pos = G * (kTcDim / 8);
     for (int64_t i = tid; i < first * per_pos; i += kTcThreads) {
@@ -327,26 +379,26 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
           make_uint4(0, 0, 0, 0);
     }
   }
-  const int t_begin = split * kTilesPerSplit;
-  if (t_begin >= geo.n_tiles) return;  // uniform for the CTA
-  const int t_end = min(geo.n_tiles, t_begin + kTilesPerSplit);
-  const int n = t_end - t_begin;
-  const int n_splits = (geo.n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
-  const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
-  const int hist_tiles = geo.hist_tiles;
+  const int n = max(ng[0], ng[1]);  // tiles staged: the union (a prefix of this split's tiles for each g)
+  if (n == 0) return;               // uniform for the CTA
+  const int t_end = t_begin + n;
 
   if (tid == 0) {
     mbar_init(q_full, kTma ? 1 : kLoaderThreads);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&k_full[i], kTma ? 1 : kLoaderThreads);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], kTma ? 1 : kLoaderThreads);
       mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2 * kPair; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], kSoftmaxThreads);
     }
-    mbar_init(o_done, 1);
-    mbar_init(o_final, 1);
+    for (int g = 0; g < kPair; ++g) {
+      mbar_init(&o_done[g], 1);
+      mbar_init(&o_final[g], 1);
+    }
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -361,9 +413,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
   bool aborted = false;
 
   if (warp == kLoaderWarp) {
-    // ---------------- loader: Q once, then K and V tiles into two 2-stage rings ----------------
-    // Order K0 K1 V0 K2 V1 K3 ...: K(i+2) waits for S(i), V(i) for PV(i-2), and the MMA thread
-    // issues ... PV(i-2) S(i) PV(i-1) S(i+1) ..., so each wait ends in the order the loads are issued.
+    // ---------------- loader: both Q tiles once, then K and V tiles into two kStages rings --------
+    // K(i) reuses the stage of tile i-S once its S is done, V(i) that of tile i-S once its PVs
+    // are.  The TMA thread polls both rings; the cp.async warp loads K0 .. K(S-1), then V(i),
+    // K(i+S) for i = 0, 1, ...: the MMA thread issues the PVs of tile i-S before the S of tile i
+    // (S(i) needs PV(i-2) issued), so each blocking wait ends in the order the loads are issued.
     if constexpr (kTma) {
       // Block ids of the split's history pages, resolved once: the pool row of each page's first
       // slot, or a row past the pool for a page at or past `start` (TMA fills it with zeros).
@@ -383,138 +437,157 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
         page_rows[j] = row0;
       }
       __syncwarp();
+      // the whole warp runs the issue loop; elected lanes issue the copies
       if (lane == 0) {
         tma_prefetch_desc(&maps.q);
         tma_prefetch_desc(&maps.k_chunk);
         tma_prefetch_desc(&maps.v_chunk);
-        mbar_arrive_expect_tx(q_full, kQBytes);
-        for (int c = 0; c < 2; ++c)  // box [64 d, G heads, 128/G tokens]: row = token * G + head
-          tma_load_4d(smem + kOffQ + c * kQRegion, &maps.q, q_full, c * 64, h * G, (int)(first + tok0), (int)b);
-        const int page_bytes = a.block_size * 128;
-        auto load = [&](int i, bool is_v) {
-          const int st = i & 1;
-          uint64_t* full = is_v ? &v_full[st] : &k_full[st];
-          if (i >= 2) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i - 2) >> 1) & 1, aborted);
-          uint8_t* dst = smem + (is_v ? kOffV : kOffK) + st * kKvBytes;
-          mbar_arrive_expect_tx(full, kKvBytes);
-          const int t = t_begin + i;
-          if (t < hist_tiles) {
-            const CUtensorMap* map = is_v ? &maps.v_pool : &maps.k_pool;
-            for (int pg = 0; pg < pages_per_tile; ++pg) {
-              const int row0 = page_rows[i * pages_per_tile + pg];
-              for (int c = 0; c < 2; ++c) tma_load_3d(dst + c * kKvRegion + pg * page_bytes, map, full, c * 64, h, row0);
-            }
-          } else {
-            const CUtensorMap* map = is_v ? &maps.v_chunk : &maps.k_chunk;
-            const int pos = (int)first + (t - hist_tiles) * kTcKv;
-            for (int c = 0; c < 2; ++c) tma_load_4d(dst + c * kKvRegion, map, full, c * 64, h, pos, (int)b);
+      }
+      __syncwarp();
+      mbar_expect_tx_e(q_full, kPair * kQBytes);
+      for (int g = 0; g < kPair; ++g)  // box [64 d, G heads, 128/G tokens]: row = token * G + head
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d_e(smem + kOffQ + g * kQBytes + c * kQRegion, &maps.q, q_full, c * 64, h * G,
+                        (int)(first + tok0[g]), (int)b);
+      const int page_bytes = a.block_size * 128;
+      auto load = [&](int i, bool is_v) {
+        const int st = i % kStages;
+        uint64_t* full = is_v ? &v_full[st] : &k_full[st];
+        uint8_t* dst = smem + (is_v ? kOffV : kOffK) + st * kKvBytes;
+        mbar_expect_tx_e(full, kKvBytes);
+        const int t = t_begin + i;
+        if (t < hist_tiles) {
+          const CUtensorMap* map = is_v ? &maps.v_pool : &maps.k_pool;
+          for (int pg = 0; pg < pages_per_tile; ++pg) {
+            const int row0 = page_rows[i * pages_per_tile + pg];
+            for (int c = 0; c < 2; ++c) tma_load_3d_e(dst + c * kKvRegion + pg * page_bytes, map, full, c * 64, h, row0);
           }
-        };
-        load(0, false);
-        if (n > 1) load(1, false);
-        for (int i = 0; i < n; ++i) {
-          load(i, true);
-          if (i + 2 < n) load(i + 2, false);
+        } else {
+          const CUtensorMap* map = is_v ? &maps.v_chunk : &maps.k_chunk;
+          const int pos = (int)first + (t - hist_tiles) * kTcKv;
+          for (int c = 0; c < 2; ++c) tma_load_4d_e(dst + c * kKvRegion, map, full, c * 64, h, pos, (int)b);
+        }
+      };
+      for (int i = 0; i < min(n, kStages); ++i) load(i, false);
+      for (int i = 0; i < n; ++i) {
+        if (i >= kStages) mbar_wait_warp(&v_empty[i % kStages], ((i / kStages) - 1) & 1, aborted);
+        load(i, true);
+        if (i + kStages < n) {
+          mbar_wait_warp(&k_empty[i % kStages], (i / kStages) & 1, aborted);  // S(i) done
+          load(i + kStages, false);
         }
       }
     } else {
       const BlockAddr ba{shift, (uint32_t)a.block_size};
       const int unit = lane & 15;
-      for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
-        const int64_t tok = tok0 + r / G;
-        const bool valid = tok < tok_end;
-        const char* src = a.q;
-        if (valid)
-          src = a.q + b * a.q_sb[0] + (first + tok) * a.q_sb[1] + (int64_t)(h * G + r % G) * a.q_sb[2] + unit * 16;
-        cp_async16(sbase + kOffQ + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
+      for (int g = 0; g < kPair; ++g) {
+        for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
+          const int64_t tok = tok0[g] + r / G;
+          const bool valid = tok < tok_end[g];
+          const char* src = a.q;
+          if (valid)
+            src = a.q + b * a.q_sb[0] + (first + tok) * a.q_sb[1] + (int64_t)(h * G + r % G) * a.q_sb[2] + unit * 16;
+          cp_async16(sbase + kOffQ + g * kQBytes + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
+        }
       }
       cp_async_arrive_noinc(q_full);
+      const int rows_end = (int)tok_end[kPair - 1] > (int)tok_end[0] ? (int)tok_end[kPair - 1] : (int)tok_end[0];
       auto load = [&](int i, bool is_v) {
-        const int st = i & 1;
-        if (i >= 2) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i - 2) >> 1) & 1, aborted);
+        const int st = i % kStages;
+        if (i >= kStages) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i / kStages) - 1) & 1, aborted);
         const int t = t_begin + i;
         const uint32_t dst = sbase + (is_v ? kOffV : kOffK) + st * kKvBytes;
         if (t < hist_tiles) stage_hist_cp<T>(a, ba, b, h, start, t, is_v ? a.v_pool : a.k_pool, dst, lane, pages);
-        else stage_chunk_cp(a, b, h, first, t - hist_tiles, (int)tok_end, is_v ? a.v_chunk : a.k_chunk, dst, lane);
+        else stage_chunk_cp(a, b, h, first, t - hist_tiles, rows_end, is_v ? a.v_chunk : a.k_chunk, dst, lane);
         cp_async_arrive_noinc(is_v ? &v_full[st] : &k_full[st]);
       };
-      load(0, false);
-      if (n > 1) load(1, false);
+      for (int i = 0; i < min(n, kStages); ++i) load(i, false);
       for (int i = 0; i < n; ++i) {
         load(i, true);
-        if (i + 2 < n) load(i + 2, false);
+        if (i + kStages < n) load(i + kStages, false);
       }
     }
   } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer: S and PV in readiness order ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer: S and PV of both row tiles in readiness order ------
+    // The whole warp runs the loop (warp-uniform control flow); elected lanes issue.
+    {
       constexpr bool kBf16 = !std::is_same<T, __half>::value;
       const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
       const uint32_t idesc_pv = idesc_f16(kBf16, true, kTcRows, kTcDim);
-      const uint32_t q0 = sbase + kOffQ;
-      auto issue_s = [&](int i) {
-        const int st = i & 1;
+      int npv[kPair] = {0, 0};  // PVs issued per row tile
+      // Shared-memory descriptors: the start-address field holds address >> 4 (14 bits, every
+      // address here is below 256 KiB), so the descriptor of base + off is desc(base) + off / 16.
+      const uint64_t dq = desc_kmajor(sbase + kOffQ);
+      const uint64_t dk = desc_kmajor(sbase + kOffK);
+      const uint64_t dv = desc_mnmajor(sbase + kOffV);
+      auto issue_s = [&](int i) {  // S of tile i for every row tile that has it
+        const int ks = i % kStages;
         fence_async_smem();
         tc_fence_after();
-        const uint32_t kb = sbase + kOffK + st * kKvBytes;
+        const uint64_t dks = dk + (uint64_t)(ks * (kKvBytes >> 4));
+        const uint32_t s_col = (uint32_t)(i & 1) * kTcKv;
 #pragma unroll
-        for (int s = 0; s < kTcDim / 16; ++s)
-          umma_f16(tmem + st * kTcKv, desc_kmajor(q0 + (s >> 2) * kQRegion + (s & 3) * 32),
-                   desc_kmajor(kb + (s >> 2) * kKvRegion + (s & 3) * 32), idesc_qk, s > 0 ? 1u : 0u);
-        umma_commit(&k_empty[st]);
-        umma_commit(&s_full[st]);
+        for (int g = 0; g < kPair; ++g) {
+          if (i >= ng[g]) continue;
+#pragma unroll
+          for (int s = 0; s < kTcDim / 16; ++s)
+            umma_f16(tmem + g * 128 + s_col, dq + (uint64_t)((g * kQBytes + (s >> 2) * kQRegion + (s & 3) * 32) >> 4),
+                     dks + (uint64_t)(((s >> 2) * kKvRegion + (s & 3) * 32) >> 4), idesc_qk, s > 0 ? 1u : 0u);
+          umma_commit(&s_full[g * 2 + (i & 1)]);
+        }
+        umma_commit(&k_empty[ks]);
       };
-      auto issue_pv = [&](int i) {
-        const int st = i & 1;
-        fence_async_smem();
+      auto issue_pv = [&](int g, int i) {
+        const int vs = i % kStages;
         tc_fence_after();
-        const uint32_t vb = sbase + kOffV + st * kKvBytes;
+        const uint64_t dvs = dv + (uint64_t)(vs * (kKvBytes >> 4));
+        const uint32_t p_col = tmem + g * 128 + (uint32_t)(i & 1) * kTcKv;
 #pragma unroll
         for (int s = 0; s < kTcKv / 16; ++s)  // P(i): 16-bit pairs in the S buffer's first 32 columns
-          umma_f16_tmem_a(tmem + kTmemO, tmem + st * kTcKv + s * 8, desc_mnmajor(vb + s * 2048), idesc_pv,
+          umma_f16_tmem_a(tmem + kTmemO + g * 128, p_col + s * 8, dvs + (uint64_t)((s * 2048) >> 4), idesc_pv,
                           (i > 0 || s > 0) ? 1u : 0u);
-        umma_commit(&v_empty[st]);
-        umma_commit(o_done);
+        umma_commit(&o_done[g]);
+        ++npv[g];
+        const int o = 1 - g;  // V(i) is free once every row tile that uses tile i has issued its PV
+        if (npv[o] > i || i >= ng[o]) umma_commit(&v_empty[vs]);
+        if (npv[g] == ng[g]) umma_commit(&o_final[g]);
       };
-      mbar_wait(q_full, 0, aborted);
-      // S(ns) as soon as its tile landed and its TMEM buffer is free (softmax(ns-2) done, i.e.
-      // ns <= npv + 1); PV(npv) as soon as P(npv) is written; whichever is ready first.
-      int ns = 0, npv = 0;
-      uint64_t t_last = globaltimer_ns();
-      while (npv < n) {
-        bool progressed = false;
-        if (ns < n && ns <= npv + 1 && mbar_test_wait(&k_full[ns & 1], (ns >> 1) & 1)) {
-          issue_s(ns++);
-          progressed = true;
+      // Fixed order S(i+1), PV_0(i), PV_1(i): S(i+1) needs the S buffers of tile i-1, whose PVs
+      // were issued in the previous step, so only the PVs wait (for softmax); the waits suspend
+      // the warp instead of spinning.
+      mbar_wait_warp(q_full, 0, aborted);
+      mbar_wait_warp(&k_full[0], 0, aborted);
+      issue_s(0);
+      for (int i = 0; i < n; ++i) {
+        if (i + 1 < n) {
+          mbar_wait_warp(&k_full[(i + 1) % kStages], ((i + 1) / kStages) & 1, aborted);
+          issue_s(i + 1);
         }
-        if (npv < ns && mbar_test_wait(&p_full[npv & 1], (npv >> 1) & 1) &&
-            mbar_test_wait(&v_full[npv & 1], (npv >> 1) & 1)) {
-          issue_pv(npv++);
-          progressed = true;
-        }
-        if (progressed) {
-          t_last = globaltimer_ns();
-        } else if (!aborted && globaltimer_ns() - t_last > kWaitLimitNs) {
-          record_status(MI_STATUS_TIMEOUT);
-          aborted = true;
-        }
-        if (aborted && !progressed) {  // give up: let the other roles time out and finish
-          if (ns < n && ns <= npv + 1) issue_s(ns++);
-          else issue_pv(npv++);
+#pragma unroll
+        for (int g = 0; g < kPair; ++g) {
+          if (i >= ng[g]) continue;
+          mbar_wait_warp(&p_full[g * 2 + (i & 1)], (i >> 1) & 1, aborted);
+          mbar_wait_warp(&v_full[i % kStages], (i / kStages) & 1, aborted);
+          issue_pv(g, i);
         }
       }
-      umma_commit(o_final);
     }
   } else {
-    // ---------------- softmax warpgroup: thread <-> row <-> TMEM lane ----------------
+    // ---------------- softmax warpgroup g: thread <-> row <-> TMEM lane ----------------
+    const int g = (warp - 2) / 4;
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
     const int r = quad * 32 + lane;            // row of the tile
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    const int64_t my_tok = tok0 + r / G;
-    const bool row_valid = my_tok < tok_end;
+    const int64_t my_tok0 = g == 0 ? tok0[0] : tok0[1];
+    const int64_t my_tok = my_tok0 + r / G;
+    const bool row_valid = my_tok < (g == 0 ? tok_end[0] : tok_end[1]);
+    const int my_n = g == 0 ? ng[0] : ng[1];
+    const int my_n_tiles = g == 0 ? n_tiles[0] : n_tiles[1];
+    const uint32_t s_col = (uint32_t)g * 128;
+    const uint32_t o_col = kTmemO + (uint32_t)g * 128;
     const float scale = a.scale_log2;
     float m_ref = -INFINITY, l_run = 0.f;
-    for (int i = 0; i < n; ++i) {
+    for (int i = 0; i < my_n; ++i) {
       const int st = i & 1;
       const int t = t_begin + i;
       // visible columns of this tile: history keys below `start`; chunk keys up to the row's token
@@ -526,16 +599,16 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       } else {
         const int k0 = (t - hist_tiles) * kTcKv;
         lim = row_valid ? (int)my_tok + 1 - k0 : 0;
-        full = k0 + kTcKv <= (int)tok0 + 1;
+        full = k0 + kTcKv <= (int)my_tok0 + 1;
       }
-      mbar_wait(&s_full[st], (i >> 1) & 1, aborted);
+      mbar_wait(&s_full[g * 2 + st], (i >> 1) & 1, aborted);
       tc_fence_after();
-      const uint32_t s_addr = tmem + st * kTcKv + lane_base;
+      const uint32_t s_addr = tmem + s_col + st * kTcKv + lane_base;
       uint32_t sr[2][32];
       tmem_ld32_async(s_addr, sr[0]);
       tmem_ld32_async(s_addr + 32, sr[1]);
       tmem_wait_ld();
-      if (!full) {  // uniform for the CTA: only tiles that cross a causal or history end are masked
+      if (!full) {  // uniform for the warpgroup: only tiles that cross a causal or history end are masked
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
 #pragma unroll
@@ -553,16 +626,16 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       const float m_new = fmaxf(m_ref, tile_max);
       const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
       if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access
-        mbar_wait(o_done, (i - 1) & 1, aborted);  // PV(i-1) finished writing O
+        mbar_wait(&o_done[g], (i - 1) & 1, aborted);  // PV(i-1) of this row tile finished writing O
         tc_fence_after();
         const float alpha = need ? fast_exp2(m_ref - m_new) : 1.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float ov[32];
-          tmem_ld32(tmem + kTmemO + lane_base + c * 32, ov);
+          tmem_ld32(tmem + o_col + lane_base + c * 32, ov);
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-          tmem_st32(tmem + kTmemO + lane_base + c * 32, ov);
+          tmem_st32(tmem + o_col + lane_base + c * 32, ov);
         }
       }
       if (need) {
@@ -587,42 +660,47 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_tc_kernel(const Prefill
       // registers already; S(i+2) overwrites them only after PV(i), issued before it, has read them)
       tmem_st32(s_addr, pw);
       tc_fence_before();  // our tcgen05.ld of S / st of P and O before the next MMAs
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(&p_full[g * 2 + st]);
     }
-    // ---- epilogue ----
-    mbar_wait(o_final, 0, aborted);
-    tc_fence_after();
-    if (n_splits == 1) {
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T* dst = out + (b * a.padded_len + first + my_tok) * row_elems + (int64_t)(h * G + r % G) * kTcDim;
+    // ---- epilogue (a row tile without tiles in this split writes nothing here) ----
+    if (my_n > 0) {
+      mbar_wait(&o_final[g], 0, aborted);
+      tc_fence_after();
+      const int n_splits = (my_n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
+      if (n_splits == 1) {
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        T* dst = out + (b * a.padded_len + first + my_tok) * row_elems + (int64_t)(h * G + r % G) * kTcDim;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        tmem_ld32(tmem + kTmemO + lane_base + c * 32, ov);
-        if (row_valid) {
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tmem + o_col + lane_base + c * 32, ov);
+          if (row_valid) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint4 pk;
-            pk.x = pack2<T>(ov[u * 8 + 0] * inv, ov[u * 8 + 1] * inv);
-            pk.y = pack2<T>(ov[u * 8 + 2] * inv, ov[u * 8 + 3] * inv);
-            pk.z = pack2<T>(ov[u * 8 + 4] * inv, ov[u * 8 + 5] * inv);
-            pk.w = pack2<T>(ov[u * 8 + 6] * inv, ov[u * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pk;
+            for (int u = 0; u < 4; ++u) {
+              uint4 pk;
+              pk.x = pack2<T>(ov[u * 8 + 0] * inv, ov[u * 8 + 1] * inv);
+              pk.y = pack2<T>(ov[u * 8 + 2] * inv, ov[u * 8 + 3] * inv);
+              pk.z = pack2<T>(ov[u * 8 + 4] * inv, ov[u * 8 + 5] * inv);
+              pk.w = pack2<T>(ov[u * 8 + 6] * inv, ov[u * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pk;
+            }
           }
         }
-      }
-    } else {
-      const int64_t part = ((b * a.hkv + h) * gridDim.x + blockIdx.x);
-      float* po = ws_o + (part * kTcRows + r) * kTcDim;
+      } else {
+        const int qt = pair * kPair + g;
+        const int64_t part = (b * a.hkv + h) * ((int64_t)qtiles * max_splits) + (int64_t)qt * max_splits + split;
+        float* po = ws_o + (part * kTcRows + r) * kTcDim;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float ov[32];
-        tmem_ld32(tmem + kTmemO + lane_base + c * 32, ov);
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(tmem + o_col + lane_base + c * 32, ov);
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<float4*>(po + c * 32 + u * 4) = make_float4(ov[u * 4], ov[u * 4 + 1], ov[u * 4 + 2], ov[u * 4 + 3]);
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(po + c * 32 + u * 4) =
+                make_float4(ov[u * 4], ov[u * 4 + 1], ov[u * 4 + 2], ov[u * 4 + 3]);
+        }
+        *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_run);
       }
-      *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_run);
     }
     tc_fence_before();
   }
@@ -727,8 +805,10 @@ cudaError_t launch_tc(const PrefillArgs& a, float* ws, const PrefillMaps& maps, 
   float* ws_o = ws;
   float* ws_ml = ws ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ((p.ws_o_bytes + 255) & ~size_t(255)))
                     : nullptr;
-  dim3 grid((unsigned)(p.qtiles * p.max_splits), (unsigned)a.hkv, (unsigned)a.batch);
-  kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, p.max_splits, log2_if_pow2(a.block_size));
+  const int64_t pairs = (p.qtiles + kPair - 1) / kPair;
+  dim3 grid((unsigned)(pairs * p.max_splits), (unsigned)a.hkv, (unsigned)a.batch);
+  kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, p.max_splits, (int)p.qtiles,
+                                              log2_if_pow2(a.block_size));
   e = cudaGetLastError();
   if (e != cudaSuccess || p.max_splits == 1) return e;
   dim3 cgrid((unsigned)(p.qtiles * (kTcRows / kCombineRows)), (unsigned)a.hkv, (unsigned)a.batch);

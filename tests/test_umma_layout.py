@@ -104,7 +104,28 @@ def test_pv_operands_read_what_the_writer_stored():
                 assert base_v <= a < base_v + 2 * KV_REGION
 
 
-def test_smem_budget_two_ctas_per_sm():
-    per_cta = 2 * Q_REGION + 2 * (2 * KV_REGION) + 2 * (2 * KV_REGION) + 128 + 65 * 8 + 1024  # + barriers, page ids
+PAIR, STAGES = 2, 4  # row tiles per CTA; depth of the K and of the V ring
+
+
+def test_smem_budget_one_cta_per_sm():
+    q = PAIR * 2 * Q_REGION
+    kv = 2 * STAGES * (2 * KV_REGION)
+    per_cta = q + kv + 256 + 65 * 8 + 1024  # + barriers, page ids, alignment slack
     assert per_cta <= 227 * 1024
-    assert 2 * (per_cta + 1024) <= 228 * 1024  # two CTAs (+1 KiB reserved each) share an SM
+    assert 2 * (per_cta + 1024) > 228 * 1024  # never two CTAs on one SM: each allocates all 512 TMEM columns
+    barriers = 1 + 4 * STAGES + 2 * PAIR * 2 + 2 * PAIR
+    assert barriers * 8 + 4 <= 256
+
+
+def test_tmem_columns():
+    s_cols = [(g * 128 + st * 64, g * 128 + st * 64 + 64) for g in range(PAIR) for st in range(2)]
+    o_cols = [(256 + g * 128, 256 + g * 128 + 128) for g in range(PAIR)]
+    spans = sorted(s_cols + o_cols)
+    assert spans[0][0] == 0 and spans[-1][1] == 512
+    assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))  # disjoint
+    # P(i) of row tile g: 32 columns (64 16-bit values per row) at the start of its S buffer; the
+    # 4 PV k-steps read 8 columns each
+    for g in range(PAIR):
+        for st in range(2):
+            lo = g * 128 + st * 64
+            assert all(lo <= lo + ks * 8 and lo + ks * 8 + 8 <= lo + 32 for ks in range(4))
