@@ -61,6 +61,21 @@ def slot_for_position(block_table: Sequence[int], position: int, block_size: int
     return int(block_table[position // block_size]) * block_size + position % block_size
 
 
+def duplicate_slots(slot_mapping: Sequence[int]) -> list[int]:
+    """Host-side duplicate-slot detector: the slots written more than once by one scatter.
+
+    A scatter (``index_copy_`` in the reference, ``worker/paged_kv_cache.py:74-95``; one thread
+    per token here) writing two tokens to one slot leaves whichever lands last — the reference
+    and the kernels may keep different ones.  Live block tables never share a block, so a correct
+    control plane never produces one; the tests run every slot mapping they build through this."""
+    seen: set[int] = set()
+    dup: set[int] = set()
+    for s in slot_mapping:
+        s = int(s)
+        (dup if s in seen else seen).add(s)
+    return sorted(dup)
+
+
 def prefill_index(
     block_tables: Sequence[Sequence[int]],
     chunk_lens: Sequence[int],

@@ -1,5 +1,7 @@
 """Block manager behaviour the paged kernels rely on (CPU, no torch)."""
 
+import random
+
 import pytest
 
 from mini_infra_b200.core import (
@@ -53,3 +55,42 @@ def test_free_returns_whole_table():
     m.allocate_slots(7, 3)
     m.free(7)
     assert m.num_used_blocks == 0 and m.block_release_count == 3
+
+
+def test_live_tables_never_share_a_block_so_slots_are_unique():
+    """Random admit / grow / free traffic: live block tables stay disjoint and null-free, so the
+    slots of all live positions (what one step's scatter writes) have no duplicates."""
+    from oracle.paged_oracle import duplicate_slots, slot_for_position
+
+    rng = random.Random(7)
+    bs = 4
+    m = KVCacheManager(block_size=bs, num_blocks=40)
+    lengths: dict[int, int] = {}
+    for step in range(400):
+        op = rng.random()
+        if op < 0.4 and len(lengths) < 12:
+            rid = step
+            n = rng.randint(1, 20)
+            if m.allocate_slots(rid, n):
+                lengths[rid] = n
+        elif op < 0.8 and lengths:
+            rid = rng.choice(sorted(lengths))
+            if m.allocate_slots(rid, 1):
+                lengths[rid] += 1
+        elif lengths:
+            rid = rng.choice(sorted(lengths))
+            m.free(rid)
+            del lengths[rid]
+        tables = {rid: m.block_table(rid) for rid in lengths}
+        blocks = [b for t in tables.values() for b in t]
+        assert NULL_BLOCK_ID not in blocks
+        assert len(blocks) == len(set(blocks)) == m.num_used_blocks
+        slots = [slot_for_position(tables[rid], p, bs) for rid, n in lengths.items() for p in range(n)]
+        assert duplicate_slots(slots) == []
+
+
+def test_duplicate_slot_detector_flags_a_planted_duplicate():
+    from oracle.paged_oracle import duplicate_slots
+
+    assert duplicate_slots([5, 9, 17, 4]) == []
+    assert duplicate_slots([5, 9, 5, 4, 9, 9]) == [5, 9]

@@ -78,6 +78,7 @@ def _random_case(b, hq, h, d, bs, max_ctx, dtype, seed, min_ctx=1):
         cur += n
     pos = ctx - 1
     slots = np.asarray([tables[i, p // bs] * bs + p % bs for i, p in enumerate(pos)], dtype=np.int64)
+    assert po.duplicate_slots(slots) == []  # disjoint tables: one appended token per slot
 
     def vals(shape):
         x = rng.standard_normal(size=shape).astype(np.float32)

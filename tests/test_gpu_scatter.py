@@ -31,6 +31,7 @@ def test_scatter_matches_reference_slots_bit_exact(case, golden):
     kp = torch.zeros(shape, dtype=key.dtype, device="cuda")
     vp = torch.zeros_like(kp)
     rows, positions, slots = (torch.from_numpy(golden[f"{name}/{k}"]).cuda() for k in ("rows", "positions", "slots"))
+    assert po.duplicate_slots(golden[f"{name}/slots"]) == []  # one writer per slot: the result is defined
     ops.kv_scatter(key, value, rows, positions, slots, kp, vp)
     assert ops.read_status() == 0
     s = golden[f"{name}/slots"]
