@@ -6,11 +6,11 @@
 // r = token r/G, head r%G); the CTA's two row tiles are consecutive, so every K/V tile staged in
 // shared memory serves 2 x 128 query rows of the whole GQA group (half the L2 -> SM bytes per
 // FLOP of one row tile per CTA).  The KV range of a row tile (history tiles, then causal chunk
-// tiles) is cut into splits of kTilesPerSplit 64-position tiles so that long histories spread
-// over many CTAs; the two row tiles' ranges differ only in their last chunk tiles, so the CTA
-// stages the union and each row tile uses a prefix of it.  A row tile with one split writes its
-// output directly, otherwise each split writes an unnormalised partial (O, m, l) that
-// prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
+// tiles) is cut into equal splits of at most kTilesPerSplit 64-position tiles so that long
+// histories spread over many CTAs of equal work; the two row tiles' ranges differ only in their
+// last chunk tiles, so the CTA stages the union and each row tile uses a prefix of it.  A row
+// tile with one split writes its output directly, otherwise each split writes an unnormalised
+// partial (O, m, l) that prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
 //   warp 0 (loader): both Q tiles once, then K and V tiles into two kStages-deep rings (K is free
 //      once the S of both row tiles is done, V once both PVs are done).  With tensor maps (block
 //      size 16/32/64) the split's block ids are first resolved into shared memory, then one thread
@@ -259,6 +259,24 @@ __device__ __forceinline__ TcGeometry tc_geometry(const PrefillArgs& a, int64_t 
   return g;
 }
 
+// Equal-size splits of a row-tile pair: the union of the pair's tile ranges (the second tile's,
+// which is never shorter unless it is empty) is cut into ceil(tiles / kTilesPerSplit) parts of
+// `per` tiles (the last one shorter), so a row's CTAs carry equal work and the grid's tail is
+// short.  Row tile g's splits are the parts that start below its own tile count.
+struct TcSplits {
+  int per;         // tiles per split
+  int splits[2];   // splits holding tiles of row tile 0 / 1
+};
+__device__ __forceinline__ TcSplits tc_splits(int n_tiles0, int n_tiles1) {
+  TcSplits sp;
+  const int nu = max(n_tiles0, n_tiles1);
+  const int parts = max(1, (nu + kTilesPerSplit - 1) / kTilesPerSplit);
+  sp.per = max(1, (nu + parts - 1) / parts);
+  sp.splits[0] = (n_tiles0 + sp.per - 1) / sp.per;
+  sp.splits[1] = (n_tiles1 + sp.per - 1) / sp.per;
+  return sp;
+}
+
 // cp.async staging (block sizes without a TMA box) of the K or the V rows of history tile k =
 // positions [64k, 64k + 64) from `pool`; rows at or past `start` zero-filled; block ids of the
 // tile's pages are read once into `pages`.
@@ -354,15 +372,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   int64_t tok0[kPair], tok_end[kPair];
   int n_tiles[kPair], ng[kPair];
   TcGeometry geo{};
-  const int t_begin = split * kTilesPerSplit;
 #pragma unroll
   for (int g = 0; g < kPair; ++g) {
     tok0[g] = (int64_t)(pair * kPair + g) * tokens_per_tile;
     geo = tc_geometry(a, b, tok0[g], tokens_per_tile, g == 0 && tid == 0 && blockIdx.x == 0 && h == 0);
     n_tiles[g] = geo.n_tiles;
     tok_end[g] = min(geo.len, tok0[g] + tokens_per_tile);
-    ng[g] = max(0, min(n_tiles[g], t_begin + kTilesPerSplit) - t_begin);  // this split's tiles of row tile g
   }
+  const TcSplits sp = tc_splits(n_tiles[0], n_tiles[1]);
+  const int t_begin = split * sp.per;
+#pragma unroll
+  for (int g = 0; g < kPair; ++g) ng[g] = max(0, min(n_tiles[g], t_begin + sp.per) - t_begin);  // this split's tiles
   const int64_t first = geo.first;
   const int start = geo.start;
   const int hist_tiles = geo.hist_tiles;
@@ -582,7 +602,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     const int64_t my_tok = my_tok0 + r / G;
     const bool row_valid = my_tok < (g == 0 ? tok_end[0] : tok_end[1]);
     const int my_n = g == 0 ? ng[0] : ng[1];
-    const int my_n_tiles = g == 0 ? n_tiles[0] : n_tiles[1];
+    const int my_splits = g == 0 ? sp.splits[0] : sp.splits[1];
     const uint32_t s_col = (uint32_t)g * 128;
     const uint32_t o_col = kTmemO + (uint32_t)g * 128;
     const float scale = a.scale_log2;
@@ -666,8 +686,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     if (my_n > 0) {
       mbar_wait(&o_final[g], 0, aborted);
       tc_fence_after();
-      const int n_splits = (my_n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
-      if (n_splits == 1) {
+      if (my_splits == 1) {
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         T* dst = out + (b * a.padded_len + first + my_tok) * row_elems + (int64_t)(h * G + r % G) * kTcDim;
 #pragma unroll
@@ -730,7 +749,12 @@ __global__ void __launch_bounds__(kCombineThreads) prefill_combine_kernel(const 
   const int tokens_per_tile = kTcRows / G;
   const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
   const TcGeometry geo = tc_geometry(a, b, tok0, tokens_per_tile, false);
-  const int n_splits = (geo.n_tiles + kTilesPerSplit - 1) / kTilesPerSplit;
+  // the split layout of this tile's pair (as the tc kernel cut it)
+  const int pair_first = qtile - qtile % kPair;
+  const int64_t other_tok0 = (int64_t)(pair_first + (qtile == pair_first ? 1 : 0)) * tokens_per_tile;
+  const int other_tiles = tc_geometry(a, b, other_tok0, tokens_per_tile, false).n_tiles;
+  const TcSplits sp = qtile == pair_first ? tc_splits(geo.n_tiles, other_tiles) : tc_splits(other_tiles, geo.n_tiles);
+  const int n_splits = sp.splits[qtile == pair_first ? 0 : 1];
   if (n_splits <= 1) return;  // uniform for the CTA
   const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
   const int rows = (int)min((int64_t)kTcRows, (tok_end - tok0) * G);  // valid rows: a prefix of the tile
