@@ -401,10 +401,11 @@ DecodePlan plan_decode(int64_t batch, int hq, int hkv, int head_dim, int64_t max
   }
   p.heads_per_cta = (hkv % 4 == 0) ? 4 : (hkv % 2 == 0) ? 2 : 1;
   p.parts_per_split = 4 / p.heads_per_cta;
-  // Splits of ~512 tokens balance long and short sequences; shrink them when the grid would be
-  // too small to cover the 148 SMs twice.
+  // Splits of ~512 tokens x 4 KV heads of K/V per CTA (512 tokens at HB = 4, 2048 at HB = 1, so a
+  // CTA's bytes do not shrink with the heads it holds) balance long and short sequences; shrink
+  // them when the grid would be too small to cover the 148 SMs twice.
   const int64_t ctas_per_split = batch * (hkv / p.heads_per_cta);
-  int64_t split_pages = std::max<int64_t>(p.parts_per_split, 512 / block_size);
+  int64_t split_pages = std::max<int64_t>(p.parts_per_split, 512 * (4 / p.heads_per_cta) / block_size);
   const int64_t target_ctas = 2 * 148 * 2;
   while (split_pages > p.parts_per_split &&
          ctas_per_split * ((max_blocks + split_pages - 1) / split_pages) < target_ctas) {
