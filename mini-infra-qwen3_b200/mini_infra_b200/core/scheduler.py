@@ -12,7 +12,11 @@ kernels see:
   are running (decode protection);
 * ``chunked-prefill`` gives every candidate (in-flight prefills first, then admissible new
   requests) a chunk of at most ``token_budget // n_candidates`` prompt tokens, with the same
-  decode protection; prefill and decode steps stay phase-exclusive.
+  decode protection; prefill and decode steps stay phase-exclusive;
+* ``chunked-prefill`` with ``mixed=True`` (not in the reference): a step holds every decoding
+  request (one token each) and the chunks planned from ``token_budget - n_decoding`` tokens
+  (at most that many candidates, so every chunk has a token); with both present it is a
+  ``MIXED`` step, otherwise a plain prefill or decode step.
 """
 
 from __future__ import annotations
@@ -174,6 +178,7 @@ def prepare_schedule(
 class SchedulePhase(str, Enum):
     PREFILL = "prefill"
     DECODE = "decode"
+    MIXED = "mixed"  # decode rows and prefill chunks in one step (ChunkedPrefillConfig(mixed=True))
 
     def __str__(self) -> str:
         return self.value
@@ -198,7 +203,8 @@ class PrefillChunk:
 
 @dataclass(frozen=True)
 class SchedulerOutput:
-    """One step's decision.  num_scheduled_tokens: padded chunk tokens (prefill) or rows (decode)."""
+    """One step's decision.  num_scheduled_tokens: padded chunk tokens (prefill) or rows (decode);
+    a mixed step has its decode rows in ``scheduled_requests`` and counts rows + padded chunk tokens."""
 
     phase: SchedulePhase
     scheduled_requests: tuple[RequestState, ...]
@@ -251,12 +257,12 @@ class IterationScheduler:
         out = self._decide()
         if out is None:
             return None
-        if out.phase is SchedulePhase.PREFILL:
+        if out.phase is not SchedulePhase.DECODE:
             newcomers = sum(1 for c in out.prefill_chunks if c.state.status is RequestStatus.WAITING)
             self.running_queue.admit(self.waiting_queue.pop_batch(newcomers), clock_ms)
             for c in out.prefill_chunks:
                 self._allocate_slots(c.state, c.num_tokens)
-        else:
+        if out.phase is not SchedulePhase.PREFILL:
             for s in out.scheduled_requests:
                 self._allocate_slots(s, 1)
         self._last_phase = out.phase
@@ -274,10 +280,17 @@ class IterationScheduler:
             for s in scheduler_output.scheduled_requests:
                 s.cache_length += 1
             producers = scheduler_output.scheduled_requests
-        else:
+        elif scheduler_output.phase is SchedulePhase.PREFILL:
             for c in scheduler_output.prefill_chunks:
                 c.state.cache_length = c.end
             producers = tuple(c.state for c in scheduler_output.prefill_chunks if c.is_last)
+        else:  # mixed: token_ids = one per decode row, then one per chunk that ends its prompt
+            for s in scheduler_output.scheduled_requests:
+                s.cache_length += 1
+            for c in scheduler_output.prefill_chunks:
+                c.state.cache_length = c.end
+            producers = (*scheduler_output.scheduled_requests,
+                         *(c.state for c in scheduler_output.prefill_chunks if c.is_last))
         finished = self.running_queue.process_step_output(token_ids, clock_ms, eos_token_id, stop_on_eos, producers)
         if finished:
             if self.kv_cache_manager is not None:
@@ -324,8 +337,10 @@ class IterationScheduler:
         rows = self.running_queue.decoding_requests
         return SchedulerOutput(phase=SchedulePhase.DECODE, scheduled_requests=rows, num_scheduled_tokens=len(rows))
 
-    def _plan_chunks(self, token_budget: int) -> tuple[PrefillChunk, ...]:
+    def _plan_chunks(self, token_budget: int, limit: int | None = None) -> tuple[PrefillChunk, ...]:
         candidates = (*self.running_queue.prefilling_requests, *self._admission_candidates())
+        if limit is not None:
+            candidates = candidates[:limit]
         if not candidates:
             return ()
         cap = token_budget // len(candidates)
@@ -336,6 +351,19 @@ class IterationScheduler:
 
     def _decide(self) -> SchedulerOutput | None:
         policy = self.scheduler_config.batching_policy
+        if isinstance(policy, ChunkedPrefillConfig) and policy.mixed:
+            rows = self.running_queue.decoding_requests
+            budget = policy.token_budget - len(rows)
+            chunks = self._plan_chunks(budget, limit=budget) if budget > 0 else ()
+            if chunks and rows:
+                return SchedulerOutput(
+                    phase=SchedulePhase.MIXED, scheduled_requests=rows,
+                    num_scheduled_tokens=len(rows) + len(chunks) * max(c.num_tokens for c in chunks),
+                    prefill_chunks=chunks,
+                )
+            if chunks:
+                return self._prefill(chunks)
+            return self._decode() if rows else None
         if isinstance(policy, ChunkedPrefillConfig):
             if self.running_queue.decoding_requests and self._last_phase is SchedulePhase.PREFILL:
                 return self._decode()

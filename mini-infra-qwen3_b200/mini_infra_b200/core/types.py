@@ -118,16 +118,22 @@ class TokenBudgetConfig:
 
 @dataclass(frozen=True)
 class ChunkedPrefillConfig:
-    """Prompts are cut into chunks; one prefill step never exceeds ``token_budget`` padded tokens."""
+    """Prompts are cut into chunks; one prefill step never exceeds ``token_budget`` padded tokens.
+
+    ``mixed`` (no counterpart in the reference, whose chunked prefill alternates prefill and
+    decode steps): every step carries all decoding requests, one token each, plus prefill chunks
+    cut from what is left of the budget (``token_budget`` minus the decode rows), in one model
+    forward.  Off by default, so schedules match the reference's."""
 
     kind: ClassVar[BatchingPolicyKind] = "chunked-prefill"
     token_budget: int
+    mixed: bool = False
 
     def __post_init__(self) -> None:
         _positive_budget(self.token_budget)
 
     def __str__(self) -> str:
-        return f"{self.kind}(token_budget={self.token_budget})"
+        return f"{self.kind}(token_budget={self.token_budget}{', mixed' if self.mixed else ''})"
 
 
 BatchingPolicy = PrefillFirstConfig | TokenBudgetConfig | ChunkedPrefillConfig

@@ -2,7 +2,7 @@
 
 ``throughput_tok_s`` = generated tokens * 1000 / busy ms, as the reference defines it;
 ``decode_tok_s`` = decode-step tokens * 1000 / decode-step ms (the engine decode throughput the
-benchmark reports).
+benchmark reports; mixed steps are in ``throughput_tok_s`` and ``num_mixed_steps``, not here).
 """
 
 from __future__ import annotations
@@ -63,6 +63,7 @@ class ScheduleMetrics:
     decode_tok_s: float
     max_prefill_step_tokens: int
     max_prefill_step_ms: float
+    num_mixed_steps: int = 0  # ChunkedPrefillConfig(mixed=True): steps holding decode rows and chunks
 
 
 @dataclass(frozen=True)
@@ -108,5 +109,6 @@ def summarize_schedule(
         decode_tok_s=dec_tokens * 1000.0 / dec_ms if dec_ms else 0.0,
         max_prefill_step_tokens=max((e.num_scheduled_tokens for e in prefill), default=0),
         max_prefill_step_ms=max((e.step_ms for e in prefill), default=0.0),
+        num_mixed_steps=sum(1 for e in events if e.phase is SchedulePhase.MIXED),
     )
     return ScheduleResult(sequences, requests, list(events), metrics, e2e_wall_ms, paged_cache)

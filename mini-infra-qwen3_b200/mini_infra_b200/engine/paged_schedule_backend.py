@@ -3,7 +3,9 @@
 Per prefill step: chunk forward (model_ms, StepTimer), then ``store_prefill`` timed as cache_ms
 (host wall clock between two synchronisations).  Per decode step: host packing + H2D timed as
 cache_ms, then the decode forward (model_ms) — a CUDA-graph replay per batch bucket unless
-``cuda_graphs=False`` (a bucket's first step captures its graph before the timing starts).  ``accessed_kv_cache_tokens`` counts history tokens
+``cuda_graphs=False`` (a bucket's first step captures its graph before the timing starts).  Per
+mixed step (mixed chunked prefill): one forward over decode rows and chunks (model_ms), then the
+chunks' ``store_prefill`` as cache_ms.  ``accessed_kv_cache_tokens`` counts history tokens
 read: sum of chunk starts (prefill) and sum of context lengths (decode).
 """
 
@@ -113,6 +115,31 @@ class PagedScheduleBackend:
             live_kv_cache_bytes=self.kv_cache_manager.num_used_blocks * self.pool.bytes_per_block,
             kv_cache_pool_bytes=self.pool.total_bytes,
             accessed_kv_cache_tokens=sum(s.cache_length + 1 for s in scheduled),
+        )
+
+    def execute_mixed(self, decoding: Sequence[RequestState], chunks: Sequence[PrefillChunk]) -> ScheduleStepOutput:
+        """A mixed step (ChunkedPrefillConfig(mixed=True)): decode rows and prefill chunks in one
+        forward, then ``store_prefill`` of the chunks (timed as cache_ms).  next_tokens: one per
+        decode row, then one per chunk that ends its prompt."""
+        d_tables = [self.kv_cache_manager.block_table(s.request.request_idx) for s in decoding]
+        c_tables = [self.kv_cache_manager.block_table(c.state.request.request_idx) for c in chunks]
+        starts = [c.start for c in chunks]
+        out = self.runner.run_mixed_step(
+            d_tables, [s.generated[-1] for s in decoding], [s.cache_length for s in decoding],
+            [c.state.request.token_ids[c.start : c.end] for c in chunks], starts, c_tables, self.pool)
+        synchronize(self.device)
+        t0 = time.perf_counter()
+        self.runner.store_prefill(self.pool, out.prefill_cache, c_tables, [c.num_tokens for c in chunks], starts)
+        synchronize(self.device)
+        cache_ms = (time.perf_counter() - t0) * 1000.0
+        return ScheduleStepOutput(
+            next_tokens=out.decode_tokens + [t for t, c in zip(out.prefill_tokens, chunks) if c.is_last],
+            model_ms=out.model_ms,
+            cache_ms=cache_ms,
+            physical_batch_size=len(decoding) + len(chunks),
+            live_kv_cache_bytes=self.kv_cache_manager.num_used_blocks * self.pool.bytes_per_block,
+            kv_cache_pool_bytes=self.pool.total_bytes,
+            accessed_kv_cache_tokens=sum(starts) + sum(s.cache_length + 1 for s in decoding),
         )
 
     def retire(self, finished: Sequence[RequestState], *, is_idle: bool) -> None:

@@ -55,6 +55,9 @@ def _run_loop(backend: PagedScheduleBackend, requests: Sequence[Request], max_ru
         if out.phase is SchedulePhase.PREFILL:
             step = backend.execute_prefill(out.prefill_chunks)
             admitted = tuple(c.state.request.request_idx for c in out.prefill_chunks if c.start == 0)
+        elif out.phase is SchedulePhase.MIXED:
+            step = backend.execute_mixed(out.scheduled_requests, out.prefill_chunks)
+            admitted = tuple(c.state.request.request_idx for c in out.prefill_chunks if c.start == 0)
         else:
             step = backend.execute_decode(out.scheduled_requests)
             admitted = ()

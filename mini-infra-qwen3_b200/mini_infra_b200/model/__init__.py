@@ -6,6 +6,7 @@ from mini_infra_b200.model.qwen3 import (
     ChunkPrefillMetadata,
     DenseAttentionMetadata,
     HeadPartition,
+    MixedMetadata,
     PagedAttentionMetadata,
     PastKeyValue,
     Qwen3ForCausalLM,
@@ -19,6 +20,7 @@ __all__ = [
     "ChunkPrefillMetadata",
     "DenseAttentionMetadata",
     "HeadPartition",
+    "MixedMetadata",
     "PagedAttentionMetadata",
     "PastKeyValue",
     "Qwen3Config",

@@ -67,6 +67,21 @@ class ChunkPrefillMetadata(NamedTuple):
     kv_pools: tuple[PastKeyValue, ...] = ()
 
 
+class MixedMetadata(NamedTuple):
+    """A mixed step (decode rows and prefill chunks in one forward; no reference counterpart): the
+    model input is [1, T] with T = num_decode + prefill_rows * prefill_len — first one token per
+    decode row, then the left-padded chunk rows.  ``decode`` addresses the decode rows,
+    ``prefill`` the chunk rows; every layer runs its projections once over all T tokens and its
+    attention as one paged decode launch (with the append) plus one chunked-prefill launch."""
+
+    decode: PagedAttentionMetadata
+    prefill: ChunkPrefillMetadata
+    num_decode: int
+    prefill_rows: int
+    prefill_len: int
+    kv_pools: tuple[PastKeyValue, ...] = ()
+
+
 class DenseAttentionMetadata(NamedTuple):
     """Kept for API compatibility; the dense KV path is not part of this package."""
 
@@ -180,6 +195,8 @@ class Qwen3Attention(nn.Module):
         q, k, v = _packed_linear(x.reshape(tokens, hidden), (self.q_proj.weight, self.k_proj.weight,
                                                               self.v_proj.weight), self.packed_qkv)
         cos2, sin2 = cos.reshape(tokens, d), sin.reshape(tokens, d)
+        if isinstance(metadata, MixedMetadata):
+            return self._mixed(q, k, v, cos2, sin2, kv_pool, metadata, b, length)
         if isinstance(metadata, PagedAttentionMetadata):
             # decode: norm + RoPE, and the new K/V appended to the pools, in one launch
             key_pool, value_pool = kv_pool
@@ -202,6 +219,28 @@ class Qwen3Attention(nn.Module):
             present = (k4.transpose(1, 2), v4.transpose(1, 2))
         attn = gather_heads(attn.view(tokens, -1), self.partition).view(b, length, -1)
         return self.o_proj(attn), present
+
+    def _mixed(self, q, k, v, cos2, sin2, kv_pool, md: "MixedMetadata", b: int, length: int):
+        """Decode rows [0, nd) through the fused append + paged decode, chunk rows through the
+        chunked-prefill kernel; both write into one attention buffer."""
+        nd, bp, lp, d = md.num_decode, md.prefill_rows, md.prefill_len, self.head_dim
+        key_pool, value_pool = kv_pool
+        attn = torch.empty((nd + bp * lp, self.num_heads * d), dtype=q.dtype, device=q.device)
+        if nd:
+            q_d, _, _ = ops.qk_norm_rope(q[:nd], k[:nd], v[:nd], self.q_norm.weight, self.k_norm.weight, cos2[:nd],
+                                         sin2[:nd], self.q_norm.eps, self.num_heads, self.num_kv_heads, kv_out=False,
+                                         slot_mapping=md.decode.slot_mapping, k_pool=key_pool, v_pool=value_pool)
+            ops.paged_decode(q_d, key_pool, value_pool, md.decode.block_tables, md.decode.context_lens, self.scaling,
+                             out=attn[:nd])
+        q_p, k_p, v_p = ops.qk_norm_rope(q[nd:], k[nd:], v[nd:], self.q_norm.weight, self.k_norm.weight, cos2[nd:],
+                                         sin2[nd:], self.q_norm.eps, self.num_heads, self.num_kv_heads)
+        k4 = k_p.view(bp, lp, self.num_kv_heads, d)
+        v4 = v_p.view(bp, lp, self.num_kv_heads, d)
+        ops.paged_prefill(q_p.view(bp, lp, self.num_heads, d), k4, v4, key_pool, value_pool, md.prefill.block_tables,
+                          md.prefill.start_positions, md.prefill.chunk_lens, self.scaling,
+                          out=attn[nd:].view(bp, lp, -1))
+        attn = gather_heads(attn, self.partition).view(b, length, -1)
+        return self.o_proj(attn), (k4.transpose(1, 2), v4.transpose(1, 2))
 
 
 class Qwen3MLP(nn.Module):
@@ -264,7 +303,16 @@ class Qwen3Model(nn.Module):
         hidden = self.embed_tokens(input_ids)
         if isinstance(attn_metadata, DenseAttentionMetadata):
             raise NotImplementedError("the dense KV path is out of scope here; use PagedAttentionMetadata")
-        if isinstance(attn_metadata, PagedAttentionMetadata):
+        if isinstance(attn_metadata, MixedMetadata):
+            md = attn_metadata
+            if b != 1 or length != md.num_decode + md.prefill_rows * md.prefill_len:
+                raise ValueError("a mixed step takes input_ids [1, num_decode + prefill_rows * prefill_len]")
+            if position_ids is None or position_ids.shape != (b, length):
+                raise ValueError("a mixed step needs position_ids shaped like input_ids")
+            if len(md.kv_pools) != len(self.layers):
+                raise ValueError("kv_pools must hold one (key, value) pool pair per layer")
+            pools = md.kv_pools
+        elif isinstance(attn_metadata, PagedAttentionMetadata):
             if length != 1:
                 raise ValueError("paged decode input_ids must be [batch, 1]")
             if position_ids is None or position_ids.shape != (b, 1):
@@ -336,6 +384,7 @@ def pack_projections_(model: nn.Module) -> nn.Module:
 
 __all__ = [
     "ChunkPrefillMetadata",
+    "MixedMetadata",
     "DenseAttentionMetadata",
     "HeadPartition",
     "PagedAttentionMetadata",

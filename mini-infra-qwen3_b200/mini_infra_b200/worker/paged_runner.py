@@ -12,6 +12,9 @@ tables).  Attention reads history in place from the pools; nothing gathers the h
 * ``store_prefill`` — writes those tokens to their slots; the slot arithmetic
   (table[pos // bs] * bs + pos % bs) runs on the device;
 * ``prepare_decode_inputs`` / ``run_decode_step`` — decode step, append fused in the attention op.
+* ``run_mixed_step`` — decode rows and prefill chunks in one forward (the mixed chunked-prefill
+  policy; no reference counterpart): one packed upload, projections over all tokens, one decode
+  and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.
   With ``enable_decode_graphs`` the packed rows are padded to a batch bucket and copied into
   that bucket's static input buffer, and the step replays the bucket's CUDA graph
   (``worker/decode_graphs.py``); otherwise it runs eagerly.
@@ -26,7 +29,7 @@ import numpy as np
 import torch
 
 from mini_infra_b200.device import StepTimer
-from mini_infra_b200.model.qwen3 import ChunkPrefillMetadata, PagedAttentionMetadata
+from mini_infra_b200.model.qwen3 import ChunkPrefillMetadata, MixedMetadata, PagedAttentionMetadata
 from mini_infra_b200.worker.base_runner import BaseModelRunner, PrefillOutput
 from mini_infra_b200.worker.decode_graphs import DecodeGraphSet, packed_length
 from mini_infra_b200.worker.kv_cache import KVCache
@@ -38,6 +41,13 @@ _NULL_BLOCK_ID = 0
 
 class PagedDecodeOutput(NamedTuple):
     next_tokens: list[int]
+    model_ms: float
+
+
+class PagedMixedOutput(NamedTuple):
+    decode_tokens: list[int]   # one per decode row
+    prefill_tokens: list[int]  # one per chunk row (its last position; meaningful for final chunks)
+    prefill_cache: KVCache     # the chunks' K/V for store_prefill
     model_ms: float
 
 
@@ -172,6 +182,62 @@ class PagedRunner(BaseModelRunner):
         )
         return packed[:b].view(b, 1), packed[b : 2 * b].view(b, 1), metadata
 
+    def run_mixed_step(
+        self,
+        decode_block_tables: Sequence[Sequence[int]],
+        last_tokens: Sequence[int],
+        positions: Sequence[int],
+        chunk_token_ids: Sequence[Sequence[int]],
+        start_positions: Sequence[int],
+        chunk_block_tables: Sequence[Sequence[int]],
+        pool: PagedKVCachePool,
+    ) -> PagedMixedOutput:
+        """Decode rows (their new token at `positions`, appended to the pool) and prefill chunks
+        (history = the first ceil(start / bs) blocks of their table) in one forward."""
+        nd, bp = len(decode_block_tables), len(chunk_token_ids)
+        lens = [len(t) for t in chunk_token_ids]
+        if nd == 0 or bp == 0 or min(lens) < 1:
+            raise ValueError("a mixed step needs decode rows and non-empty chunks")
+        bs = pool.block_size
+        width = max(lens)
+        n_hist = [-(-int(st) // bs) for st in start_positions]
+        nbp = max(max(n_hist), 1)
+        nbd = max(len(t) for t in decode_block_tables)
+        slots = [int(t[p // bs]) * bs + p % bs for t, p in zip(decode_block_tables, positions)]
+        ids = [int(x) for x in last_tokens]
+        pos = [int(x) for x in positions]
+        for toks, n in zip(chunk_token_ids, lens):
+            ids += [self.pad_token_id] * (width - n) + [int(t) for t in toks]
+        for st, n in zip(start_positions, lens):
+            pos += [0] * (width - n) + list(range(int(st), int(st) + n))
+        flat = ids + pos + slots + [p + 1 for p in positions] + [int(x) for x in start_positions] + lens
+        for t in decode_block_tables:
+            flat += [int(x) for x in t] + [_NULL_BLOCK_ID] * (nbd - len(t))
+        for table, h in zip(chunk_block_tables, n_hist):
+            if len(table) < h:
+                raise ValueError(f"block table {list(table)} does not cover {h} history blocks")
+            flat += [int(x) for x in table[:h]] + [_NULL_BLOCK_ID] * (nbp - h)
+        packed = self._upload(flat)
+        t_all = nd + bp * width
+        o = 2 * t_all
+        input_ids, position_ids = packed[:t_all].view(1, t_all), packed[t_all:o].view(1, t_all)
+        decode_md = PagedAttentionMetadata(slot_mapping=packed[o : o + nd], context_lens=packed[o + nd : o + 2 * nd],
+                                           block_tables=packed[o + 2 * nd + 2 * bp : o + 2 * nd + 2 * bp + nd * nbd]
+                                           .view(nd, nbd))
+        q = o + 2 * nd + 2 * bp + nd * nbd
+        prefill_md = ChunkPrefillMetadata(block_tables=packed[q : q + bp * nbp].view(bp, nbp),
+                                          start_positions=packed[o + 2 * nd : o + 2 * nd + bp],
+                                          chunk_lens=packed[o + 2 * nd + bp : o + 2 * nd + 2 * bp])
+        md = MixedMetadata(decode_md, prefill_md, nd, bp, width, kv_pools=tuple(pool.kv_pools))
+        with StepTimer(self.device) as timer:
+            hidden, presents = self.model.model(input_ids, position_ids=position_ids, attn_metadata=md)
+            rows = torch.cat((torch.arange(nd, device=self.device),
+                              nd + torch.arange(bp, device=self.device) * width + (width - 1)))
+            next_token, _ = greedy_sample(self.model.lm_head(hidden[0, rows]).unsqueeze(1))
+        tokens = next_token.squeeze(-1).tolist()
+        self.d2h_bytes += 8 * (nd + bp)
+        return PagedMixedOutput(tokens[:nd], tokens[nd:], KVCache(presents), timer.elapsed_ms)
+
     def _prepare_graph_inputs(self, g: DecodeGraphSet, n: int, block_tables, last_tokens, positions, slots):
         """Packed rows padded to bucket n, copied into the bucket's static buffer; views of its first b rows."""
         b, w = len(block_tables), g.width
@@ -220,4 +286,4 @@ class PagedRunner(BaseModelRunner):
         return PagedDecodeOutput(next_token.squeeze(-1).tolist(), timer.elapsed_ms)
 
 
-__all__ = ["PagedDecodeOutput", "PagedRunner"]
+__all__ = ["PagedDecodeOutput", "PagedMixedOutput", "PagedRunner"]

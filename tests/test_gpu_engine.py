@@ -6,6 +6,9 @@
   steps replayed from CUDA graphs (every one of them) and run eagerly.
 * Runner-level checks mirroring the reference's own paged tests: chunked prefill in rounds
   leaves the same K/V in the pool as a one-shot prefill and yields the same first token.
+* Mixed chunked prefill (decode rows and prefill chunks in one step, a flag with no reference
+  counterpart): the golden workloads still produce the reference's greedy ids, and a bf16 mixed
+  forward equals the separate decode and chunked-prefill forwards of the same rows.
 """
 
 import json
@@ -108,3 +111,86 @@ def test_pool_layout_and_byte_accounting():
     kp, vp = pool.kv_pools[0]
     assert kp.shape == (10, 4, 2, 32) == vp.shape and not kp.any()
     assert pool.bytes_per_block == 2 * 2 * 4 * 2 * 32 * 4 and pool.total_bytes == 10 * pool.bytes_per_block
+
+
+@pytest.mark.parametrize("case", [c for c in GOLDEN["cases"] if c["batching_policy"] == "chunked-prefill"],
+                         ids=lambda c: c["name"])
+def test_mixed_steps_keep_reference_tokens(case):
+    """Per-request greedy ids do not depend on how steps are packed, so the mixed policy must
+    reproduce the reference engine's ids on the fp32 golden workloads, taking mixed steps."""
+    model = c1_model(case["tied"])
+    cfg = EngineConfig(PagedCacheConfig(block_size=16), BatchingMethod.CONTINUOUS,
+                       scheduler_config=SchedulerConfig(case["max_running_requests"],
+                                                        ChunkedPrefillConfig(case["token_budget"], mixed=True)))
+    result = run_scheduler(cfg, model, make_requests(case["prompts"], case["max_new_tokens"]), None,
+                           stop_on_eos=False)
+    assert [s.token_ids for s in result.sequences] == case["tokens"]
+    assert result.schedule_metrics.num_mixed_steps > 0
+    assert ops.read_status() == 0
+
+
+@torch.inference_mode()
+def test_bf16_mixed_forward_equals_separate_forwards():
+    """One mixed forward (decode rows through the fused append + paged decode, chunk rows through
+    the tcgen05 chunked-prefill kernel, shared projections) against a decode forward and a
+    chunked-prefill forward of the same rows: hidden states within the bf16 attention
+    tolerance, and the decode rows' K/V appended to the same slots."""
+    import numpy as np
+
+    from mini_infra_b200.model import ChunkPrefillMetadata, MixedMetadata, PagedAttentionMetadata
+    from mini_infra_b200.model.config import TINY_C1
+
+    cfg = Qwen3Config(**dict(TINY_C1, head_dim=128, hidden_size=256), torch_dtype="bfloat16")
+    model = build_model(cfg, seed=5, device="cuda", dtype=torch.bfloat16)
+    bs, nb = 16, 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    pool = PagedKVCachePool(cfg.num_hidden_layers, nb, bs, cfg.num_key_value_heads, cfg.head_dim, torch.bfloat16,
+                            torch.device("cuda"))
+    for kp, vp in pool.kv_pools:
+        kp.copy_(torch.randn(kp.shape, generator=g, device="cuda"))
+        vp.copy_(torch.randn(vp.shape, generator=g, device="cuda"))
+    perm = np.random.RandomState(0).permutation(np.arange(1, nb)).tolist()
+    ctx = [40, 70, 17]                    # decode rows: context incl. the new token
+    starts, lens = [32, 0], [20, 33]      # chunk rows: history, chunk tokens
+    need = [-(-c // bs) for c in ctx] + [-(-(s + n) // bs) for s, n in zip(starts, lens)]
+    tables, off = [], 0
+    for n in need:
+        tables.append(perm[off : off + n])
+        off += n
+    nd, bp, width = 3, 2, max(lens)
+    dev = torch.device("cuda")
+    t = lambda x: torch.tensor(x, dtype=torch.long, device=dev)  # noqa: E731
+    pad = lambda rows, w: [r + [0] * (w - len(r)) for r in rows]  # noqa: E731
+    d_ids = torch.randint(1, cfg.vocab_size, (nd,), generator=g, device=dev)
+    p_ids = torch.randint(1, cfg.vocab_size, (bp, width), generator=g, device=dev)
+    d_pos = t([c - 1 for c in ctx])
+    p_pos = t([[0] * (width - n) + list(range(s, s + n)) for s, n in zip(starts, lens)])
+    d_md = PagedAttentionMetadata(slot_mapping=t([tables[i][(c - 1) // bs] * bs + (c - 1) % bs for i, c in enumerate(ctx)]),
+                                  block_tables=t(pad(tables[:nd], max(need[:nd]))), context_lens=t(ctx))
+    n_hist = max(-(-s // bs) for s in starts)
+    p_md = ChunkPrefillMetadata(block_tables=t(pad([tb[: -(-s // bs)] for tb, s in zip(tables[nd:], starts)], n_hist)),
+                                start_positions=t(starts), chunk_lens=t(lens))
+    pools = tuple(pool.kv_pools)
+    snapshot = [(kp.clone(), vp.clone()) for kp, vp in pools]
+    ids = torch.cat((d_ids, p_ids.reshape(-1))).view(1, -1)
+    pos = torch.cat((d_pos, p_pos.reshape(-1))).view(1, -1)
+    h_mixed, _ = model.model(ids, position_ids=pos,
+                             attn_metadata=MixedMetadata(d_md, p_md, nd, bp, width, kv_pools=pools))
+    appended = [(kp.clone(), vp.clone()) for kp, vp in pools]
+    for (kp, vp), (k0, v0) in zip(pools, snapshot):
+        kp.copy_(k0)
+        vp.copy_(v0)
+    h_dec, _ = model.model(d_ids.view(nd, 1), position_ids=d_pos.view(nd, 1), attn_metadata=d_md._replace(kv_pools=pools))
+    h_pre, _ = model.model(p_ids, position_ids=p_pos, attn_metadata=p_md._replace(kv_pools=pools))
+    scale = h_dec.float().abs().max().item()
+    assert (h_mixed[0, :nd].float() - h_dec[:, 0].float()).abs().max().item() <= 2e-2 * max(scale, 1.0)
+    valid = torch.cat([torch.arange(width - n, width, device=dev) + b * width for b, n in enumerate(lens)])
+    got = h_mixed[0, nd:][valid].float()
+    want = h_pre.reshape(bp * width, -1)[valid].float()
+    assert (got - want).abs().max().item() <= 2e-2 * max(want.abs().max().item(), 1.0)
+    slots = d_md.slot_mapping
+    for (kp, vp), (ka, va) in zip(pools, appended):
+        kd = kp.view(-1, *kp.shape[2:])[slots].float()
+        ka_ = ka.view(-1, *ka.shape[2:])[slots].float()
+        assert (kd - ka_).abs().max().item() <= 2e-2 * max(kd.abs().max().item(), 1.0)
+    assert ops.read_status() == 0

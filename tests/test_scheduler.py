@@ -34,6 +34,9 @@ def _drive(requests, sched_cfg, block_size=16, num_blocks=None):
         if out.phase is SchedulePhase.PREFILL:
             n = sum(c.is_last for c in out.prefill_chunks)
             trace.append(("P", tuple((c.start, c.end) for c in out.prefill_chunks)))
+        elif out.phase is SchedulePhase.MIXED:
+            n = len(out.scheduled_requests) + sum(c.is_last for c in out.prefill_chunks)
+            trace.append(("M", len(out.scheduled_requests), tuple((c.start, c.end) for c in out.prefill_chunks)))
         else:
             n = len(out.scheduled_requests)
             trace.append(("D", n))
@@ -90,3 +93,24 @@ def test_exhausted_pool_fails_loudly():
     reqs = make_requests([list(range(1, 9)), list(range(1, 9))], 8)
     with pytest.raises(RuntimeError):
         _drive(reqs, SchedulerConfig(2, PrefillFirstConfig()), block_size=4, num_blocks=5)
+
+
+def test_mixed_chunked_prefill_packs_decode_rows_and_budgeted_chunks():
+    """ChunkedPrefillConfig(mixed=True): once a request decodes, each step carries every decode
+    row plus chunks planned from the remaining budget (token_budget - decode rows)."""
+    reqs = make_requests([list(range(1, 4)), list(range(1, 11))], 4)
+    budget = 6
+    states, trace = _drive(reqs, SchedulerConfig(2, ChunkedPrefillConfig(budget, mixed=True)), block_size=2)
+    assert trace[0] == ("P", ((0, 3), (0, 3)))          # nothing decodes yet: a plain prefill, cap 6 // 2
+    assert trace[1] == ("M", 1, ((3, 8),))               # 1 decode row + a chunk of 6 - 1 = 5 tokens
+    assert trace[2] == ("M", 1, ((8, 10),))              # the last chunk rides with the next decode token
+    assert all(t[0] == "D" for t in trace[3:])           # both decode: nothing left to prefill
+    for t in trace:
+        if t[0] == "M":
+            assert sum(e - b for b, e in t[2]) <= budget - t[1] and len(t[2]) <= budget - t[1]
+    assert all(len(s.generated) == 4 for s in states)
+
+
+def test_mixed_flag_is_off_by_default_and_named():
+    assert ChunkedPrefillConfig(8).mixed is False
+    assert str(ChunkedPrefillConfig(8, mixed=True)) == "chunked-prefill(token_budget=8, mixed)"
