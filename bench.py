@@ -341,6 +341,20 @@ def c3_requests(num: int, seed: int, max_new: int, rate_per_s: float = 32.0, lo:
     return make_requests(prompts, max_new, arrivals.tolist())
 
 
+C3_TOKEN_BUDGET = 2048
+
+
+def c3_latency(results) -> dict:
+    """TTFT and inter-token latency percentiles (logical-clock ms) over all requests of all runs."""
+    ttft, itl = [], []
+    for r in results:
+        for m in r.requests:
+            ttft.append(m.ttft_ms)
+            itl += list(np.diff(m.token_times_ms))
+    pct = lambda xs, q: round(float(np.percentile(xs, q)), 3) if len(xs) else None  # noqa: E731
+    return {"ttft_p50": pct(ttft, 50), "ttft_p95": pct(ttft, 95), "itl_p50": pct(itl, 50), "itl_p95": pct(itl, 95)}
+
+
 def run_c3(args) -> None:
     """Config 3: the full paged engine on random-init Qwen3-0.6B (bf16), 128 requests.
 
@@ -368,8 +382,12 @@ def run_c3(args) -> None:
     cfg = Qwen3Config(**QWEN3_0_6B, torch_dtype="bfloat16")
     model = build_model(cfg, seed=0, device=device, dtype=torch.bfloat16, partition=HeadPartition(rank, world, group),
                         generator_device="cuda")
+    from mini_infra_b200.core import ChunkedPrefillConfig
+
+    policy = {"prefill-first": None, "chunked": ChunkedPrefillConfig(C3_TOKEN_BUDGET),
+              "mixed": ChunkedPrefillConfig(C3_TOKEN_BUDGET, mixed=True)}[args.policy]
     engine = EngineConfig(PagedCacheConfig(block_size=16), BatchingMethod.CONTINUOUS,
-                          scheduler_config=SchedulerConfig(None))
+                          scheduler_config=SchedulerConfig(None, policy) if policy else SchedulerConfig(None))
     for i in range(args.warmup):
         run_scheduler(engine, model, c3_requests(8, 100 + i, 8), None, stop_on_eos=False)
     results = []
@@ -391,7 +409,9 @@ def run_c3(args) -> None:
             "config": {"workload": "config3_engine_qwen3_0.6b", "model": "Qwen3-0.6B shape (28L, 16q/8kv, d128)",
                        "requests": 128, "arrivals": "Poisson 32/s", "prompt_len": "log-uniform[32,2048]",
                        "max_new_tokens": 128, "engine": str(engine), "engine_steps": steps,
+                       "policy": str(policy) if policy else "prefill-first",
                        "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU"},
+            "latency_ms": c3_latency(results),
             "engine": {"decode_tokens": dec_tokens, "decode_ms": dec_ms, "throughput_tok_s": out_tokens * 1000.0 / busy_ms,
                        "busy_ms": busy_ms, "prefill_steps": sum(r.schedule_metrics.num_prefill_steps for r in results),
                        "decode_steps": sum(r.schedule_metrics.num_decode_steps for r in results)},
@@ -416,6 +436,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c3", "c4"], default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--policy", choices=["prefill-first", "chunked", "mixed"], default="prefill-first",
+                    help="config 3 batching policy (chunked / mixed: token budget %d)" % C3_TOKEN_BUDGET)
     args = ap.parse_args()
     if args.workload == "c3":
         args.steps = args.steps or 1
