@@ -5,19 +5,20 @@ step's integer metadata into ONE int64 host buffer, copied to the device in one 
 sections become contiguous views (ids, positions, starts/lengths or slots/context lengths, block
 tables).  Attention reads history in place from the pools; nothing gathers the history.
 
-* ``run_prefill_chunk_step`` — left-padded chunk forward; history of row i is the first
+* ``run_prefill_chunk_step`` — left-padded chunk forward (padded to a few widths, see
+  ``padded_width``); history of row i is the first
   ceil(start_i / bs) blocks of its table; returns the chunk's K/V as ``prefill_cache``
   ([B, H_kv, L, D] per layer, valid tokens right-aligned) and the greedy token of each row's
   last position;
 * ``store_prefill`` — writes those tokens to their slots; the slot arithmetic
   (table[pos // bs] * bs + pos % bs) runs on the device;
 * ``prepare_decode_inputs`` / ``run_decode_step`` — decode step, append fused in the attention op.
-* ``run_mixed_step`` — decode rows and prefill chunks in one forward (the mixed chunked-prefill
-  policy; no reference counterpart): one packed upload, projections over all tokens, one decode
-  and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.
   With ``enable_decode_graphs`` the packed rows are padded to a batch bucket and copied into
   that bucket's static input buffer, and the step replays the bucket's CUDA graph
   (``worker/decode_graphs.py``); otherwise it runs eagerly.
+* ``run_mixed_step`` — decode rows and prefill chunks in one forward (the mixed chunked-prefill
+  policy; no reference counterpart): one packed upload, projections over all tokens, one decode
+  and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.
 """
 
 from __future__ import annotations
@@ -49,6 +50,16 @@ class PagedMixedOutput(NamedTuple):
     prefill_tokens: list[int]  # one per chunk row (its last position; meaningful for final chunks)
     prefill_cache: KVCache     # the chunks' K/V for store_prefill
     model_ms: float
+
+
+def padded_width(longest: int) -> int:
+    """Padded chunk length of a prefill step: the longest chunk rounded up to a multiple of 32 (up
+    to 256 tokens), 128 (up to 2048) or 256.  Prompt lengths rarely repeat, and the first GEMM of
+    each new shape costs ~70 us of host time in the library's algorithm selection (~8 ms per step
+    over a 28-layer model); a few widths make them repeat.  The extra left padding is masked by the
+    kernels (chunk lengths), so results do not change."""
+    step = 32 if longest <= 256 else 128 if longest <= 2048 else 256
+    return -(-longest // step) * step
 
 
 def _to_device(values: list[int], device: torch.device) -> torch.Tensor:
@@ -101,7 +112,7 @@ class PagedRunner(BaseModelRunner):
         lens = [len(t) for t in chunk_token_ids]
         if b == 0 or min(lens) < 1:
             raise ValueError("every chunk must hold at least one token")
-        width = max(lens)
+        width = padded_width(max(lens))
         bs = pool.block_size if pool is not None else 1
         n_hist = [-(-int(s) // bs) for s in start_positions]
         if pool is None and any(n_hist):
@@ -199,7 +210,7 @@ class PagedRunner(BaseModelRunner):
         if nd == 0 or bp == 0 or min(lens) < 1:
             raise ValueError("a mixed step needs decode rows and non-empty chunks")
         bs = pool.block_size
-        width = max(lens)
+        width = padded_width(max(lens))
         n_hist = [-(-int(st) // bs) for st in start_positions]
         nbp = max(max(n_hist), 1)
         nbd = max(len(t) for t in decode_block_tables)

@@ -93,8 +93,9 @@ def test_chunked_prefill_rounds_match_one_shot_prefill(block_size):
                 table = manager.block_table(idx)
                 k = torch.cat([kp[b] for b in table])[: len(prompt)].transpose(0, 1)
                 v = torch.cat([vp[b] for b in table])[: len(prompt)].transpose(0, 1)
-                torch.testing.assert_close(k, k_ref[0], atol=1e-5, rtol=0)
-                torch.testing.assert_close(v, v_ref[0], atol=1e-5, rtol=0)
+                # prefill_cache is left-padded (valid tokens right-aligned)
+                torch.testing.assert_close(k, k_ref[0, :, -len(prompt):], atol=1e-5, rtol=0)
+                torch.testing.assert_close(v, v_ref[0, :, -len(prompt):], atol=1e-5, rtol=0)
 
 
 def test_prepare_decode_inputs_golden_values():
