@@ -6,28 +6,31 @@
 // r = token r/G, head r%G); the CTA's two row tiles are consecutive, so every K/V tile staged in
 // shared memory serves 2 x 128 query rows of the whole GQA group (half the L2 -> SM bytes per
 // FLOP of one row tile per CTA).  The KV range of a row tile (history tiles, then causal chunk
-// tiles) is cut into equal splits of at most kTilesPerSplit 64-position tiles so that long
+// tiles) is cut into equal splits of at most kTilesPerSplit 128-position tiles so that long
 // histories spread over many CTAs of equal work; the two row tiles' ranges differ only in their
 // last chunk tiles, so the CTA stages the union and each row tile uses a prefix of it.  A row
 // tile with one split writes its output directly, otherwise each split writes an unnormalised
 // partial (O, m, l) that prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
-//   warp 0 (loader): both Q tiles once, then K and V tiles into two kStages-deep rings (K is free
-//      once the S of both row tiles is done, V once both PVs are done).  With tensor maps (block
-//      size 16/32/64) the split's block ids are first resolved into shared memory, then one thread
-//      issues TMA copies: one 3D box per pool page of a history tile (a page past `start` reads
-//      rows past the pool, which TMA fills with zeros) and one 4D box per half of a chunk tile;
-//      otherwise the warp stages rows with cp.async;
-//   warp 1 (MMA, one thread): per row tile g, S = Q_g K^T as 8 tcgen05.mma (M=128, N=64, K=16,
-//      kind::f16, fp32 accumulate) into one of g's two TMEM S buffers, and O_g += P V as 4
-//      tcgen05.mma (M=128, N=128, P read from TMEM, V read MN-major) into g's TMEM O columns,
-//      issued in readiness order so S(i+1) runs under softmax(i); tcgen05.commit signals mbarriers;
-//   warps 2-5 / 6-9 (softmax of row tile 0 / 1): each thread owns one row (its TMEM lane): one
-//      tcgen05.ld of the row's 64 scores, causal / length mask (set to -inf) only on tiles that
-//      cross a row's causal end or
-//      the history end, online softmax in the exp2 domain; the running O in TMEM is rescaled
-//      (tcgen05.ld/st, warp-wide) only when a row maximum grew by more than 2^8 since its last
-//      rescale (p <= 2^8 stays exact in fp32 and the final 1/l absorbs it); P is written back with
-//      tcgen05.st as 16-bit pairs into the first 32 columns of the tile's S buffer.
+//   warp 0 (loader): both Q tiles once, then K and V tiles into a kStagesK-deep K ring and a
+//      kStagesV-deep V ring (K is free once the S of both row tiles is done, V once both PVs
+//      are).  With tensor maps (block size 16/32/64) the split's block ids are first resolved
+//      into shared memory, then an elected lane issues TMA copies: one 3D box per pool page of a
+//      history tile (a page past `start` reads rows past the pool, which TMA fills with zeros)
+//      and 4D boxes of 64 tokens for a chunk tile; otherwise the warp stages rows with cp.async;
+//   warp 1 (MMA, elected lane): per row tile g, S_g = Q_g K^T as 8 tcgen05.mma (M=128, N=128,
+//      K=16, kind::f16, fp32 accumulate: 8 KiB of shared-memory operands per 64 cycles of math,
+//      the shared-memory rate) into g's TMEM S columns, and O_g += P_g V as 8 tcgen05.mma
+//      (M=128, N=128, P read from TMEM, V read MN-major) into g's TMEM O columns.  The row tiles
+//      alternate: PV_0(i), S_0(i+1), PV_1(i), S_1(i+1), so the softmax of one row tile runs
+//      under the MMAs of the other; tcgen05.commit signals mbarriers;
+//   warps 2-5 / 6-9 (softmax of row tile 0 / 1): each thread owns one row (its TMEM lane):
+//      tcgen05.ld of the row's 128 scores, causal / length mask (set to -inf) only on tiles that
+//      cross a row's causal end or the history end, online softmax in the exp2 domain; the
+//      running O in TMEM is rescaled (tcgen05.ld/st, warp-wide) only when a row maximum grew by
+//      more than 2^8 since its last rescale (p <= 2^8 stays exact in fp32 and the final 1/l
+//      absorbs it); P is written back with tcgen05.st as 16-bit pairs into the first 64 columns
+//      of g's S columns (S_g(i+1) overwrites them only after PV_g(i), issued before it, has read
+//      them: tcgen05.mma of one thread run in issue order).
 // Epilogue: tcgen05.ld of O, divide by l (or store the partial), 16-byte stores.  Padding
 // positions get zeros.
 //
@@ -35,9 +38,9 @@
 // regions of R*128 bytes (columns 0-63 and 64-127); row r of a region is 128 bytes at r*128 and
 // its 16-byte unit u lives at unit u ^ (r % 8).  Every region starts 1024-byte aligned.
 // Descriptors:
-//   K-major (Q: R=128, K: R=64):  LBO = 16 B (unused),
+//   K-major (Q and K: R=128):  LBO = 16 B (unused),
 //     SBO = 1024 B (8-row groups), swizzle 128B; k-step s starts at region(s/4) + (s%4)*32 B.
-//   MN-major (V as the B operand of PV, N = head_dim):  LBO = 8 KiB (next 64 columns of N),
+//   MN-major (V as the B operand of PV, N = head_dim):  LBO = 16 KiB (next 64 columns of N),
 //     SBO = 1024 B (next 8 K-rows); k-step s starts at s*16 rows = s*2048 B.
 #include <type_traits>
 
@@ -49,26 +52,28 @@ namespace {
 
 constexpr int kTcRows = 128;                        // query rows per row tile (MMA M)
 constexpr int kPair = 2;                            // row tiles per CTA, sharing every K/V tile
-constexpr int kTcKv = 64;                           // KV positions per tile
+constexpr int kTcKv = 128;                          // KV positions per tile (MMA N of S)
 constexpr int kTcDim = 128;                         // head_dim
 constexpr int kSoftmaxThreads = 128;                // one warpgroup per row tile
 constexpr int kTcThreads = 64 + kPair * kSoftmaxThreads;  // warp 0 loader, warp 1 MMA, then the warpgroups
 constexpr int kLoaderWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kLoaderThreads = 32;
-constexpr int kTilesPerSplit = 32;                  // 2048 KV positions per CTA at most
-constexpr int kStages = 4;                          // depth of the K ring and of the V ring
+constexpr int kTilesPerSplit = 16;                  // 2048 KV positions per CTA at most
+constexpr int kStagesK = 3;                         // depth of the K ring
+constexpr int kStagesV = 2;                         // depth of the V ring
 constexpr int kQRegion = kTcRows * 128;             // 16 KiB: one 64-column half of a Q tile
-constexpr int kKvRegion = kTcKv * 128;              // 8 KiB: one 64-column half of a K or V tile
+constexpr int kKvRegion = kTcKv * 128;              // 16 KiB: one 64-column half of a K or V tile
 constexpr int kQBytes = 2 * kQRegion;               // 32 KiB per row tile
-constexpr int kKvBytes = 2 * kKvRegion;             // 16 KiB
+constexpr int kKvBytes = 2 * kKvRegion;             // 32 KiB
 constexpr int kOffQ = 0;                            // kPair Q tiles
-constexpr int kOffK = kOffQ + kPair * kQBytes;      // kStages K buffers
-constexpr int kOffV = kOffK + kStages * kKvBytes;   // kStages V buffers
-constexpr int kOffBar = kOffV + kStages * kKvBytes;
-constexpr int kOffPages = kOffBar + 256;            // block ids (cp.async: 65 int64 of one tile; TMA: 128 int32)
-constexpr int kTcSmemBytes = kOffPages + 65 * 8 + 1024;  // + alignment slack (~194 KiB: one CTA per SM)
-// TMEM (512 columns): S buffers of row tile g at g*128 + {0, 64}; O of row tile g at 256 + g*128.
+constexpr int kOffK = kOffQ + kPair * kQBytes;      // kStagesK K buffers
+constexpr int kOffV = kOffK + kStagesK * kKvBytes;  // kStagesV V buffers
+constexpr int kOffBar = kOffV + kStagesV * kKvBytes;
+constexpr int kOffPages = kOffBar + 256;            // block ids (cp.async: kTcKv+1 int64 of one tile; TMA: 128 int32)
+constexpr int kTcSmemBytes = kOffPages + (kTcKv + 1) * 8 + 1024;  // + alignment slack (~226 KiB: one CTA per SM)
+static_assert(kTcSmemBytes <= 232448, "shared memory above the 227 KiB a CTA may use");
+// TMEM (512 columns): S (then P) of row tile g at g*128; O of row tile g at 256 + g*128.
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 256;
 constexpr float kRescaleLog2 = 8.0f;
@@ -190,17 +195,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+// tcgen05.st of 16 columns without the wait: issue several, then one tmem_wait_st().
+__device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void cp_async16(uint32_t sdst, const void* gsrc, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sdst), "l"(gsrc), "r"(valid ? 16u : 0u)
@@ -225,14 +229,14 @@ struct BlockAddr {
   }
 };
 
-// KV tiles of a row tile: first the history tiles (positions [64k, 64k + 64) of [0, start), read
-// from the pool), then the chunk tiles (chunk tokens [64k, 64k + 64) of [0, tok_end), read from the
-// chunk's own K/V).  Keeping the two apart aligns every tile to its source, so each one is a few
-// whole TMA boxes: pool pages [64 x 1 x block_size] or a [64 x 1 x 64 x 1] chunk box.
+// KV tiles of a row tile: first the history tiles (positions [128k, 128k + 128) of [0, start),
+// read from the pool), then the chunk tiles (chunk tokens [128k, 128k + 128) of [0, tok_end), read
+// from the chunk's own K/V).  Keeping the two apart aligns every tile to its source, so each one is
+// a few whole TMA boxes: pool pages [64 x 1 x block_size] or [64 x 1 x 64 x 1] chunk boxes.
 struct TcGeometry {
   int64_t len, first;
   int start;
-  int hist_tiles;  // ceil(start / 64)
+  int hist_tiles;  // ceil(start / kTcKv)
   int n_tiles;     // history tiles + chunk tiles up to the causal end of the tile's last token
 };
 
@@ -278,7 +282,7 @@ __device__ __forceinline__ TcSplits tc_splits(int n_tiles0, int n_tiles1) {
 }
 
 // cp.async staging (block sizes without a TMA box) of the K or the V rows of history tile k =
-// positions [64k, 64k + 64) from `pool`; rows at or past `start` zero-filled; block ids of the
+// positions [128k, 128k + 128) from `pool`; rows at or past `start` zero-filled; block ids of the
 // tile's pages are read once into `pages`.
 template <typename T>
 __device__ __forceinline__ void stage_hist_cp(const PrefillArgs& a, const BlockAddr& ba, int64_t b, int h, int start,
@@ -315,7 +319,7 @@ __device__ __forceinline__ void stage_hist_cp(const PrefillArgs& a, const BlockA
 }
 
 // cp.async staging of the K or V rows (`chunk` = k_chunk or v_chunk) of chunk tile k = chunk
-// tokens [64k, 64k + 64); rows at or past `rows_end` zero.
+// tokens [128k, 128k + 128); rows at or past `rows_end` zero.
 __device__ __forceinline__ void stage_chunk_cp(const PrefillArgs& a, int64_t b, int h, int64_t first, int k,
                                                int rows_end, const char* chunk, uint32_t dst, int lane) {
   const int unit = lane & 15;
@@ -348,13 +352,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;                    // loader -> MMA: both Q tiles landed
-  uint64_t* k_full = bars + 1;                    // [kStages] loader -> MMA: K stage landed
-  uint64_t* k_empty = k_full + kStages;           // [kStages] MMA -> loader: the S of the stage done
-  uint64_t* v_full = k_empty + kStages;           // [kStages] loader -> MMA: V stage landed
-  uint64_t* v_empty = v_full + kStages;           // [kStages] MMA -> loader: the PVs of the stage done
-  uint64_t* s_full = v_empty + kStages;           // [kPair][2] MMA -> softmax g: S tile ready
-  uint64_t* p_full = s_full + 2 * kPair;          // [kPair][2] softmax g -> MMA: P written into TMEM
-  uint64_t* o_done = p_full + 2 * kPair;          // [kPair] MMA -> softmax g: one phase per PV
+  uint64_t* k_full = bars + 1;                    // [kStagesK] loader -> MMA: K stage landed
+  uint64_t* k_empty = k_full + kStagesK;          // [kStagesK] MMA -> loader: the S of the stage done
+  uint64_t* v_full = k_empty + kStagesK;          // [kStagesV] loader -> MMA: V stage landed
+  uint64_t* v_empty = v_full + kStagesV;          // [kStagesV] MMA -> loader: the PVs of the stage done
+  uint64_t* s_full = v_empty + kStagesV;          // [kPair] MMA -> softmax g: S tile ready
+  uint64_t* p_full = s_full + kPair;              // [kPair] softmax g -> MMA: P written into TMEM
+  uint64_t* o_done = p_full + kPair;              // [kPair] MMA -> softmax g: one phase per PV
   uint64_t* o_final = o_done + kPair;             // [kPair] MMA -> softmax g: its last PV is done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + kPair);
   int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async loader: block ids of one tile
@@ -405,15 +409,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
 
   if (tid == 0) {
     mbar_init(q_full, kTma ? 1 : kLoaderThreads);
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kStagesK; ++i) {
       mbar_init(&k_full[i], kTma ? 1 : kLoaderThreads);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kStagesV; ++i) {
       mbar_init(&v_full[i], kTma ? 1 : kLoaderThreads);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2 * kPair; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], kSoftmaxThreads);
+    for (int g = 0; g < kPair; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], kSoftmaxThreads);
     }
     for (int g = 0; g < kPair; ++g) {
       mbar_init(&o_done[g], 1);
@@ -433,11 +439,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   bool aborted = false;
 
   if (warp == kLoaderWarp) {
-    // ---------------- loader: both Q tiles once, then K and V tiles into two kStages rings --------
-    // K(i) reuses the stage of tile i-S once its S is done, V(i) that of tile i-S once its PVs
-    // are.  The TMA thread polls both rings; the cp.async warp loads K0 .. K(S-1), then V(i),
-    // K(i+S) for i = 0, 1, ...: the MMA thread issues the PVs of tile i-S before the S of tile i
-    // (S(i) needs PV(i-2) issued), so each blocking wait ends in the order the loads are issued.
+    // ---------------- loader: both Q tiles once, then K and V tiles into their rings --------
+    // K(i) reuses the stage of tile i - kStagesK once its S is done, V(i) that of tile i - kStagesV
+    // once its PVs are.  Loads go in the order K(0 .. kStagesK-1), then V(i), K(i + kStagesK) for
+    // i = 0, 1, ...: the MMA warp issues PV(i - 2) before S(i), so each blocking wait ends in the
+    // order the loads are issued.
     if constexpr (kTma) {
       // Block ids of the split's history pages, resolved once: the pool row of each page's first
       // slot, or a row past the pool for a page at or past `start` (TMA fills it with zeros).
@@ -471,7 +477,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
                         (int)(first + tok0[g]), (int)b);
       const int page_bytes = a.block_size * 128;
       auto load = [&](int i, bool is_v) {
-        const int st = i % kStages;
+        const int stages = is_v ? kStagesV : kStagesK;
+        const int st = i % stages;
+        if (i >= stages) mbar_wait_warp(is_v ? &v_empty[st] : &k_empty[st], ((i / stages) - 1) & 1, aborted);
         uint64_t* full = is_v ? &v_full[st] : &k_full[st];
         uint8_t* dst = smem + (is_v ? kOffV : kOffK) + st * kKvBytes;
         mbar_expect_tx_e(full, kKvBytes);
@@ -482,20 +490,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
             const int row0 = page_rows[i * pages_per_tile + pg];
             for (int c = 0; c < 2; ++c) tma_load_3d_e(dst + c * kKvRegion + pg * page_bytes, map, full, c * 64, h, row0);
           }
-        } else {
+        } else {  // boxes of 64 chunk tokens (rows past the chunk read as zeros)
           const CUtensorMap* map = is_v ? &maps.v_chunk : &maps.k_chunk;
           const int pos = (int)first + (t - hist_tiles) * kTcKv;
-          for (int c = 0; c < 2; ++c) tma_load_4d_e(dst + c * kKvRegion, map, full, c * 64, h, pos, (int)b);
+          for (int sub = 0; sub < kTcKv / 64; ++sub)
+            for (int c = 0; c < 2; ++c)
+              tma_load_4d_e(dst + c * kKvRegion + sub * 64 * 128, map, full, c * 64, h, pos + sub * 64, (int)b);
         }
       };
-      for (int i = 0; i < min(n, kStages); ++i) load(i, false);
+      for (int i = 0; i < min(n, kStagesK); ++i) load(i, false);
       for (int i = 0; i < n; ++i) {
-        if (i >= kStages) mbar_wait_warp(&v_empty[i % kStages], ((i / kStages) - 1) & 1, aborted);
         load(i, true);
-        if (i + kStages < n) {
-          mbar_wait_warp(&k_empty[i % kStages], (i / kStages) & 1, aborted);  // S(i) done
-          load(i + kStages, false);
-        }
+        if (i + kStagesK < n) load(i + kStagesK, false);
       }
     } else {
       const BlockAddr ba{shift, (uint32_t)a.block_size};
@@ -513,82 +519,76 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
       cp_async_arrive_noinc(q_full);
       const int rows_end = (int)tok_end[kPair - 1] > (int)tok_end[0] ? (int)tok_end[kPair - 1] : (int)tok_end[0];
       auto load = [&](int i, bool is_v) {
-        const int st = i % kStages;
-        if (i >= kStages) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i / kStages) - 1) & 1, aborted);
+        const int stages = is_v ? kStagesV : kStagesK;
+        const int st = i % stages;
+        if (i >= stages) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i / stages) - 1) & 1, aborted);
         const int t = t_begin + i;
         const uint32_t dst = sbase + (is_v ? kOffV : kOffK) + st * kKvBytes;
         if (t < hist_tiles) stage_hist_cp<T>(a, ba, b, h, start, t, is_v ? a.v_pool : a.k_pool, dst, lane, pages);
         else stage_chunk_cp(a, b, h, first, t - hist_tiles, rows_end, is_v ? a.v_chunk : a.k_chunk, dst, lane);
         cp_async_arrive_noinc(is_v ? &v_full[st] : &k_full[st]);
       };
-      for (int i = 0; i < min(n, kStages); ++i) load(i, false);
+      for (int i = 0; i < min(n, kStagesK); ++i) load(i, false);
       for (int i = 0; i < n; ++i) {
         load(i, true);
-        if (i + kStages < n) load(i + kStages, false);
+        if (i + kStagesK < n) load(i + kStagesK, false);
       }
     }
   } else if (warp == kMmaWarp) {
-    // ---------------- MMA issuer: S and PV of both row tiles in readiness order ------
+    // ---------------- MMA issuer: the row tiles alternate PV_g(i), S_g(i+1) ----------------
     // The whole warp runs the loop (warp-uniform control flow); elected lanes issue.
     {
       constexpr bool kBf16 = !std::is_same<T, __half>::value;
       const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
       const uint32_t idesc_pv = idesc_f16(kBf16, true, kTcRows, kTcDim);
-      int npv[kPair] = {0, 0};  // PVs issued per row tile
       // Shared-memory descriptors: the start-address field holds address >> 4 (14 bits, every
       // address here is below 256 KiB), so the descriptor of base + off is desc(base) + off / 16.
       const uint64_t dq = desc_kmajor(sbase + kOffQ);
       const uint64_t dk = desc_kmajor(sbase + kOffK);
       const uint64_t dv = desc_mnmajor(sbase + kOffV);
-      auto issue_s = [&](int i) {  // S of tile i for every row tile that has it
-        const int ks = i % kStages;
+      auto issue_s = [&](int g, int i) {  // S_g(i) = Q_g K(i)^T into g's S columns
+        const int ks = i % kStagesK;
         fence_async_smem();
         tc_fence_after();
         const uint64_t dks = dk + (uint64_t)(ks * (kKvBytes >> 4));
-        const uint32_t s_col = (uint32_t)(i & 1) * kTcKv;
 #pragma unroll
-        for (int g = 0; g < kPair; ++g) {
-          if (i >= ng[g]) continue;
-#pragma unroll
-          for (int s = 0; s < kTcDim / 16; ++s)
-            umma_f16(tmem + g * 128 + s_col, dq + (uint64_t)((g * kQBytes + (s >> 2) * kQRegion + (s & 3) * 32) >> 4),
-                     dks + (uint64_t)(((s >> 2) * kKvRegion + (s & 3) * 32) >> 4), idesc_qk, s > 0 ? 1u : 0u);
-          umma_commit(&s_full[g * 2 + (i & 1)]);
-        }
-        umma_commit(&k_empty[ks]);
+        for (int s = 0; s < kTcDim / 16; ++s)
+          umma_f16(tmem + g * 128, dq + (uint64_t)((g * kQBytes + (s >> 2) * kQRegion + (s & 3) * 32) >> 4),
+                   dks + (uint64_t)(((s >> 2) * kKvRegion + (s & 3) * 32) >> 4), idesc_qk, s > 0 ? 1u : 0u);
+        umma_commit(&s_full[g]);
+        // K(i) is free once every row tile that uses tile i has issued its S (row tile 1 issues last)
+        if (g == kPair - 1 || i >= ng[kPair - 1]) umma_commit(&k_empty[ks]);
       };
-      auto issue_pv = [&](int g, int i) {
-        const int vs = i % kStages;
+      auto issue_pv = [&](int g, int i) {  // O_g += P_g(i) V(i)
+        const int vs = i % kStagesV;
         tc_fence_after();
         const uint64_t dvs = dv + (uint64_t)(vs * (kKvBytes >> 4));
-        const uint32_t p_col = tmem + g * 128 + (uint32_t)(i & 1) * kTcKv;
 #pragma unroll
-        for (int s = 0; s < kTcKv / 16; ++s)  // P(i): 16-bit pairs in the S buffer's first 32 columns
-          umma_f16_tmem_a(tmem + kTmemO + g * 128, p_col + s * 8, dvs + (uint64_t)((s * 2048) >> 4), idesc_pv,
-                          (i > 0 || s > 0) ? 1u : 0u);
+        for (int s = 0; s < kTcKv / 16; ++s)  // P: 16-bit pairs in the first 64 of g's S columns
+          umma_f16_tmem_a(tmem + kTmemO + g * 128, tmem + g * 128 + s * 8, dvs + (uint64_t)((s * 2048) >> 4),
+                          idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
         umma_commit(&o_done[g]);
-        ++npv[g];
-        const int o = 1 - g;  // V(i) is free once every row tile that uses tile i has issued its PV
-        if (npv[o] > i || i >= ng[o]) umma_commit(&v_empty[vs]);
-        if (npv[g] == ng[g]) umma_commit(&o_final[g]);
+        if (g == kPair - 1 || i >= ng[kPair - 1]) umma_commit(&v_empty[vs]);
+        if (i + 1 == ng[g]) umma_commit(&o_final[g]);
       };
-      // Fixed order S(i+1), PV_0(i), PV_1(i): S(i+1) needs the S buffers of tile i-1, whose PVs
-      // were issued in the previous step, so only the PVs wait (for softmax); the waits suspend
-      // the warp instead of spinning.
+      // S_g(i+1) overwrites P_g(i) in g's S columns, so it follows PV_g(i); the waits suspend the
+      // warp instead of spinning.
       mbar_wait_warp(q_full, 0, aborted);
       mbar_wait_warp(&k_full[0], 0, aborted);
-      issue_s(0);
+#pragma unroll
+      for (int g = 0; g < kPair; ++g)
+        if (ng[g] > 0) issue_s(g, 0);
       for (int i = 0; i < n; ++i) {
-        if (i + 1 < n) {
-          mbar_wait_warp(&k_full[(i + 1) % kStages], ((i + 1) / kStages) & 1, aborted);
-          issue_s(i + 1);
-        }
 #pragma unroll
         for (int g = 0; g < kPair; ++g) {
           if (i >= ng[g]) continue;
-          mbar_wait_warp(&p_full[g * 2 + (i & 1)], (i >> 1) & 1, aborted);
-          mbar_wait_warp(&v_full[i % kStages], (i / kStages) & 1, aborted);
+          mbar_wait_warp(&p_full[g], i & 1, aborted);
+          mbar_wait_warp(&v_full[i % kStagesV], (i / kStagesV) & 1, aborted);
           issue_pv(g, i);
+          if (i + 1 < ng[g]) {
+            mbar_wait_warp(&k_full[(i + 1) % kStagesK], ((i + 1) / kStagesK) & 1, aborted);
+            issue_s(g, i + 1);
+          }
         }
       }
     }
@@ -608,7 +608,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     const float scale = a.scale_log2;
     float m_ref = -INFINITY, l_run = 0.f;
     for (int i = 0; i < my_n; ++i) {
-      const int st = i & 1;
       const int t = t_begin + i;
       // visible columns of this tile: history keys below `start`; chunk keys up to the row's token
       bool full;
@@ -621,16 +620,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         lim = row_valid ? (int)my_tok + 1 - k0 : 0;
         full = k0 + kTcKv <= (int)my_tok0 + 1;
       }
-      mbar_wait(&s_full[g * 2 + st], (i >> 1) & 1, aborted);
+      mbar_wait(&s_full[g], i & 1, aborted);
       tc_fence_after();
-      const uint32_t s_addr = tmem + s_col + st * kTcKv + lane_base;
-      uint32_t sr[2][32];
-      tmem_ld32_async(s_addr, sr[0]);
-      tmem_ld32_async(s_addr + 32, sr[1]);
+      const uint32_t s_addr = tmem + s_col + lane_base;
+      uint32_t sr[kTcKv / 32][32];
+#pragma unroll
+      for (int c = 0; c < kTcKv / 32; ++c) tmem_ld32_async(s_addr + c * 32, sr[c]);
       tmem_wait_ld();
       if (!full) {  // uniform for the warpgroup: only tiles that cross a causal or history end are masked
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < kTcKv / 32; ++c) {
 #pragma unroll
           for (int e = 0; e < 32; ++e)
             if (c * 32 + e >= lim) sr[c][e] = 0xff800000u;  // -inf: exp2 gives 0 below
@@ -638,17 +637,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
       }
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kTcKv / 32; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[c][e]));
       }
       const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
       const float m_new = fmaxf(m_ref, tile_max);
       const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
+      const float alpha = need ? fast_exp2(m_ref - m_new) : 1.f;
+      if (need) {
+        l_run *= alpha;
+        m_ref = m_new;
+      } else if (m_ref == -INFINITY) {
+        m_ref = m_new;
+      }
+      const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;  // a row with nothing visible yet: all -inf
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      // P as the A operand of PV: 16-bit pairs over the first 64 S columns, 32 scores (16
+      // columns) per store; every S value is in registers before the first store.
+#pragma unroll
+      for (int c = 0; c < kTcKv / 32; ++c) {
+        uint32_t pw[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          // branch-free: every exponent is independent, so the ex2 issue overlaps
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * j]), scale, neg_m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * j + 1]), scale, neg_m));
+          ps[j & 3] += p0 + p1;
+          pw[j] = pack2<T>(p0, p1);
+        }
+        tmem_st16_async(s_addr + c * 16, pw);
+      }
+      l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      // The running O is rescaled after P is out of registers; PV(i) waits for both.
       if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access
         mbar_wait(&o_done[g], (i - 1) & 1, aborted);  // PV(i-1) of this row tile finished writing O
         tc_fence_after();
-        const float alpha = need ? fast_exp2(m_ref - m_new) : 1.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           float ov[32];
@@ -658,29 +682,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
           tmem_st32(tmem + o_col + lane_base + c * 32, ov);
         }
       }
-      if (need) {
-        l_run *= fast_exp2(m_ref - m_new);
-        m_ref = m_new;
-      } else if (m_ref == -INFINITY) {
-        m_ref = m_new;
-      }
-      const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;  // a row with nothing visible yet: all -inf
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pw[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        // branch-free: every exponent is independent, so the ex2 issue overlaps
-        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[j >> 4][(2 * j) & 31]), scale, neg_m));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[j >> 4][(2 * j + 1) & 31]), scale, neg_m));
-        ps[j & 3] += p0 + p1;
-        pw[j] = pack2<T>(p0, p1);
-      }
-      l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      // P(i) as the A operand of PV: 16-bit pairs over the S buffer's first 32 columns (S(i) is in
-      // registers already; S(i+2) overwrites them only after PV(i), issued before it, has read them)
-      tmem_st32(s_addr, pw);
+      tmem_wait_st();
       tc_fence_before();  // our tcgen05.ld of S / st of P and O before the next MMAs
-      mbar_arrive(&p_full[g * 2 + st]);
+      mbar_arrive(&p_full[g]);
     }
     // ---- epilogue (a row tile without tiles in this split writes nothing here) ----
     if (my_n > 0) {
