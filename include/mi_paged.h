@@ -153,8 +153,9 @@ int mi_paged_decode_static_scratch(const void* q, const int64_t* q_strides, cons
  *            b*q_strides[0] + p*q_strides[1] + h*q_strides[2] + d
  *   k_chunk  [batch, padded_len, num_kv_heads, head_dim], strides kv_strides[0..2] (v_chunk same)
  *   out      [batch, padded_len, num_q_heads*head_dim] contiguous
- *   workspace  >= mi_paged_prefill_workspace_size(...) bytes, 256-byte aligned (split-KV partials
- *            of long histories; the size depends only on the arguments of that function)
+ *   workspace  >= mi_paged_prefill_workspace_size(...) bytes, 256-byte aligned (partials of the
+ *            work units that straddle two persistent CTAs, ~39 MB for the tensor-core path; the
+ *            size depends only on the arguments of that function)
  */
 size_t mi_paged_prefill_workspace_size(int64_t batch, int64_t padded_len, int num_q_heads, int num_kv_heads,
                                        int head_dim, int64_t table_stride, int block_size, int dtype);

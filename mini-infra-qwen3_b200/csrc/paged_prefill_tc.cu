@@ -1,20 +1,20 @@
 // Chunked-prefill paged attention on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
 // Variant: bf16 / fp16, head_dim 128, any block size, G = Hq/H_kv in {1, 2, 4, 8}.
-// One CTA (320 threads, one CTA per SM) = one (sequence, KV head, pair of tiles of 128 query
-// rows, KV split).  A row tile packs 128/G chunk tokens x the G query heads of the KV head (row
-// r = token r/G, head r%G); the CTA's two row tiles are consecutive, so every K/V tile staged in
+// Persistent CTAs (320 threads, one per SM) share the work as equal ranges of one stream of KV
+// tiles (see TcWalker below).  A unit of that stream is one (sequence, pair of tiles of 128 query
+// rows, KV head): a row tile packs 128/G chunk tokens x the G query heads of the KV head (row
+// r = token r/G, head r%G); the unit's two row tiles are consecutive, so every K/V tile staged in
 // shared memory serves 2 x 128 query rows of the whole GQA group (half the L2 -> SM bytes per
-// FLOP of one row tile per CTA).  The KV range of a row tile (history tiles, then causal chunk
-// tiles) is cut into equal splits of at most kTilesPerSplit 128-position tiles so that long
-// histories spread over many CTAs of equal work; the two row tiles' ranges differ only in their
-// last chunk tiles, so the CTA stages the union and each row tile uses a prefix of it.  A row
-// tile with one split writes its output directly, otherwise each split writes an unnormalised
-// partial (O, m, l) that prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
-//   warp 0 (loader): both Q tiles once, then K and V tiles into a kStagesK-deep K ring and a
+// FLOP of one row tile per CTA).  The KV range of a row tile is its history tiles, then its causal
+// chunk tiles; the two row tiles' ranges differ only in their last chunk tiles, so the CTA stages
+// the union and each row tile uses a prefix of it.  A unit inside one CTA's range writes its
+// output directly; a unit cut by CTA boundaries leaves unnormalised partials (O, m, l) that
+// prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
+//   warp 0 (loader): per unit both Q tiles, then K and V tiles into a kStagesK-deep K ring and a
 //      kStagesV-deep V ring (K is free once the S of both row tiles is done, V once both PVs
-//      are).  With tensor maps (block size 16/32/64) the split's block ids are first resolved
-//      into shared memory, then an elected lane issues TMA copies: one 3D box per pool page of a
+//      are).  With tensor maps (block size 16/32/64) the block ids of a tile's pages are read one
+//      K load ahead, then an elected lane issues TMA copies: one 3D box per pool page of a
 //      history tile (a page past `start` reads rows past the pool, which TMA fills with zeros)
 //      and 4D boxes of 64 tokens for a chunk tile; otherwise the warp stages rows with cp.async;
 //   warp 1 (MMA, elected lane): per row tile g, S_g = Q_g K^T as 8 tcgen05.mma (M=128, N=128,
@@ -56,10 +56,10 @@ constexpr int kTcKv = 128;                          // KV positions per tile (MM
 constexpr int kTcDim = 128;                         // head_dim
 constexpr int kSoftmaxThreads = 128;                // one warpgroup per row tile
 constexpr int kTcThreads = 64 + kPair * kSoftmaxThreads;  // warp 0 loader, warp 1 MMA, then the warpgroups
+constexpr int kFirstSoftmaxWarp = 2;
 constexpr int kLoaderWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kLoaderThreads = 32;
-constexpr int kTilesPerSplit = 16;                  // 2048 KV positions per CTA at most
 constexpr int kStagesK = 3;                         // depth of the K ring
 constexpr int kStagesV = 2;                         // depth of the V ring
 constexpr int kQRegion = kTcRows * 128;             // 16 KiB: one 64-column half of a Q tile
@@ -233,23 +233,21 @@ struct BlockAddr {
 // read from the pool), then the chunk tiles (chunk tokens [128k, 128k + 128) of [0, tok_end), read
 // from the chunk's own K/V).  Keeping the two apart aligns every tile to its source, so each one is
 // a few whole TMA boxes: pool pages [64 x 1 x block_size] or [64 x 1 x 64 x 1] chunk boxes.
-struct TcGeometry {
-  int64_t len, first;
+struct TcRow {  // one sequence: chunk placement and history length, clamped to the arguments
+  int len, first;  // positions are below 2^30 (prefill_tc_supported)
   int start;
   int hist_tiles;  // ceil(start / kTcKv)
-  int n_tiles;     // history tiles + chunk tiles up to the causal end of the tile's last token
 };
 
-__device__ __forceinline__ TcGeometry tc_geometry(const PrefillArgs& a, int64_t b, int64_t tok0, int tokens_per_tile,
-                                                  bool report) {
-  TcGeometry g;
+__device__ __forceinline__ TcRow tc_row(const PrefillArgs& a, int64_t b, bool report) {
+  TcRow g;
   int64_t len = a.chunk_lens[b];
   if (len > a.padded_len) {
     if (report) record_status(MI_STATUS_BAD_LENGTH);
     len = a.padded_len;
   }
-  g.len = len < 0 ? 0 : len;
-  g.first = a.padded_len - g.len;
+  g.len = len < 0 ? 0 : (int)len;
+  g.first = (int)a.padded_len - g.len;
   int64_t start = a.starts[b];
   if (start < 0) start = 0;
   if (start > a.table_stride * a.block_size) {
@@ -258,28 +256,100 @@ __device__ __forceinline__ TcGeometry tc_geometry(const PrefillArgs& a, int64_t 
   }
   g.start = (int)start;
   g.hist_tiles = (int)((start + kTcKv - 1) / kTcKv);
-  const int64_t tok_end = min(g.len, tok0 + tokens_per_tile);
-  g.n_tiles = tok0 < g.len ? g.hist_tiles + (int)((tok_end + kTcKv - 1) / kTcKv) : 0;
   return g;
 }
 
-// Equal-size splits of a row-tile pair: the union of the pair's tile ranges (the second tile's,
-// which is never shorter unless it is empty) is cut into ceil(tiles / kTilesPerSplit) parts of
-// `per` tiles (the last one shorter), so a row's CTAs carry equal work and the grid's tail is
-// short.  Row tile g's splits are the parts that start below its own tile count.
-struct TcSplits {
-  int per;         // tiles per split
-  int splits[2];   // splits holding tiles of row tile 0 / 1
+// Work distribution ("stream-K" per KV head).  A unit of work is (sequence b, row-tile pair p) of
+// one KV head; its KV tiles are the union of the two row tiles' ranges (history tiles, then chunk
+// tiles up to the causal end of the row tile's last token; the second row tile's range is never
+// shorter unless it is empty), the same for every head.  The units u = b * pairs + p of a head
+// laid end to end form a stream of T tiles; the grid is R CTAs per head, CTA c = r * hkv + h, and
+// with R' = min(R, T) the CTA takes tiles [r*T/R', (r+1)*T/R') of head h's stream, walking them
+// unit after unit with its K/V rings, TMEM and barrier phases carried across unit boundaries.  The
+// hkv CTAs of one r read the same pool pages at the same time (the heads of a page row are
+// adjacent in memory).  A unit inside one CTA's range writes its output directly; a unit cut by
+// CTA boundaries leaves one unnormalised partial (O, m, l) per piece -- the piece that opens the
+// unit (CTA r0) in slot 2*c(r0) + 1, the piece in CTA r (r0 < r <= r1) in slot 2*c(r) -- and CTA
+// r0 records the unit in its descriptor for prefill_combine_kernel.
+struct TcPair {  // one (sequence, row-tile pair)
+  int b;
+  int pair;
+  TcRow row;
+  int tok0[kPair], tok_end[kPair];  // chunk tokens of each row tile
+  int n_tiles[kPair];
+  int n;  // union of the two ranges
 };
-__device__ __forceinline__ TcSplits tc_splits(int n_tiles0, int n_tiles1) {
-  TcSplits sp;
-  const int nu = max(n_tiles0, n_tiles1);
-  const int parts = max(1, (nu + kTilesPerSplit - 1) / kTilesPerSplit);
-  sp.per = max(1, (nu + parts - 1) / parts);
-  sp.splits[0] = (n_tiles0 + sp.per - 1) / sp.per;
-  sp.splits[1] = (n_tiles1 + sp.per - 1) / sp.per;
-  return sp;
+
+__device__ __forceinline__ TcPair tc_pair(const PrefillArgs& a, int rp, int pairs) {
+  TcPair u;
+  u.b = rp / pairs;
+  u.pair = rp - u.b * pairs;
+  u.row = tc_row(a, u.b, false);
+  const int tpt = kTcRows / a.groups;
+#pragma unroll
+  for (int g = 0; g < kPair; ++g) {
+    u.tok0[g] = (u.pair * kPair + g) * tpt;
+    u.tok_end[g] = min(u.row.len, u.tok0[g] + tpt);
+    u.n_tiles[g] = u.tok0[g] < u.row.len ? u.row.hist_tiles + (int)((u.tok_end[g] + kTcKv - 1) / kTcKv) : 0;
+  }
+  u.n = max(u.n_tiles[0], u.n_tiles[1]);
+  return u;
 }
+
+struct TcItem {  // one piece of a unit inside one CTA's range
+  TcPair u;
+  int h;
+  int t_begin;     // first tile of the piece within the unit
+  int n;           // tiles of the piece
+  int ng[kPair];   // tiles of row tile g in the piece: [t_begin, t_begin + ng[g])
+  int slot;        // partial slot, or -1 when the piece is the whole unit
+};
+
+struct TcWalker {  // position in a head's tile stream, advanced item by item
+  int rp, rows;      // current row-tile pair, number of pairs in the batch (below 2^31: prefill_tc_supported)
+  int h, off;        // KV head; tile offset of the position within its unit
+  int left;          // tiles left in the CTA's range
+  int pairs, cta;
+  __device__ __forceinline__ bool next(const PrefillArgs& a, TcItem& it) {
+    if (left <= 0) return false;
+    it.u = tc_pair(a, rp, pairs);
+    it.h = h;
+    it.t_begin = off;
+    it.n = min(it.u.n - off, left);
+#pragma unroll
+    for (int g = 0; g < kPair; ++g) it.ng[g] = max(0, min(it.u.n_tiles[g] - off, it.n));
+    const bool opened_before = off > 0, continues = off + it.n < it.u.n;
+    it.slot = opened_before ? 2 * cta : (continues ? 2 * cta + 1 : -1);
+    left -= it.n;
+    off += it.n;
+    if (off == it.u.n) {  // on to the next unit with tiles
+      off = 0;
+      while (left > 0 && ++rp < rows && tc_pair(a, rp, pairs).n == 0) {
+      }
+    }
+    return true;
+  }
+};
+
+// A tile cursor: the item of the stream position and the tile's index within the item.
+struct TcCursor {
+  TcWalker w;
+  TcItem it;
+  int i;
+  bool valid;
+  __device__ __forceinline__ void init(const TcWalker& w0, const PrefillArgs& a) {
+    w = w0;
+    i = 0;
+    valid = w.next(a, it);
+  }
+  __device__ __forceinline__ void advance(const PrefillArgs& a) {
+    if (++i == it.n) {
+      i = 0;
+      valid = w.next(a, it);
+    }
+  }
+  __device__ __forceinline__ bool last_of_item() const { return i + 1 == it.n; }
+};
 
 // cp.async staging (block sizes without a TMA box) of the K or the V rows of history tile k =
 // positions [128k, 128k + 128) from `pool`; rows at or past `start` zero-filled; block ids of the
@@ -341,17 +411,92 @@ __device__ __forceinline__ float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 3-input maximum (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Zeros for the padding positions (left of the chunk) of rows b = blockIdx.x (mod gridDim.x), all
+// query heads.
+template <typename T>
+__device__ __forceinline__ void zero_padding(const PrefillArgs& a, int tid) {
+  const int64_t row_elems = (int64_t)a.hq * kTcDim;
+  for (int64_t b = blockIdx.x; b < a.batch; b += gridDim.x) {
+    const int64_t first = tc_row(a, b, tid == 0).first;
+    const int64_t units = first * row_elems * (int64_t)sizeof(T) / 16;  // 16-byte stores
+    uint4* dst = reinterpret_cast<uint4*>(a.out + b * a.padded_len * row_elems * (int64_t)sizeof(T));
+    for (int64_t i = tid; i < units; i += kTcThreads) dst[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Work range of this CTA (all threads): the per-pair tile counts are summed in per-thread chunks
+// of pairs and scanned across the block (`scratch`: 16 int64 of shared memory), then the thread
+// whose chunk holds the CTA's first tile locates it.  Returns the walker at that position, the
+// tiles of a head's stream (`total`) and the CTAs per head that share them (`ctas`).
+__device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, int64_t* scratch, int tid, int64_t& total,
+                                             int64_t& ctas) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int rows = (int)(a.batch * pairs);
+  const int r0 = (int)((int64_t)rows * tid / kTcThreads), r1 = (int)((int64_t)rows * (tid + 1) / kTcThreads);
+  int64_t mine = 0;
+  for (int rp = r0; rp < r1; ++rp) mine += tc_pair(a, rp, pairs).n;
+  int64_t x = mine;  // inclusive scan within the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  int64_t before = 0;
+  total = 0;
+  for (int w = 0; w < kTcThreads / 32; ++w) {
+    const int64_t v = scratch[w];
+    if (w < warp) before += v;
+    total += v;
+  }
+  const int64_t excl = before + x - mine;  // tiles ahead of this thread's chunk
+  ctas = min((int64_t)(gridDim.x / a.hkv), total);
+  const int64_t c = blockIdx.x / a.hkv;  // range index within the head
+  const int64_t x0 = c < ctas ? c * total / ctas : 0;
+  const int64_t x1 = c < ctas ? (c + 1) * total / ctas : 0;
+  __syncthreads();  // every warp total read before the start is written over them
+  if (c < ctas && excl <= x0 && x0 < excl + mine) {
+    int64_t pos = excl;
+    for (int rp = r0; rp < r1; ++rp) {
+      const int n = tc_pair(a, rp, pairs).n;
+      if (x0 < pos + n) {
+        scratch[0] = rp;
+        scratch[1] = x0 - pos;
+        break;
+      }
+      pos += n;
+    }
+  }
+  __syncthreads();
+  TcWalker w;
+  w.rows = rows;
+  w.pairs = pairs;
+  w.cta = (int)blockIdx.x;
+  w.left = (int)(x1 - x0);
+  w.rp = w.left > 0 ? (int)scratch[0] : 0;
+  w.h = (int)(blockIdx.x % a.hkv);
+  w.off = w.left > 0 ? (int)scratch[1] : 0;
+  return w;
+}
 
 template <typename T, bool kTma>
 __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const PrefillArgs a,
                                                                     const __grid_constant__ PrefillMaps maps,
-                                                                    float* ws_o, float* ws_ml, int max_splits,
-                                                                    int qtiles, int shift) {
+                                                                    float* ws_o, float* ws_ml, int64_t* ws_desc,
+                                                                    int pairs, int shift) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars + 0;                    // loader -> MMA: both Q tiles landed
+  uint64_t* q_full = bars + 0;                    // loader -> MMA: both Q tiles of the item landed
   uint64_t* k_full = bars + 1;                    // [kStagesK] loader -> MMA: K stage landed
   uint64_t* k_empty = k_full + kStagesK;          // [kStagesK] MMA -> loader: the S of the stage done
   uint64_t* v_full = k_empty + kStagesK;          // [kStagesV] loader -> MMA: V stage landed
@@ -359,53 +504,41 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   uint64_t* s_full = v_empty + kStagesV;          // [kPair] MMA -> softmax g: S tile ready
   uint64_t* p_full = s_full + kPair;              // [kPair] softmax g -> MMA: P written into TMEM
   uint64_t* o_done = p_full + kPair;              // [kPair] MMA -> softmax g: one phase per PV
-  uint64_t* o_final = o_done + kPair;             // [kPair] MMA -> softmax g: its last PV is done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + kPair);
-  int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async loader: block ids of one tile
+  uint64_t* o_final = o_done + kPair;             // [kPair] MMA -> softmax g: the item's last PV is done
+  uint64_t* o_free = o_final + kPair;             // [kPair] softmax g -> MMA: the item's O read out of TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + kPair);
+  int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async: block ids; TMA: page-row ring
 
-  const int pair = blockIdx.x / max_splits;
-  const int split = blockIdx.x % max_splits;
-  const int h = blockIdx.y;
-  const int64_t b = blockIdx.z;
-  const int G = a.groups;
-  const int tokens_per_tile = kTcRows / G;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  // row tile g of this CTA = q-tile 2*pair + g; both share the row's history and chunk geometry
-  int64_t tok0[kPair], tok_end[kPair];
-  int n_tiles[kPair], ng[kPair];
-  TcGeometry geo{};
-#pragma unroll
-  for (int g = 0; g < kPair; ++g) {
-    tok0[g] = (int64_t)(pair * kPair + g) * tokens_per_tile;
-    geo = tc_geometry(a, b, tok0[g], tokens_per_tile, g == 0 && tid == 0 && blockIdx.x == 0 && h == 0);
-    n_tiles[g] = geo.n_tiles;
-    tok_end[g] = min(geo.len, tok0[g] + tokens_per_tile);
-  }
-  const TcSplits sp = tc_splits(n_tiles[0], n_tiles[1]);
-  const int t_begin = split * sp.per;
-#pragma unroll
-  for (int g = 0; g < kPair; ++g) ng[g] = max(0, min(n_tiles[g], t_begin + sp.per) - t_begin);  // this split's tiles
-  const int64_t first = geo.first;
-  const int start = geo.start;
-  const int hist_tiles = geo.hist_tiles;
+  const int G = a.groups;
   const int row_elems = a.hq * kTcDim;  // elements per output position
   T* out = reinterpret_cast<T*>(a.out);
 
-  // Padding positions of this KV head's query heads are zeros (written by pair 0, split 0).
-  if (blockIdx.x == 0) {
-    const int per_pos = G * (kTcDim / 8);
-    for (int64_t i = tid; i < first * per_pos; i += kTcThreads) {
-      const int64_t p = i / per_pos;
-      const int rem = (int)(i - p * per_pos);
-      *reinterpret_cast<uint4*>(out + (b * a.padded_len + p) * row_elems + (int64_t)(h * G) * kTcDim + rem * 8) =
-          make_uint4(0, 0, 0, 0);
+  zero_padding<T>(a, tid);
+  int64_t total, ctas;
+  const TcWalker walk0 = tc_start(a, pairs, reinterpret_cast<int64_t*>(smem + kOffK), tid, total, ctas);
+  if (tid == 0) {  // the unit this CTA opens and leaves unfinished, for the combine kernel
+    int64_t d0 = -1, d1 = 0, d2 = 0;
+    TcWalker w = walk0;
+    TcItem it;
+    const int64_t r = blockIdx.x / a.hkv;
+    int64_t pos = r * total / max(ctas, (int64_t)1);
+    while (w.next(a, it)) {
+      if (it.slot == 2 * (int)blockIdx.x + 1) {  // t_begin == 0: the unit ends at pos + its tiles
+        d0 = it.u.b * pairs + it.u.pair;
+        d1 = it.h;
+        d2 = ((pos + it.u.n) * ctas - 1) / total * a.hkv + it.h;  // CTA of the unit's last tile
+      }
+      pos += it.n;
     }
+    ws_desc[blockIdx.x * 4 + 0] = d0;
+    ws_desc[blockIdx.x * 4 + 1] = d1;
+    ws_desc[blockIdx.x * 4 + 2] = d2;
   }
-  const int n = max(ng[0], ng[1]);  // tiles staged: the union (a prefix of this split's tiles for each g)
-  if (n == 0) return;               // uniform for the CTA
-  const int t_end = t_begin + n;
+  if (walk0.left == 0) return;  // uniform for the CTA
+  const int64_t n_tiles = walk0.left;
 
   if (tid == 0) {
     mbar_init(q_full, kTma ? 1 : kLoaderThreads);
@@ -420,10 +553,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     for (int g = 0; g < kPair; ++g) {
       mbar_init(&s_full[g], 1);
       mbar_init(&p_full[g], kSoftmaxThreads);
-    }
-    for (int g = 0; g < kPair; ++g) {
       mbar_init(&o_done[g], 1);
       mbar_init(&o_final[g], 1);
+      mbar_init(&o_free[g], kSoftmaxThreads);
     }
     fence_mbar_init();
   }
@@ -439,115 +571,182 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   bool aborted = false;
 
   if (warp == kLoaderWarp) {
-    // ---------------- loader: both Q tiles once, then K and V tiles into their rings --------
-    // K(i) reuses the stage of tile i - kStagesK once its S is done, V(i) that of tile i - kStagesV
-    // once its PVs are.  Loads go in the order K(0 .. kStagesK-1), then V(i), K(i + kStagesK) for
-    // i = 0, 1, ...: the MMA warp issues PV(i - 2) before S(i), so each blocking wait ends in the
-    // order the loads are issued.
+    // ---------------- loader: per item both Q tiles, then K and V tiles into their rings ----------
+    // K(j) reuses the stage of tile j - kStagesK once its S is done, V(j) that of tile j - kStagesV
+    // once its PVs are (j counts the CTA's tiles across items).  Loads go in the order
+    // K(0 .. kStagesK-1), then V(j), K(j + kStagesK) for j = 0, 1, ...: the MMA warp issues PV(j - 2)
+    // before S(j), so each blocking wait ends in the order the loads are issued.  The Q tiles of
+    // an item are loaded once every S of the previous item is done (K(j) free, j its last tile).
+    TcCursor ck, cv;  // tiles of the next K load and of the next V load
+    ck.init(walk0, a);
+    cv.init(walk0, a);
     if constexpr (kTma) {
-      // Block ids of the split's history pages, resolved once: the pool row of each page's first
-      // slot, or a row past the pool for a page at or past `start` (TMA fills it with zeros).
-      int* page_rows = reinterpret_cast<int*>(pages);
-      const int pages_per_tile = kTcKv / a.block_size;
-      const int num_slots = (int)(a.num_blocks * a.block_size);
-      const int n_pages = max(0, min(t_end, hist_tiles) - t_begin) * pages_per_tile;
-      const int64_t* table = a.block_tables + b * a.table_stride;
-      for (int j = lane; j < n_pages; j += 32) {
-        const int pos0 = t_begin * kTcKv + j * a.block_size;
-        int row0 = num_slots;
-        if (pos0 < start) {
-          const int64_t blk = table[pos0 >> shift];
-          if (blk < 0 || blk >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
-          else row0 = (int)(blk * a.block_size);
-        }
-        page_rows[j] = row0;
-      }
-      __syncwarp();
-      // the whole warp runs the issue loop; elected lanes issue the copies
       if (lane == 0) {
         tma_prefetch_desc(&maps.q);
         tma_prefetch_desc(&maps.k_chunk);
         tma_prefetch_desc(&maps.v_chunk);
+        tma_prefetch_desc(&maps.k_pool);
+        tma_prefetch_desc(&maps.v_pool);
       }
       __syncwarp();
-      mbar_expect_tx_e(q_full, kPair * kQBytes);
-      for (int g = 0; g < kPair; ++g)  // box [64 d, G heads, 128/G tokens]: row = token * G + head
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d_e(smem + kOffQ + g * kQBytes + c * kQRegion, &maps.q, q_full, c * 64, h * G,
-                        (int)(first + tok0[g]), (int)b);
+      // Pool rows of the pages of the tiles in flight: ring of 8 tiles x 8 pages (int32), written at
+      // the K load of a tile and read again at its V load.  The block ids of the next K tile's
+      // pages are loaded one K load ahead (lane pg holds page pg), so their latency is hidden.
+      int* page_ring = reinterpret_cast<int*>(pages);
+      const int pages_per_tile = kTcKv / a.block_size;
+      const int num_slots = (int)(a.num_blocks * a.block_size);
       const int page_bytes = a.block_size * 128;
-      auto load = [&](int i, bool is_v) {
+      int64_t pend = 0;
+      bool pend_valid = false;
+      auto fetch_pages = [&](const TcCursor& c) {  // block ids of the pages of c's tile (history tiles)
+        pend_valid = false;
+        if (!c.valid || lane >= pages_per_tile) return;
+        const int t = c.it.t_begin + c.i;
+        const int pos0 = t * kTcKv + lane * a.block_size;
+        if (t < c.it.u.row.hist_tiles && pos0 < c.it.u.row.start) {
+          pend = a.block_tables[c.it.u.b * a.table_stride + (pos0 >> shift)];
+          pend_valid = true;
+        }
+      };
+      auto load_q = [&](const TcItem& it) {
+        mbar_expect_tx_e(q_full, kPair * kQBytes);
+        for (int g = 0; g < kPair; ++g)  // box [64 d, G heads, 128/G tokens]: row = token * G + head
+          for (int c = 0; c < 2; ++c)
+            tma_load_4d_e(smem + kOffQ + g * kQBytes + c * kQRegion, &maps.q, q_full, c * 64, it.h * G,
+                          (int)(it.u.row.first + it.u.tok0[g]), (int)it.u.b);
+      };
+      auto issue_tile = [&](const TcCursor& c, int64_t j, bool is_v) {
         const int stages = is_v ? kStagesV : kStagesK;
-        const int st = i % stages;
-        if (i >= stages) mbar_wait_warp(is_v ? &v_empty[st] : &k_empty[st], ((i / stages) - 1) & 1, aborted);
+        const int st = (int)(j % stages);
         uint64_t* full = is_v ? &v_full[st] : &k_full[st];
         uint8_t* dst = smem + (is_v ? kOffV : kOffK) + st * kKvBytes;
         mbar_expect_tx_e(full, kKvBytes);
-        const int t = t_begin + i;
-        if (t < hist_tiles) {
+        const int t = c.it.t_begin + c.i;
+        const int h = c.it.h;
+        if (t < c.it.u.row.hist_tiles) {
           const CUtensorMap* map = is_v ? &maps.v_pool : &maps.k_pool;
+          const int* rows = page_ring + (j & 7) * 8;
           for (int pg = 0; pg < pages_per_tile; ++pg) {
-            const int row0 = page_rows[i * pages_per_tile + pg];
-            for (int c = 0; c < 2; ++c) tma_load_3d_e(dst + c * kKvRegion + pg * page_bytes, map, full, c * 64, h, row0);
+            const int row0 = rows[pg];
+            for (int cc = 0; cc < 2; ++cc)
+              tma_load_3d_e(dst + cc * kKvRegion + pg * page_bytes, map, full, cc * 64, h, row0);
           }
         } else {  // boxes of 64 chunk tokens (rows past the chunk read as zeros)
           const CUtensorMap* map = is_v ? &maps.v_chunk : &maps.k_chunk;
-          const int pos = (int)first + (t - hist_tiles) * kTcKv;
+          const int pos = (int)c.it.u.row.first + (t - c.it.u.row.hist_tiles) * kTcKv;
           for (int sub = 0; sub < kTcKv / 64; ++sub)
-            for (int c = 0; c < 2; ++c)
-              tma_load_4d_e(dst + c * kKvRegion + sub * 64 * 128, map, full, c * 64, h, pos + sub * 64, (int)b);
+            for (int cc = 0; cc < 2; ++cc)
+              tma_load_4d_e(dst + cc * kKvRegion + sub * 64 * 128, map, full, cc * 64, h, pos + sub * 64,
+                            (int)c.it.u.b);
         }
       };
-      for (int i = 0; i < min(n, kStagesK); ++i) load(i, false);
-      for (int i = 0; i < n; ++i) {
-        load(i, true);
-        if (i + kStagesK < n) load(i + kStagesK, false);
+      int64_t jk = 0;  // tiles whose K is loaded
+      auto load_k = [&]() {
+        if (jk >= kStagesK) mbar_wait_warp(&k_empty[jk % kStagesK], ((jk / kStagesK) - 1) & 1, aborted);
+        if (lane < pages_per_tile) {  // pool rows of this tile's pages (a row past the pool reads zeros)
+          int row0 = num_slots;
+          if (pend_valid) {
+            if (pend < 0 || pend >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
+            else row0 = (int)(pend * a.block_size);
+          }
+          page_ring[(jk & 7) * 8 + lane] = row0;
+        }
+        __syncwarp();
+        issue_tile(ck, jk, false);
+        ++jk;
+        ck.advance(a);
+        fetch_pages(ck);
+      };
+      fetch_pages(ck);
+      load_q(cv.it);
+      for (int64_t j = 0; j < min(n_tiles, (int64_t)kStagesK); ++j) load_k();
+      for (int64_t j = 0; j < n_tiles; ++j) {
+        if (j >= kStagesV) mbar_wait_warp(&v_empty[j % kStagesV], ((j / kStagesV) - 1) & 1, aborted);
+        issue_tile(cv, j, true);
+        if (cv.last_of_item() && j + 1 < n_tiles) {  // next item's Q once every S of this one is done
+          mbar_wait_warp(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
+          cv.advance(a);
+          load_q(cv.it);
+        } else {
+          cv.advance(a);
+        }
+        if (j + kStagesK < n_tiles) load_k();
       }
     } else {
       const BlockAddr ba{shift, (uint32_t)a.block_size};
       const int unit = lane & 15;
-      for (int g = 0; g < kPair; ++g) {
-        for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
-          const int64_t tok = tok0[g] + r / G;
-          const bool valid = tok < tok_end[g];
-          const char* src = a.q;
-          if (valid)
-            src = a.q + b * a.q_sb[0] + (first + tok) * a.q_sb[1] + (int64_t)(h * G + r % G) * a.q_sb[2] + unit * 16;
-          cp_async16(sbase + kOffQ + g * kQBytes + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src, valid);
+      auto load_q = [&](const TcItem& it) {
+        for (int g = 0; g < kPair; ++g) {
+          for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
+            const int64_t tok = it.u.tok0[g] + r / G;
+            const bool valid = tok < it.u.tok_end[g];
+            const char* src = a.q;
+            if (valid)
+              src = a.q + it.u.b * a.q_sb[0] + (it.u.row.first + tok) * a.q_sb[1] +
+                    (int64_t)(it.h * G + r % G) * a.q_sb[2] + unit * 16;
+            cp_async16(sbase + kOffQ + g * kQBytes + sw128_offset((uint32_t)r, (uint32_t)unit, kQRegion), src,
+                       valid);
+          }
         }
-      }
-      cp_async_arrive_noinc(q_full);
-      const int rows_end = (int)tok_end[kPair - 1] > (int)tok_end[0] ? (int)tok_end[kPair - 1] : (int)tok_end[0];
-      auto load = [&](int i, bool is_v) {
+        cp_async_arrive_noinc(q_full);
+      };
+      auto issue_tile = [&](const TcCursor& c, int64_t j, bool is_v) {
         const int stages = is_v ? kStagesV : kStagesK;
-        const int st = i % stages;
-        if (i >= stages) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((i / stages) - 1) & 1, aborted);
-        const int t = t_begin + i;
+        const int st = (int)(j % stages);
+        if (j >= stages) mbar_wait(is_v ? &v_empty[st] : &k_empty[st], ((j / stages) - 1) & 1, aborted);
+        const TcPair& u = c.it.u;
+        const int t = c.it.t_begin + c.i;
         const uint32_t dst = sbase + (is_v ? kOffV : kOffK) + st * kKvBytes;
-        if (t < hist_tiles) stage_hist_cp<T>(a, ba, b, h, start, t, is_v ? a.v_pool : a.k_pool, dst, lane, pages);
-        else stage_chunk_cp(a, b, h, first, t - hist_tiles, rows_end, is_v ? a.v_chunk : a.k_chunk, dst, lane);
+        const int rows_end = (int)max(u.tok_end[0], u.tok_end[kPair - 1]);
+        if (t < u.row.hist_tiles)
+          stage_hist_cp<T>(a, ba, u.b, c.it.h, u.row.start, t, is_v ? a.v_pool : a.k_pool, dst, lane, pages);
+        else
+          stage_chunk_cp(a, u.b, c.it.h, u.row.first, t - u.row.hist_tiles, rows_end, is_v ? a.v_chunk : a.k_chunk,
+                         dst, lane);
         cp_async_arrive_noinc(is_v ? &v_full[st] : &k_full[st]);
       };
-      for (int i = 0; i < min(n, kStagesK); ++i) load(i, false);
-      for (int i = 0; i < n; ++i) {
-        load(i, true);
-        if (i + kStagesK < n) load(i + kStagesK, false);
+      int64_t jk = 0;
+      load_q(cv.it);
+      for (; jk < min(n_tiles, (int64_t)kStagesK); ++jk) {
+        issue_tile(ck, jk, false);
+        ck.advance(a);
+      }
+      for (int64_t j = 0; j < n_tiles; ++j) {
+        issue_tile(cv, j, true);
+        if (cv.last_of_item() && j + 1 < n_tiles) {
+          mbar_wait(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
+          cv.advance(a);
+          load_q(cv.it);
+        } else {
+          cv.advance(a);
+        }
+        if (jk < n_tiles) {
+          issue_tile(ck, jk, false);
+          ++jk;
+          ck.advance(a);
+        }
       }
     }
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer: the row tiles alternate PV_g(i), S_g(i+1) ----------------
     // The whole warp runs the loop (warp-uniform control flow); elected lanes issue.
-    {
-      constexpr bool kBf16 = !std::is_same<T, __half>::value;
-      const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
-      const uint32_t idesc_pv = idesc_f16(kBf16, true, kTcRows, kTcDim);
-      // Shared-memory descriptors: the start-address field holds address >> 4 (14 bits, every
-      // address here is below 256 KiB), so the descriptor of base + off is desc(base) + off / 16.
-      const uint64_t dq = desc_kmajor(sbase + kOffQ);
-      const uint64_t dk = desc_kmajor(sbase + kOffK);
-      const uint64_t dv = desc_mnmajor(sbase + kOffV);
+    constexpr bool kBf16 = !std::is_same<T, __half>::value;
+    const uint32_t idesc_qk = idesc_f16(kBf16, false, kTcRows, kTcKv);
+    const uint32_t idesc_pv = idesc_f16(kBf16, true, kTcRows, kTcDim);
+    // Shared-memory descriptors: the start-address field holds address >> 4 (14 bits, every
+    // address here is below 256 KiB), so the descriptor of base + off is desc(base) + off / 16.
+    const uint64_t dq = desc_kmajor(sbase + kOffQ);
+    const uint64_t dk = desc_kmajor(sbase + kOffK);
+    const uint64_t dv = desc_mnmajor(sbase + kOffV);
+    TcWalker w = walk0;
+    TcItem it;
+    int64_t j0 = 0;            // CTA tile index of the item's first tile (ring positions)
+    int cnt[kPair] = {0, 0};   // tiles of row tile g so far (phases of s_full, p_full, o_done)
+    int fin[kPair] = {0, 0};   // items with tiles of row tile g so far (phases of o_final, o_free)
+    int items = 0;
+    while (w.next(a, it)) {
       auto issue_s = [&](int g, int i) {  // S_g(i) = Q_g K(i)^T into g's S columns
-        const int ks = i % kStagesK;
+        const int ks = (int)((j0 + i) % kStagesK);
         fence_async_smem();
         tc_fence_after();
         const uint64_t dks = dk + (uint64_t)(ks * (kKvBytes >> 4));
@@ -557,10 +756,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
                    dks + (uint64_t)(((s >> 2) * kKvRegion + (s & 3) * 32) >> 4), idesc_qk, s > 0 ? 1u : 0u);
         umma_commit(&s_full[g]);
         // K(i) is free once every row tile that uses tile i has issued its S (row tile 1 issues last)
-        if (g == kPair - 1 || i >= ng[kPair - 1]) umma_commit(&k_empty[ks]);
+        if (g == kPair - 1 || i >= it.ng[kPair - 1]) umma_commit(&k_empty[ks]);
       };
       auto issue_pv = [&](int g, int i) {  // O_g += P_g(i) V(i)
-        const int vs = i % kStagesV;
+        const int vs = (int)((j0 + i) % kStagesV);
         tc_fence_after();
         const uint64_t dvs = dv + (uint64_t)(vs * (kKvBytes >> 4));
 #pragma unroll
@@ -568,165 +767,187 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
           umma_f16_tmem_a(tmem + kTmemO + g * 128, tmem + g * 128 + s * 8, dvs + (uint64_t)((s * 2048) >> 4),
                           idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
         umma_commit(&o_done[g]);
-        if (g == kPair - 1 || i >= ng[kPair - 1]) umma_commit(&v_empty[vs]);
-        if (i + 1 == ng[g]) umma_commit(&o_final[g]);
+        if (g == kPair - 1 || i >= it.ng[kPair - 1]) umma_commit(&v_empty[vs]);
+        if (i + 1 == it.ng[g]) umma_commit(&o_final[g]);
       };
       // S_g(i+1) overwrites P_g(i) in g's S columns, so it follows PV_g(i); the waits suspend the
       // warp instead of spinning.
-      mbar_wait_warp(q_full, 0, aborted);
-      mbar_wait_warp(&k_full[0], 0, aborted);
+      mbar_wait_warp(q_full, items & 1, aborted);
+      mbar_wait_warp(&k_full[j0 % kStagesK], (j0 / kStagesK) & 1, aborted);
 #pragma unroll
       for (int g = 0; g < kPair; ++g)
-        if (ng[g] > 0) issue_s(g, 0);
-      for (int i = 0; i < n; ++i) {
+        if (it.ng[g] > 0) issue_s(g, 0);
+      for (int i = 0; i < it.n; ++i) {
 #pragma unroll
         for (int g = 0; g < kPair; ++g) {
-          if (i >= ng[g]) continue;
-          mbar_wait_warp(&p_full[g], i & 1, aborted);
-          mbar_wait_warp(&v_full[i % kStagesV], (i / kStagesV) & 1, aborted);
+          if (i >= it.ng[g]) continue;
+          mbar_wait_warp(&p_full[g], (cnt[g] + i) & 1, aborted);
+          mbar_wait_warp(&v_full[(j0 + i) % kStagesV], ((j0 + i) / kStagesV) & 1, aborted);
+          // the previous item's O of this row tile has been read out before PV overwrites it
+          if (i == 0 && fin[g] > 0) mbar_wait_warp(&o_free[g], (fin[g] - 1) & 1, aborted);
           issue_pv(g, i);
-          if (i + 1 < ng[g]) {
-            mbar_wait_warp(&k_full[(i + 1) % kStagesK], ((i + 1) / kStagesK) & 1, aborted);
+          if (i + 1 < it.ng[g]) {
+            mbar_wait_warp(&k_full[(j0 + i + 1) % kStagesK], ((j0 + i + 1) / kStagesK) & 1, aborted);
             issue_s(g, i + 1);
           }
         }
       }
+#pragma unroll
+      for (int g = 0; g < kPair; ++g) {
+        cnt[g] += it.ng[g];
+        fin[g] += it.ng[g] > 0 ? 1 : 0;
+      }
+      j0 += it.n;
+      ++items;
     }
   } else {
     // ---------------- softmax warpgroup g: thread <-> row <-> TMEM lane ----------------
-    const int g = (warp - 2) / 4;
+    const int g = (warp - kFirstSoftmaxWarp) / 4;
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
     const int r = quad * 32 + lane;            // row of the tile
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    const int64_t my_tok0 = g == 0 ? tok0[0] : tok0[1];
-    const int64_t my_tok = my_tok0 + r / G;
-    const bool row_valid = my_tok < (g == 0 ? tok_end[0] : tok_end[1]);
-    const int my_n = g == 0 ? ng[0] : ng[1];
-    const int my_splits = g == 0 ? sp.splits[0] : sp.splits[1];
     const uint32_t s_col = (uint32_t)g * 128;
     const uint32_t o_col = kTmemO + (uint32_t)g * 128;
     const float scale = a.scale_log2;
-    float m_ref = -INFINITY, l_run = 0.f;
-    for (int i = 0; i < my_n; ++i) {
-      const int t = t_begin + i;
-      // visible columns of this tile: history keys below `start`; chunk keys up to the row's token
-      bool full;
-      int lim;
-      if (t < hist_tiles) {
-        lim = row_valid ? start - t * kTcKv : 0;
-        full = (t + 1) * kTcKv <= start;
-      } else {
-        const int k0 = (t - hist_tiles) * kTcKv;
-        lim = row_valid ? (int)my_tok + 1 - k0 : 0;
-        full = k0 + kTcKv <= (int)my_tok0 + 1;
-      }
-      mbar_wait(&s_full[g], i & 1, aborted);
-      tc_fence_after();
-      const uint32_t s_addr = tmem + s_col + lane_base;
-      uint32_t sr[kTcKv / 32][32];
+    TcWalker w = walk0;
+    TcItem it;
+    int cnt = 0, fin = 0;  // tiles and items of this row tile so far (barrier phases)
+    while (w.next(a, it)) {
+      const TcPair& u = it.u;
+      const int my_n = it.ng[g];
+      const int64_t my_tok0 = u.tok0[g];
+      const int64_t my_tok = my_tok0 + r / G;
+      const bool row_valid = my_tok < u.tok_end[g];
+      const int start = u.row.start;
+      const int hist_tiles = u.row.hist_tiles;
+      float m_ref = -INFINITY, l_run = 0.f;
+      for (int i = 0; i < my_n; ++i) {
+        const int t = it.t_begin + i;
+        // visible columns of this tile: history keys below `start`; chunk keys up to the row's token
+        bool full;
+        int lim;
+        if (t < hist_tiles) {
+          lim = row_valid ? start - t * kTcKv : 0;
+          full = (t + 1) * kTcKv <= start;
+        } else {
+          const int k0 = (t - hist_tiles) * kTcKv;
+          lim = row_valid ? (int)my_tok + 1 - k0 : 0;
+          full = k0 + kTcKv <= (int)my_tok0 + 1;
+        }
+        mbar_wait(&s_full[g], (cnt + i) & 1, aborted);
+        tc_fence_after();
+        const uint32_t s_addr = tmem + s_col + lane_base;
+        uint32_t sr[kTcKv / 32][32];
 #pragma unroll
-      for (int c = 0; c < kTcKv / 32; ++c) tmem_ld32_async(s_addr + c * 32, sr[c]);
-      tmem_wait_ld();
-      if (!full) {  // uniform for the warpgroup: only tiles that cross a causal or history end are masked
+        for (int c = 0; c < kTcKv / 32; ++c) tmem_ld32_async(s_addr + c * 32, sr[c]);
+        tmem_wait_ld();
+        if (!full) {  // uniform for the warpgroup: only tiles that cross a causal or history end are masked
+#pragma unroll
+          for (int c = 0; c < kTcKv / 32; ++c) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= lim) sr[c][e] = 0xff800000u;  // -inf: exp2 gives 0 below
+          }
+        }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < kTcKv / 32; ++c) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= lim) sr[c][e] = 0xff800000u;  // -inf: exp2 gives 0 below
+          for (int e = 0; e < 32; e += 2)
+            mx[(e >> 1) & 3] = fmax3(mx[(e >> 1) & 3], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
         }
-      }
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < kTcKv / 32; ++c) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) mx[e & 3] = fmaxf(mx[e & 3], __uint_as_float(sr[c][e]));
-      }
-      const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
-      const float m_new = fmaxf(m_ref, tile_max);
-      const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
-      const float alpha = need ? fast_exp2(m_ref - m_new) : 1.f;
-      if (need) {
-        l_run *= alpha;
-        m_ref = m_new;
-      } else if (m_ref == -INFINITY) {
-        m_ref = m_new;
-      }
-      const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;  // a row with nothing visible yet: all -inf
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-      // P as the A operand of PV: 16-bit pairs over the first 64 S columns, 32 scores (16
-      // columns) per store; every S value is in registers before the first store.
-#pragma unroll
-      for (int c = 0; c < kTcKv / 32; ++c) {
-        uint32_t pw[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          // branch-free: every exponent is independent, so the ex2 issue overlaps
-          const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * j]), scale, neg_m));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * j + 1]), scale, neg_m));
-          ps[j & 3] += p0 + p1;
-          pw[j] = pack2<T>(p0, p1);
+        const float tile_max = fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]) * scale;
+        const float m_new = fmaxf(m_ref, tile_max);
+        const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
+        const float alpha = need ? fast_exp2(m_ref - m_new) : 1.f;
+        if (need) {
+          l_run *= alpha;
+          m_ref = m_new;
+        } else if (m_ref == -INFINITY) {
+          m_ref = m_new;
         }
-        tmem_st16_async(s_addr + c * 16, pw);
-      }
-      l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      // The running O is rescaled after P is out of registers; PV(i) waits for both.
-      if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access
-        mbar_wait(&o_done[g], (i - 1) & 1, aborted);  // PV(i-1) of this row tile finished writing O
-        tc_fence_after();
+        const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;  // a row with nothing visible yet: all -inf
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+        // P as the A operand of PV: 16-bit pairs over the first 64 S columns, 32 scores (16
+        // columns) per store; every S value is in registers before the first store.
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float ov[32];
-          tmem_ld32(tmem + o_col + lane_base + c * 32, ov);
+        for (int c = 0; c < kTcKv / 32; ++c) {
+          uint32_t pw[16];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-          tmem_st32(tmem + o_col + lane_base + c * 32, ov);
+          for (int j = 0; j < 16; ++j) {
+            // branch-free: every exponent is independent, so the ex2 issue overlaps
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * j]), scale, neg_m));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c][2 * j + 1]), scale, neg_m));
+            ps[j & 3] += p0 + p1;
+            pw[j] = pack2<T>(p0, p1);
+          }
+          tmem_st16_async(s_addr + c * 16, pw);
         }
-      }
-      tmem_wait_st();
-      tc_fence_before();  // our tcgen05.ld of S / st of P and O before the next MMAs
-      mbar_arrive(&p_full[g]);
-    }
-    // ---- epilogue (a row tile without tiles in this split writes nothing here) ----
-    if (my_n > 0) {
-      mbar_wait(&o_final[g], 0, aborted);
-      tc_fence_after();
-      if (my_splits == 1) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        T* dst = out + (b * a.padded_len + first + my_tok) * row_elems + (int64_t)(h * G + r % G) * kTcDim;
+        l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+        // The running O is rescaled after P is out of registers; PV(i) waits for both.
+        if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access
+          mbar_wait(&o_done[g], (cnt + i - 1) & 1, aborted);  // PV(i-1) of this row tile finished writing O
+          tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float ov[32];
-          tmem_ld32(tmem + o_col + lane_base + c * 32, ov);
-          if (row_valid) {
+          for (int c = 0; c < 4; ++c) {
+            float ov[32];
+            tmem_ld32(tmem + o_col + lane_base + c * 32, ov);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 pk;
-              pk.x = pack2<T>(ov[u * 8 + 0] * inv, ov[u * 8 + 1] * inv);
-              pk.y = pack2<T>(ov[u * 8 + 2] * inv, ov[u * 8 + 3] * inv);
-              pk.z = pack2<T>(ov[u * 8 + 4] * inv, ov[u * 8 + 5] * inv);
-              pk.w = pack2<T>(ov[u * 8 + 6] * inv, ov[u * 8 + 7] * inv);
-              *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = pk;
-            }
+            for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+            tmem_st32(tmem + o_col + lane_base + c * 32, ov);
           }
         }
-      } else {
-        const int qt = pair * kPair + g;
-        const int64_t part = (b * a.hkv + h) * ((int64_t)qtiles * max_splits) + (int64_t)qt * max_splits + split;
+        tmem_wait_st();
+        tc_fence_before();  // our tcgen05.ld of S / st of P and O before the next MMAs
+        mbar_arrive(&p_full[g]);
+      }
+      cnt += my_n;
+      // ---- epilogue of the item: O out of TMEM (then free for the next item), then global stores
+      if (my_n > 0) {
+        mbar_wait(&o_final[g], fin & 1, aborted);
+        tc_fence_after();
+        ++fin;
+        // O 32 columns at a time; TMEM is handed back once the last columns are loaded
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        T* dst = out + (u.b * a.padded_len + u.row.first + my_tok) * row_elems + (int64_t)(it.h * G + r % G) * kTcDim;
+        const int64_t part = (int64_t)it.slot * kPair + g;
         float* po = ws_o + (part * kTcRows + r) * kTcDim;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float ov[32];
-          tmem_ld32(tmem + o_col + lane_base + c * 32, ov);
+          uint32_t ov[32];
+          tmem_ld32_async(tmem + o_col + lane_base + c * 32, ov);
+          tmem_wait_ld();
+          if (c == 3) {
+            tc_fence_before();
+            mbar_arrive(&o_free[g]);
+          }
+          if (it.slot < 0) {
+            if (row_valid) {
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            *reinterpret_cast<float4*>(po + c * 32 + u * 4) =
-                make_float4(ov[u * 4], ov[u * 4 + 1], ov[u * 4 + 2], ov[u * 4 + 3]);
+              for (int v = 0; v < 4; ++v) {
+                const uint32_t* f = &ov[v * 8];
+                uint4 pk;
+                pk.x = pack2<T>(__uint_as_float(f[0]) * inv, __uint_as_float(f[1]) * inv);
+                pk.y = pack2<T>(__uint_as_float(f[2]) * inv, __uint_as_float(f[3]) * inv);
+                pk.z = pack2<T>(__uint_as_float(f[4]) * inv, __uint_as_float(f[5]) * inv);
+                pk.w = pack2<T>(__uint_as_float(f[6]) * inv, __uint_as_float(f[7]) * inv);
+                *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = pk;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              *reinterpret_cast<uint4*>(po + c * 32 + v * 4) = make_uint4(ov[v * 4], ov[v * 4 + 1], ov[v * 4 + 2], ov[v * 4 + 3]);
+          }
         }
-        *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_run);
+        if (it.slot >= 0) *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_run);
+      } else if (it.slot >= 0) {  // no tiles of this row tile in the piece: an empty partial
+        *reinterpret_cast<float2*>(ws_ml + (((int64_t)it.slot * kPair + g) * kTcRows + r) * 2) =
+            make_float2(-INFINITY, 0.f);
       }
     }
-    tc_fence_before();
   }
+  tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
@@ -734,64 +955,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   }
 }
 
-// Merge the split partials of row tiles that needed more than one split.  A CTA takes one group
-// of kCombineRows rows of a row tile; each thread merges (row, 16-byte column chunk) items in one
-// online pass over the splits (running max, rescaled sums), so the loads of every split are
-// independent of each other and a warp reads 512 contiguous bytes of one row per split.
+// Merge the pieces of units cut by CTA boundaries.  CTA (c, g, row group) reads CTA c's
+// descriptor (the unit c opened and left unfinished, and the last CTA c1 of the same head holding
+// a piece of it) and merges row tile g's rows [16 * group, 16 * group + 16) over the pieces in
+// slots 2c + 1 and 2c' (c' = c + hkv, c + 2 hkv, ..., c1); each thread merges (row, 16-byte column chunk) items in one online pass
+// (running max, rescaled sums), so a warp reads 512 contiguous bytes of one row per piece.
 constexpr int kCombineThreads = 128;
 constexpr int kCombineRows = 16;
 
 template <typename T>
 __global__ void __launch_bounds__(kCombineThreads) prefill_combine_kernel(const PrefillArgs a, const float* ws_o,
-                                                                          const float* ws_ml, int max_splits) {
-  constexpr int kGroups = kTcRows / kCombineRows;
-  const int qtile = blockIdx.x / kGroups;
-  const int r0 = (blockIdx.x % kGroups) * kCombineRows;
-  const int h = blockIdx.y;
-  const int64_t b = blockIdx.z;
+                                                                          const float* ws_ml,
+                                                                          const int64_t* ws_desc, int pairs) {
+  const int c = blockIdx.x;
+  const int g = blockIdx.y;
+  const int r0 = blockIdx.z * kCombineRows;
+  const int64_t rp = ws_desc[c * 4 + 0];
+  if (rp < 0) return;  // uniform for the CTA
+  const int h = (int)ws_desc[c * 4 + 1];
+  const int c1 = (int)ws_desc[c * 4 + 2];
+  const TcPair u = tc_pair(a, (int)rp, pairs);
   const int G = a.groups;
-  const int tokens_per_tile = kTcRows / G;
-  const int64_t tok0 = (int64_t)qtile * tokens_per_tile;
-  const TcGeometry geo = tc_geometry(a, b, tok0, tokens_per_tile, false);
-  // the split layout of this tile's pair (as the tc kernel cut it)
-  const int pair_first = qtile - qtile % kPair;
-  const int64_t other_tok0 = (int64_t)(pair_first + (qtile == pair_first ? 1 : 0)) * tokens_per_tile;
-  const int other_tiles = tc_geometry(a, b, other_tok0, tokens_per_tile, false).n_tiles;
-  const TcSplits sp = qtile == pair_first ? tc_splits(geo.n_tiles, other_tiles) : tc_splits(other_tiles, geo.n_tiles);
-  const int n_splits = sp.splits[qtile == pair_first ? 0 : 1];
-  if (n_splits <= 1) return;  // uniform for the CTA
-  const int64_t tok_end = min(geo.len, tok0 + tokens_per_tile);
-  const int rows = (int)min((int64_t)kTcRows, (tok_end - tok0) * G);  // valid rows: a prefix of the tile
-  // partial (split s, row r) lives at row (part0 + s) * kTcRows + r
-  const int64_t part0 = (b * a.hkv + h) * ((int64_t)(gridDim.x / kGroups) * max_splits) + (int64_t)qtile * max_splits;
+  const int rows = max(0, min(kTcRows, (u.tok_end[g] - u.tok0[g]) * G));  // valid rows
   T* out = reinterpret_cast<T*>(a.out);
   constexpr int kChunks = kTcDim / 4;  // float4 chunks of a row
   for (int item = threadIdx.x; item < kCombineRows * kChunks; item += kCombineThreads) {
     const int r = r0 + item / kChunks;
-    const int c = item % kChunks;
+    const int cc = item % kChunks;
     if (r >= rows) break;  // items are row-major: the rest of this thread's items are past the end too
     float m = -INFINITY, l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
-    for (int sp = 0; sp < n_splits; ++sp) {
-      const int64_t row = (part0 + sp) * kTcRows + r;
+    for (int p = c; p <= c1; p += a.hkv) {
+      const int64_t slot = p == c ? 2 * (int64_t)c + 1 : 2 * (int64_t)p;
+      const int64_t row = (slot * kPair + g) * kTcRows + r;
       const float2 ml = *reinterpret_cast<const float2*>(ws_ml + row * 2);
-      const float4 o = *reinterpret_cast<const float4*>(ws_o + row * kTcDim + c * 4);
-      if (ml.x == -INFINITY) continue;  // an empty split contributes nothing
+      if (ml.x == -INFINITY) continue;  // an empty piece contributes nothing
+      const float4 o = *reinterpret_cast<const float4*>(ws_o + row * kTcDim + cc * 4);
       const float m_new = fmaxf(m, ml.x);
       const float alpha = exp2f(m - m_new);  // 0 on the first contribution (m = -inf)
-      const float w = exp2f(ml.x - m_new);
-      l = l * alpha + w * ml.y;
-      acc.x = acc.x * alpha + w * o.x;
-      acc.y = acc.y * alpha + w * o.y;
-      acc.z = acc.z * alpha + w * o.z;
-      acc.w = acc.w * alpha + w * o.w;
+      const float wt = exp2f(ml.x - m_new);
+      l = l * alpha + wt * ml.y;
+      acc.x = acc.x * alpha + wt * o.x;
+      acc.y = acc.y * alpha + wt * o.y;
+      acc.z = acc.z * alpha + wt * o.z;
+      acc.w = acc.w * alpha + wt * o.w;
       m = m_new;
     }
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int64_t tok = tok0 + r / G;
-    T* dst = out + (b * a.padded_len + geo.first + tok) * (int64_t)(a.hq * kTcDim) +
-             (int64_t)(h * G + r % G) * kTcDim + c * 4;
+    const int64_t tok = u.tok0[g] + r / G;
+    T* dst = out + (u.b * a.padded_len + u.row.first + tok) * (int64_t)(a.hq * kTcDim) +
+             (int64_t)(h * G + r % G) * kTcDim + cc * 4;
     uint2 pk;
     pk.x = pack2<T>(acc.x * inv, acc.y * inv);
     pk.y = pack2<T>(acc.z * inv, acc.w * inv);
@@ -799,23 +1013,12 @@ __global__ void __launch_bounds__(kCombineThreads) prefill_combine_kernel(const 
   }
 }
 
-struct TcPlan {
-  int64_t qtiles;
-  int max_splits;
-  size_t ws_o_bytes, ws_ml_bytes;
-};
-
-TcPlan tc_plan(const PrefillArgs& a) {
-  TcPlan p;
-  const int tokens_per_tile = kTcRows / a.groups;
-  p.qtiles = (a.padded_len + tokens_per_tile - 1) / tokens_per_tile;
-  const int64_t max_tiles = (a.table_stride * a.block_size + kTcKv - 1) / kTcKv + (a.padded_len + kTcKv - 1) / kTcKv;
-  p.max_splits = (int)std::max<int64_t>(1, (max_tiles + kTilesPerSplit - 1) / kTilesPerSplit);
-  const int64_t parts = p.max_splits > 1 ? a.batch * a.hkv * p.qtiles * p.max_splits : 0;
-  p.ws_o_bytes = (size_t)parts * kTcRows * kTcDim * sizeof(float);
-  p.ws_ml_bytes = (size_t)parts * kTcRows * 2 * sizeof(float);
-  return p;
-}
+// Workspace: partial O [2 * kMaxCtas slots][kPair][128 rows][128] fp32, then (m, l) per row, then
+// one descriptor (4 int64) per CTA.
+constexpr int kMaxCtas = 148;  // persistent CTAs: one per SM of a B200
+constexpr size_t kWsOBytes = (size_t)2 * kMaxCtas * kPair * kTcRows * kTcDim * sizeof(float);
+constexpr size_t kWsMlBytes = (size_t)2 * kMaxCtas * kPair * kTcRows * 2 * sizeof(float);
+constexpr size_t kWsDescBytes = (size_t)kMaxCtas * 4 * sizeof(int64_t);
 
 int log2_if_pow2(int x) {
   if (x <= 0 || (x & (x - 1))) return -1;
@@ -824,40 +1027,53 @@ int log2_if_pow2(int x) {
   return s;
 }
 
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return kMaxCtas;
+  return n;
+}
+
 template <typename T, bool kTma>
 cudaError_t launch_tc(const PrefillArgs& a, float* ws, const PrefillMaps& maps, cudaStream_t s) {
   auto kern = prefill_tc_kernel<T, kTma>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
   if (e != cudaSuccess) return e;
-  const TcPlan p = tc_plan(a);
+  static const int sms = std::min(kMaxCtas, num_sms());
+  const int ctas = std::max(1, sms / a.hkv) * a.hkv;  // CTAs per head x heads
   float* ws_o = ws;
-  float* ws_ml = ws ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + ((p.ws_o_bytes + 255) & ~size_t(255)))
-                    : nullptr;
-  const int64_t pairs = (p.qtiles + kPair - 1) / kPair;
-  dim3 grid((unsigned)(pairs * p.max_splits), (unsigned)a.hkv, (unsigned)a.batch);
-  kern<<<grid, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, p.max_splits, (int)p.qtiles,
-                                              log2_if_pow2(a.block_size));
+  float* ws_ml = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + kWsOBytes);
+  int64_t* ws_desc = reinterpret_cast<int64_t*>(reinterpret_cast<char*>(ws) + kWsOBytes + kWsMlBytes);
+  const int64_t tokens_per_tile = kTcRows / a.groups;
+  const int64_t qtiles = (a.padded_len + tokens_per_tile - 1) / tokens_per_tile;
+  const int pairs = (int)((qtiles + kPair - 1) / kPair);
+  kern<<<ctas, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, ws_desc, pairs, log2_if_pow2(a.block_size));
   e = cudaGetLastError();
-  if (e != cudaSuccess || p.max_splits == 1) return e;
-  dim3 cgrid((unsigned)(p.qtiles * (kTcRows / kCombineRows)), (unsigned)a.hkv, (unsigned)a.batch);
-  prefill_combine_kernel<T><<<cgrid, kCombineThreads, 0, s>>>(a, ws_o, ws_ml, p.max_splits);
+  if (e != cudaSuccess) return e;
+  prefill_combine_kernel<T><<<dim3(ctas, kPair, kTcRows / kCombineRows), kCombineThreads, 0, s>>>(a, ws_o, ws_ml,
+                                                                                                  ws_desc, pairs);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 size_t prefill_tc_workspace_bytes(const PrefillArgs& a) {
-  const TcPlan p = tc_plan(a);
-  if (p.max_splits == 1) return 0;
-  return ((p.ws_o_bytes + 255) & ~size_t(255)) + ((p.ws_ml_bytes + 255) & ~size_t(255));
+  (void)a;
+  return kWsOBytes + kWsMlBytes + kWsDescBytes;
 }
 
 bool prefill_tc_supported(const PrefillArgs& a, int dtype) {
   if (dtype != MI_BF16 && dtype != MI_F16) return false;
   if (a.head_dim != kTcDim) return false;
   if (!(a.groups == 1 || a.groups == 2 || a.groups == 4 || a.groups == 8)) return false;
-  if (a.batch > 65535 || a.hkv > 65535) return false;
+  if (a.batch > 65535 || a.hkv > kMaxCtas) return false;
   if (a.table_stride * a.block_size + a.padded_len >= (int64_t(1) << 30)) return false;
+  {  // the stream of one head (pairs of the batch x their tiles) is counted in 32-bit integers
+    const int64_t tpt = kTcRows / a.groups;
+    const int64_t pairs = ((a.padded_len + tpt - 1) / tpt + kPair - 1) / kPair;
+    const int64_t tiles = (a.table_stride * a.block_size + a.padded_len) / kTcKv + 2;
+    if (a.batch * pairs * tiles >= (int64_t(1) << 31)) return false;
+  }
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!al16(a.q) || !al16(a.k_chunk) || !al16(a.v_chunk) || !al16(a.out)) return false;
   if (a.table_stride > 0 && (!al16(a.k_pool) || !al16(a.v_pool))) return false;
