@@ -608,36 +608,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
           pend_valid = true;
         }
       };
+      // Copies are issued one box per lane (the lanes' TMA instructions go out together).
       auto load_q = [&](const TcItem& it) {
-        mbar_expect_tx_e(q_full, kPair * kQBytes);
-        for (int g = 0; g < kPair; ++g)  // box [64 d, G heads, 128/G tokens]: row = token * G + head
-          for (int c = 0; c < 2; ++c)
-            tma_load_4d_e(smem + kOffQ + g * kQBytes + c * kQRegion, &maps.q, q_full, c * 64, it.h * G,
-                          (int)(it.u.row.first + it.u.tok0[g]), (int)it.u.b);
+        if (lane == 0) mbar_arrive_expect_tx(q_full, kPair * kQBytes);
+        __syncwarp();
+        if (lane < 2 * kPair) {  // box [64 d, G heads, 128/G tokens]: row = token * G + head
+          const int g = lane >> 1, c = lane & 1;
+          tma_load_4d(smem + kOffQ + g * kQBytes + c * kQRegion, &maps.q, q_full, c * 64, it.h * G,
+                      it.u.row.first + it.u.tok0[g], it.u.b);
+        }
       };
       auto issue_tile = [&](const TcCursor& c, int64_t j, bool is_v) {
         const int stages = is_v ? kStagesV : kStagesK;
         const int st = (int)(j % stages);
         uint64_t* full = is_v ? &v_full[st] : &k_full[st];
         uint8_t* dst = smem + (is_v ? kOffV : kOffK) + st * kKvBytes;
-        mbar_expect_tx_e(full, kKvBytes);
         const int t = c.it.t_begin + c.i;
         const int h = c.it.h;
-        if (t < c.it.u.row.hist_tiles) {
-          const CUtensorMap* map = is_v ? &maps.v_pool : &maps.k_pool;
-          const int* rows = page_ring + (j & 7) * 8;
-          for (int pg = 0; pg < pages_per_tile; ++pg) {
-            const int row0 = rows[pg];
-            for (int cc = 0; cc < 2; ++cc)
-              tma_load_3d_e(dst + cc * kKvRegion + pg * page_bytes, map, full, cc * 64, h, row0);
-          }
-        } else {  // boxes of 64 chunk tokens (rows past the chunk read as zeros)
-          const CUtensorMap* map = is_v ? &maps.v_chunk : &maps.k_chunk;
-          const int pos = (int)c.it.u.row.first + (t - c.it.u.row.hist_tiles) * kTcKv;
-          for (int sub = 0; sub < kTcKv / 64; ++sub)
-            for (int cc = 0; cc < 2; ++cc)
-              tma_load_4d_e(dst + cc * kKvRegion + sub * 64 * 128, map, full, cc * 64, h, pos + sub * 64,
-                            (int)c.it.u.b);
+        const bool hist = t < c.it.u.row.hist_tiles;
+        const int pos = c.it.u.row.first + (t - c.it.u.row.hist_tiles) * kTcKv;
+        const int b = c.it.u.b;
+        // lane = (page or 64-token sub-tile) * 2 + 64-column half
+        const int boxes = hist ? 2 * pages_per_tile : 2 * (kTcKv / 64);
+        const int q = lane >> 1, cc = lane & 1;
+        const int row0 = hist && lane < boxes ? page_ring[(j & 7) * 8 + q] : 0;
+        if (lane == 0) mbar_arrive_expect_tx(full, kKvBytes);
+        __syncwarp();
+        if (lane < boxes) {
+          if (hist)
+            tma_load_3d(dst + cc * kKvRegion + q * page_bytes, is_v ? &maps.v_pool : &maps.k_pool, full, cc * 64, h,
+                        row0);
+          else  // boxes of 64 chunk tokens (rows past the chunk read as zeros)
+            tma_load_4d(dst + cc * kKvRegion + q * 64 * 128, is_v ? &maps.v_chunk : &maps.k_chunk, full, cc * 64, h,
+                        pos + q * 64, b);
         }
       };
       int64_t jk = 0;  // tiles whose K is loaded
