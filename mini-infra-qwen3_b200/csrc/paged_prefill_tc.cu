@@ -574,9 +574,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     // ---------------- loader: per item both Q tiles, then K and V tiles into their rings ----------
     // K(j) reuses the stage of tile j - kStagesK once its S is done, V(j) that of tile j - kStagesV
     // once its PVs are (j counts the CTA's tiles across items).  Loads go in the order
-    // K(0 .. kStagesK-1), then V(j), K(j + kStagesK) for j = 0, 1, ...: the MMA warp issues PV(j - 2)
-    // before S(j), so each blocking wait ends in the order the loads are issued.  The Q tiles of
-    // an item are loaded once every S of the previous item is done (K(j) free, j its last tile).
+    // K(0 .. kStagesK-1), V(0), then V(j+1), K(j + kStagesK) for j = 0, 1, ...: the MMA warp issues
+    // the PVs of tile j-1 before the S of tile j, so each blocking wait ends in the order the loads
+    // are issued.  The Q tiles of an item are loaded once every S of the previous item is done
+    // (K(j) free, j its last tile).
     TcCursor ck, cv;  // tiles of the next K load and of the next V load
     ck.init(walk0, a);
     cv.init(walk0, a);
@@ -663,14 +664,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
       fetch_pages(ck);
       load_q(cv.it);
       for (int64_t j = 0; j < min(n_tiles, (int64_t)kStagesK); ++j) load_k();
+      issue_tile(cv, 0, true);
+      cv.advance(a);
       for (int64_t j = 0; j < n_tiles; ++j) {
-        if (j >= kStagesV) mbar_wait_warp(&v_empty[j % kStagesV], ((j / kStagesV) - 1) & 1, aborted);
-        issue_tile(cv, j, true);
-        if (cv.last_of_item() && j + 1 < n_tiles) {  // next item's Q once every S of this one is done
-          mbar_wait_warp(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
-          cv.advance(a);
-          load_q(cv.it);
-        } else {
+        if (j + 1 < n_tiles) {  // V(j+1): its stage frees (PVs of j-1) before K(j+3)'s (S of j)
+          const bool opens = cv.i == 0;  // tile j+1 opens an item
+          if (j + 1 >= kStagesV) mbar_wait_warp(&v_empty[(j + 1) % kStagesV], (((j + 1) / kStagesV) - 1) & 1, aborted);
+          issue_tile(cv, j + 1, true);
+          if (opens) {  // the item's Q once every S of the previous item (last tile j) is done
+            mbar_wait_warp(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
+            load_q(cv.it);
+          }
           cv.advance(a);
         }
         if (j + kStagesK < n_tiles) load_k();
@@ -714,13 +718,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         issue_tile(ck, jk, false);
         ck.advance(a);
       }
+      issue_tile(cv, 0, true);
+      cv.advance(a);
       for (int64_t j = 0; j < n_tiles; ++j) {
-        issue_tile(cv, j, true);
-        if (cv.last_of_item() && j + 1 < n_tiles) {
-          mbar_wait(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
-          cv.advance(a);
-          load_q(cv.it);
-        } else {
+        if (j + 1 < n_tiles) {
+          const bool opens = cv.i == 0;
+          issue_tile(cv, j + 1, true);
+          if (opens) {
+            mbar_wait(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
+            load_q(cv.it);
+          }
           cv.advance(a);
         }
         if (jk < n_tiles) {
