@@ -977,6 +977,9 @@ template <typename T>
 __global__ void __launch_bounds__(kCombineThreads) prefill_combine_kernel(const PrefillArgs a, const float* ws_o,
                                                                           const float* ws_ml,
                                                                           const int64_t* ws_desc, int pairs) {
+  // Launched as a programmatic dependent of the tc kernel: the CTAs start while it drains and
+  // wait here for its completion (partials and descriptors written and visible).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int c = blockIdx.x;
   const int g = blockIdx.y;
   const int r0 = blockIdx.z * kCombineRows;
@@ -1060,9 +1063,17 @@ cudaError_t launch_tc(const PrefillArgs& a, float* ws, const PrefillMaps& maps, 
   kern<<<ctas, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, ws_desc, pairs, log2_if_pow2(a.block_size));
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  prefill_combine_kernel<T><<<dim3(ctas, kPair, kTcRows / kCombineRows), kCombineThreads, 0, s>>>(a, ws_o, ws_ml,
-                                                                                                  ws_desc, pairs);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas, kPair, kTcRows / kCombineRows);
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prefill_combine_kernel<T>, a, static_cast<const float*>(ws_o),
+                            static_cast<const float*>(ws_ml), static_cast<const int64_t*>(ws_desc), pairs);
 }
 
 }  // namespace
