@@ -1,7 +1,7 @@
 // Chunked-prefill paged attention on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
 // Variant: bf16 / fp16, head_dim 128, any block size, G = Hq/H_kv in {1, 2, 4, 8}.
-// Persistent CTAs (320 threads, one per SM) share the work as equal ranges of one stream of KV
+// Persistent CTAs (352 threads, one per SM) share the work as equal ranges of one stream of KV
 // tiles (see TcWalker below).  A unit of that stream is one (sequence, pair of tiles of 128 query
 // rows, KV head): a row tile packs 128/G chunk tokens x the G query heads of the KV head (row
 // r = token r/G, head r%G); the unit's two row tiles are consecutive, so every K/V tile staged in
@@ -11,12 +11,13 @@
 // the union and each row tile uses a prefix of it.  A unit inside one CTA's range writes its
 // output directly; a unit cut by CTA boundaries leaves unnormalised partials (O, m, l) that
 // prefill_combine_kernel merges.  Warp roles, linked by mbarriers:
-//   warp 0 (loader): per unit both Q tiles, then K and V tiles into a kStagesK-deep K ring and a
-//      kStagesV-deep V ring (K is free once the S of both row tiles is done, V once both PVs
-//      are).  With tensor maps (block size 16/32/64) the block ids of a tile's pages are read one
-//      K load ahead, then an elected lane issues TMA copies: one 3D box per pool page of a
-//      history tile (a page past `start` reads rows past the pool, which TMA fills with zeros)
-//      and 4D boxes of 64 tokens for a chunk tile; otherwise the warp stages rows with cp.async;
+//   warp 0 (loader): per unit both Q tiles, then K tiles into a kStagesK-deep ring, and warp 10
+//      V tiles into a kStagesV-deep ring (K is free once the S of both row tiles is done, V once
+//      both PVs are).  With tensor maps (block size 16/32/64) each loader reads the block ids of
+//      its next tile's pages one tile ahead and issues the tile as one TMA box per lane: one 3D
+//      box per pool page and 64-column half of a history tile (a page past `start` reads rows
+//      past the pool, which TMA fills with zeros), 4D boxes of 64 tokens for a chunk tile;
+//      otherwise warp 0 stages K and V rows with cp.async;
 //   warp 1 (MMA, elected lane): per row tile g, S_g = Q_g K^T as 8 tcgen05.mma (M=128, N=128,
 //      K=16, kind::f16, fp32 accumulate: 8 KiB of shared-memory operands per 64 cycles of math,
 //      the shared-memory rate) into g's TMEM S columns, and O_g += P_g V as 8 tcgen05.mma
@@ -55,7 +56,8 @@ constexpr int kPair = 2;                            // row tiles per CTA, sharin
 constexpr int kTcKv = 128;                          // KV positions per tile (MMA N of S)
 constexpr int kTcDim = 128;                         // head_dim
 constexpr int kSoftmaxThreads = 128;                // one warpgroup per row tile
-constexpr int kTcThreads = 64 + kPair * kSoftmaxThreads;  // warp 0 loader, warp 1 MMA, then the warpgroups
+constexpr int kTcThreads = 96 + kPair * kSoftmaxThreads;  // warp 0 K loader, warp 1 MMA, the warpgroups, V loader
+constexpr int kVLoaderWarp = 2 + 2 * kPair * kSoftmaxThreads / 64;
 constexpr int kFirstSoftmaxWarp = 2;
 constexpr int kLoaderWarp = 0;
 constexpr int kMmaWarp = 1;
@@ -418,6 +420,58 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// One loader warp's stream of K (or V) tiles over the CTA's items: lanes 0..pages-1 hold the block
+// ids of the next tile's pool pages, loaded one tile ahead; a tile goes out as one TMA box per lane
+// (page or 64-token sub-tile x 64-column half).
+struct KvTileLoader {
+  TcCursor c;
+  int64_t pend;
+  bool pend_valid;
+  int lane, shift;
+  __device__ __forceinline__ void fetch(const PrefillArgs& a) {
+    pend_valid = false;
+    const int pages_per_tile = kTcKv / a.block_size;
+    if (!c.valid || lane >= pages_per_tile) return;
+    const int t = c.it.t_begin + c.i;
+    const int pos0 = t * kTcKv + lane * a.block_size;
+    if (t < c.it.u.row.hist_tiles && pos0 < c.it.u.row.start) {
+      pend = a.block_tables[c.it.u.b * a.table_stride + (pos0 >> shift)];
+      pend_valid = true;
+    }
+  }
+  __device__ __forceinline__ void init(const TcWalker& w0, const PrefillArgs& a, int lane_, int shift_) {
+    lane = lane_;
+    shift = shift_;
+    c.init(w0, a);
+    fetch(a);
+  }
+  __device__ __forceinline__ void issue(const PrefillArgs& a, const CUtensorMap& pool_map, const CUtensorMap& chunk_map,
+                                        uint8_t* dst, uint64_t* full) {
+    const int pages_per_tile = kTcKv / a.block_size;
+    int my_row = (int)(a.num_blocks * a.block_size);  // past the pool: TMA reads zeros
+    if (lane < pages_per_tile && pend_valid) {
+      if (pend < 0 || pend >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
+      else my_row = (int)(pend * a.block_size);
+    }
+    const int t = c.it.t_begin + c.i;
+    const bool hist = t < c.it.u.row.hist_tiles;
+    const int h = c.it.h;
+    const int pos = c.it.u.row.first + (t - c.it.u.row.hist_tiles) * kTcKv;
+    const int b = c.it.u.b;
+    const int boxes = hist ? 2 * pages_per_tile : 2 * (kTcKv / 64);
+    const int q = lane >> 1, cc = lane & 1;
+    const int row0 = __shfl_sync(0xffffffffu, my_row, q & 31);
+    if (lane == 0) mbar_arrive_expect_tx(full, kKvBytes);
+    __syncwarp();
+    if (lane < boxes) {
+      if (hist) tma_load_3d(dst + cc * kKvRegion + q * a.block_size * 128, &pool_map, full, cc * 64, h, row0);
+      else tma_load_4d(dst + cc * kKvRegion + q * 64 * 128, &chunk_map, full, cc * 64, h, pos + q * 64, b);
+    }
+    c.advance(a);
+    fetch(a);
+  }
+};
+
 // Zeros for the padding positions (left of the chunk) of rows b = blockIdx.x (mod gridDim.x), all
 // query heads.
 template <typename T>
@@ -570,46 +624,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   const uint32_t tmem = *tmem_slot;
   bool aborted = false;
 
-  if (warp == kLoaderWarp) {
-    // ---------------- loader: per item both Q tiles, then K and V tiles into their rings ----------
-    // K(j) reuses the stage of tile j - kStagesK once its S is done, V(j) that of tile j - kStagesV
-    // once its PVs are (j counts the CTA's tiles across items).  Loads go in the order
-    // K(0 .. kStagesK-1), V(0), then V(j+1), K(j + kStagesK) for j = 0, 1, ...: the MMA warp issues
-    // the PVs of tile j-1 before the S of tile j, so each blocking wait ends in the order the loads
-    // are issued.  The Q tiles of an item are loaded once every S of the previous item is done
-    // (K(j) free, j its last tile).
-    TcCursor ck, cv;  // tiles of the next K load and of the next V load
-    ck.init(walk0, a);
-    cv.init(walk0, a);
-    if constexpr (kTma) {
-      if (lane == 0) {
-        tma_prefetch_desc(&maps.q);
-        tma_prefetch_desc(&maps.k_chunk);
-        tma_prefetch_desc(&maps.v_chunk);
-        tma_prefetch_desc(&maps.k_pool);
-        tma_prefetch_desc(&maps.v_pool);
+  auto tma_loader_prologue = [&]() {
+    if (lane == 0) {
+      tma_prefetch_desc(&maps.q);
+      tma_prefetch_desc(&maps.k_chunk);
+      tma_prefetch_desc(&maps.v_chunk);
+      tma_prefetch_desc(&maps.k_pool);
+      tma_prefetch_desc(&maps.v_pool);
+    }
+    __syncwarp();
+  };
+  if (warp == kVLoaderWarp) {
+    if constexpr (kTma) {  // V tiles into the V ring (the cp.async loader stages both K and V)
+      tma_loader_prologue();
+      KvTileLoader ld;
+      ld.init(walk0, a, lane, shift);
+      for (int64_t j = 0; j < n_tiles; ++j) {
+        if (j >= kStagesV) mbar_wait_warp(&v_empty[j % kStagesV], ((j / kStagesV) - 1) & 1, aborted);
+        ld.issue(a, maps.v_pool, maps.v_chunk, smem + kOffV + (int)(j % kStagesV) * kKvBytes, &v_full[j % kStagesV]);
       }
-      __syncwarp();
-      // Pool rows of the pages of the tiles in flight: ring of 8 tiles x 8 pages (int32), written at
-      // the K load of a tile and read again at its V load.  The block ids of the next K tile's
-      // pages are loaded one K load ahead (lane pg holds page pg), so their latency is hidden.
-      int* page_ring = reinterpret_cast<int*>(pages);
-      const int pages_per_tile = kTcKv / a.block_size;
-      const int num_slots = (int)(a.num_blocks * a.block_size);
-      const int page_bytes = a.block_size * 128;
-      int64_t pend = 0;
-      bool pend_valid = false;
-      auto fetch_pages = [&](const TcCursor& c) {  // block ids of the pages of c's tile (history tiles)
-        pend_valid = false;
-        if (!c.valid || lane >= pages_per_tile) return;
-        const int t = c.it.t_begin + c.i;
-        const int pos0 = t * kTcKv + lane * a.block_size;
-        if (t < c.it.u.row.hist_tiles && pos0 < c.it.u.row.start) {
-          pend = a.block_tables[c.it.u.b * a.table_stride + (pos0 >> shift)];
-          pend_valid = true;
-        }
-      };
-      // Copies are issued one box per lane (the lanes' TMA instructions go out together).
+    }
+  } else if (warp == kLoaderWarp) {
+    // ---------------- loader: per item both Q tiles, then K (and V) tiles into their rings ---------
+    // K(j) reuses the stage of tile j - kStagesK once its S is done, V(j) that of tile j - kStagesV
+    // once its PVs are (j counts the CTA's tiles across items).  With TMA this warp loads Q and K
+    // and kVLoaderWarp loads V, each in tile order; the cp.async loader stages K(0 .. kStagesK-1),
+    // V(0), then V(j+1), K(j + kStagesK) for j = 0, 1, ... (the MMA warp issues the PVs of tile j-1
+    // before the S of tile j, so each blocking wait ends in the order the loads are issued).  The Q
+    // tiles of an item are loaded once every S of the previous item is done (K(j) free, j its last
+    // tile).
+    if constexpr (kTma) {
+      // K loader (this warp: K tiles and the Q tiles of each item); V tiles come from kVLoaderWarp.
+      tma_loader_prologue();
+      TcCursor cq;  // tile j of the loop below: its item's end gates the next item's Q
+      cq.init(walk0, a);
+      KvTileLoader ld;
+      ld.init(walk0, a, lane, shift);
       auto load_q = [&](const TcItem& it) {
         if (lane == 0) mbar_arrive_expect_tx(q_full, kPair * kQBytes);
         __syncwarp();
@@ -619,67 +669,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
                       it.u.row.first + it.u.tok0[g], it.u.b);
         }
       };
-      auto issue_tile = [&](const TcCursor& c, int64_t j, bool is_v) {
-        const int stages = is_v ? kStagesV : kStagesK;
-        const int st = (int)(j % stages);
-        uint64_t* full = is_v ? &v_full[st] : &k_full[st];
-        uint8_t* dst = smem + (is_v ? kOffV : kOffK) + st * kKvBytes;
-        const int t = c.it.t_begin + c.i;
-        const int h = c.it.h;
-        const bool hist = t < c.it.u.row.hist_tiles;
-        const int pos = c.it.u.row.first + (t - c.it.u.row.hist_tiles) * kTcKv;
-        const int b = c.it.u.b;
-        // lane = (page or 64-token sub-tile) * 2 + 64-column half
-        const int boxes = hist ? 2 * pages_per_tile : 2 * (kTcKv / 64);
-        const int q = lane >> 1, cc = lane & 1;
-        const int row0 = hist && lane < boxes ? page_ring[(j & 7) * 8 + q] : 0;
-        if (lane == 0) mbar_arrive_expect_tx(full, kKvBytes);
-        __syncwarp();
-        if (lane < boxes) {
-          if (hist)
-            tma_load_3d(dst + cc * kKvRegion + q * page_bytes, is_v ? &maps.v_pool : &maps.k_pool, full, cc * 64, h,
-                        row0);
-          else  // boxes of 64 chunk tokens (rows past the chunk read as zeros)
-            tma_load_4d(dst + cc * kKvRegion + q * 64 * 128, is_v ? &maps.v_chunk : &maps.k_chunk, full, cc * 64, h,
-                        pos + q * 64, b);
-        }
-      };
-      int64_t jk = 0;  // tiles whose K is loaded
-      auto load_k = [&]() {
-        if (jk >= kStagesK) mbar_wait_warp(&k_empty[jk % kStagesK], ((jk / kStagesK) - 1) & 1, aborted);
-        if (lane < pages_per_tile) {  // pool rows of this tile's pages (a row past the pool reads zeros)
-          int row0 = num_slots;
-          if (pend_valid) {
-            if (pend < 0 || pend >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
-            else row0 = (int)(pend * a.block_size);
-          }
-          page_ring[(jk & 7) * 8 + lane] = row0;
-        }
-        __syncwarp();
-        issue_tile(ck, jk, false);
-        ++jk;
-        ck.advance(a);
-        fetch_pages(ck);
-      };
-      fetch_pages(ck);
-      load_q(cv.it);
-      for (int64_t j = 0; j < min(n_tiles, (int64_t)kStagesK); ++j) load_k();
-      issue_tile(cv, 0, true);
-      cv.advance(a);
+      load_q(cq.it);
+      for (int64_t j = 0; j < min(n_tiles, (int64_t)kStagesK); ++j)
+        ld.issue(a, maps.k_pool, maps.k_chunk, smem + kOffK + (int)(j % kStagesK) * kKvBytes, &k_full[j % kStagesK]);
       for (int64_t j = 0; j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {  // V(j+1): its stage frees (PVs of j-1) before K(j+3)'s (S of j)
-          const bool opens = cv.i == 0;  // tile j+1 opens an item
-          if (j + 1 >= kStagesV) mbar_wait_warp(&v_empty[(j + 1) % kStagesV], (((j + 1) / kStagesV) - 1) & 1, aborted);
-          issue_tile(cv, j + 1, true);
-          if (opens) {  // the item's Q once every S of the previous item (last tile j) is done
-            mbar_wait_warp(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
-            load_q(cv.it);
-          }
-          cv.advance(a);
+        const bool item_end = cq.last_of_item() && j + 1 < n_tiles;
+        cq.advance(a);
+        if (item_end || j + kStagesK < n_tiles) mbar_wait_warp(&k_empty[j % kStagesK], (j / kStagesK) & 1, aborted);
+        if (item_end) load_q(cq.it);  // every S of the finished item is done
+        if (j + kStagesK < n_tiles) {
+          const int64_t jk = j + kStagesK;
+          ld.issue(a, maps.k_pool, maps.k_chunk, smem + kOffK + (int)(jk % kStagesK) * kKvBytes, &k_full[jk % kStagesK]);
         }
-        if (j + kStagesK < n_tiles) load_k();
       }
     } else {
+      TcCursor ck, cv;  // tiles of the next K load and of the next V load
+      ck.init(walk0, a);
+      cv.init(walk0, a);
       const BlockAddr ba{shift, (uint32_t)a.block_size};
       const int unit = lane & 15;
       auto load_q = [&](const TcItem& it) {
