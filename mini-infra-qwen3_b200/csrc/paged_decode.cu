@@ -42,6 +42,9 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
                                                                 const DecodeArgs a) {
   using S = DecodeShape<D, BS, HB, TG>;
   constexpr int NST = S::kStages;
+  // Launched as a programmatic dependent of the stream's previous kernel (typically the one that
+  // appended this step's K/V): nothing is read before that kernel has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + NST * S::kStageBytes);
@@ -239,6 +242,7 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
 template <typename T, int D>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeArgs a) {
   constexpr int PER_LANE = D / 32;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent of the split kernel
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= a.batch * a.hq) return;
@@ -354,13 +358,25 @@ cudaError_t launch_split(const DecodeArgs& a, const CUtensorMap* tk, const CUten
   auto kern = decode_split_kernel<T, D, BS, HB, TG>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)a.max_splits, (unsigned)(a.hkv / HB), (unsigned)a.batch);
-  kern<<<grid, kThreads, S::kSmemBytes, s>>>(*tk, *tv, a);
-  e = cudaGetLastError();
+  // Both launches are programmatic dependents of their predecessor (their CTAs are placed while it
+  // drains; each kernel waits for it before touching memory).
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.max_splits, (unsigned)(a.hkv / HB), (unsigned)a.batch);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = S::kSmemBytes;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, *tk, *tv, a);
   if (e != cudaSuccess) return e;
   const int64_t warps = a.batch * a.hq;
-  decode_combine_kernel<T, D><<<(unsigned)((warps + 3) / 4), 128, 0, s>>>(a);
-  return cudaGetLastError();
+  cfg.gridDim = dim3((unsigned)((warps + 3) / 4));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  return cudaLaunchKernelEx(&cfg, decode_combine_kernel<T, D>, a);
 }
 
 template <typename T, int D, int BS>

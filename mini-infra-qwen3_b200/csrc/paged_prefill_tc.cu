@@ -563,6 +563,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + kPair);
   int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async: block ids; TMA: page-row ring
 
+  // Launched as a programmatic dependent of the stream's previous kernel (so its CTAs are placed
+  // while that kernel drains): nothing is read or written before that kernel has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -1066,16 +1069,24 @@ cudaError_t launch_tc(const PrefillArgs& a, float* ws, const PrefillMaps& maps, 
   const int64_t tokens_per_tile = kTcRows / a.groups;
   const int64_t qtiles = (a.padded_len + tokens_per_tile - 1) / tokens_per_tile;
   const int pairs = (int)((qtiles + kPair - 1) / kPair);
-  kern<<<ctas, kTcThreads, kTcSmemBytes, s>>>(a, maps, ws_o, ws_ml, ws_desc, pairs, log2_if_pow2(a.block_size));
-  e = cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kTcSmemBytes;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a, maps, ws_o, ws_ml, ws_desc, pairs, log2_if_pow2(a.block_size));
+  }
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, kPair, kTcRows / kCombineRows);
   cfg.blockDim = dim3(kCombineThreads);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, prefill_combine_kernel<T>, a, static_cast<const float*>(ws_o),
