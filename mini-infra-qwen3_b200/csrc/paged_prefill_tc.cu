@@ -668,8 +668,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         __syncwarp();
         if (lane < 2 * kPair) {  // box [64 d, G heads, 128/G tokens]: row = token * G + head
           const int g = lane >> 1, c = lane & 1;
+          const int tok0 = g ? it.u.tok0[1] : it.u.tok0[0];  // a select: no indexing by a lane value
           tma_load_4d(smem + kOffQ + g * kQBytes + c * kQRegion, &maps.q, q_full, c * 64, it.h * G,
-                      it.u.row.first + it.u.tok0[g], it.u.b);
+                      it.u.row.first + tok0, it.u.b);
         }
       };
       load_q(cq.it);
@@ -692,6 +693,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
       const BlockAddr ba{shift, (uint32_t)a.block_size};
       const int unit = lane & 15;
       auto load_q = [&](const TcItem& it) {
+#pragma unroll
         for (int g = 0; g < kPair; ++g) {
           for (int r = lane >> 4; r < kTcRows; r += kLoaderThreads / 16) {
             const int64_t tok = it.u.tok0[g] + r / G;
@@ -833,10 +835,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     int cnt = 0, fin = 0;  // tiles and items of this row tile so far (barrier phases)
     while (w.next(a, it)) {
       const TcPair& u = it.u;
-      const int my_n = it.ng[g];
-      const int64_t my_tok0 = u.tok0[g];
+      // selects, not indexing by the warp-dependent g (which would put the item in local memory)
+      const int my_n = g ? it.ng[1] : it.ng[0];
+      const int64_t my_tok0 = g ? u.tok0[1] : u.tok0[0];
       const int64_t my_tok = my_tok0 + r / G;
-      const bool row_valid = my_tok < u.tok_end[g];
+      const bool row_valid = my_tok < (g ? u.tok_end[1] : u.tok_end[0]);
       const int start = u.row.start;
       const int hist_tiles = u.row.hist_tiles;
       float m_ref = -INFINITY, l_run = 0.f;
