@@ -62,7 +62,7 @@ constexpr int kFirstSoftmaxWarp = 2;
 constexpr int kLoaderWarp = 0;
 constexpr int kMmaWarp = 1;
 constexpr int kLoaderThreads = 32;
-constexpr int kStagesK = 3;                         // depth of the K ring
+constexpr int kStagesK = 2;                         // depth of the K ring (3 measured slower)
 constexpr int kStagesV = 2;                         // depth of the V ring
 constexpr int kQRegion = kTcRows * 128;             // 16 KiB: one 64-column half of a Q tile
 constexpr int kKvRegion = kTcKv * 128;              // 16 KiB: one 64-column half of a K or V tile
@@ -73,7 +73,7 @@ constexpr int kOffK = kOffQ + kPair * kQBytes;      // kStagesK K buffers
 constexpr int kOffV = kOffK + kStagesK * kKvBytes;  // kStagesV V buffers
 constexpr int kOffBar = kOffV + kStagesV * kKvBytes;
 constexpr int kOffPages = kOffBar + 256;            // block ids (cp.async: kTcKv+1 int64 of one tile; TMA: 128 int32)
-constexpr int kTcSmemBytes = kOffPages + (kTcKv + 1) * 8 + 1024;  // + alignment slack (~226 KiB: one CTA per SM)
+constexpr int kTcSmemBytes = kOffPages + (kTcKv + 1) * 8 + 1024;  // + alignment slack (~194 KiB: one CTA per SM)
 static_assert(kTcSmemBytes <= 232448, "shared memory above the 227 KiB a CTA may use");
 // TMEM (512 columns): S (then P) of row tile g at g*128; O of row tile g at 256 + g*128.
 constexpr uint32_t kTmemCols = 512;
