@@ -265,8 +265,9 @@ __device__ __forceinline__ TcRow tc_row(const PrefillArgs& a, int64_t b, bool re
 // one KV head; its KV tiles are the union of the two row tiles' ranges (history tiles, then chunk
 // tiles up to the causal end of the row tile's last token; the second row tile's range is never
 // shorter unless it is empty), the same for every head.  The units u = b * pairs + p of a head
-// laid end to end form a stream of T tiles; the grid is R CTAs per head, CTA c = r * hkv + h, and
-// with R' = min(R, T) the CTA takes tiles [r*T/R', (r+1)*T/R') of head h's stream, walking them
+// laid end to end form a stream of T cost units (a unit's tiles plus kUnitCost for starting it,
+// TcWalker); the grid is R CTAs per head, CTA c = r * hkv + h, and with R' = min(R, T) the CTA
+// takes positions [r*T/R', (r+1)*T/R') of head h's stream, walking them
 // unit after unit with its K/V rings, TMEM and barrier phases carried across unit boundaries.  The
 // hkv CTAs of one r read the same pool pages at the same time (the heads of a page row are
 // adjacent in memory).  A unit inside one CTA's range writes its output directly; a unit cut by
@@ -307,24 +308,39 @@ struct TcItem {  // one piece of a unit inside one CTA's range
   int slot;        // partial slot, or -1 when the piece is the whole unit
 };
 
-struct TcWalker {  // position in a head's tile stream, advanced item by item
+// Positions in a head's stream are in cost units: a unit of n tiles costs kUnitCost + n, its
+// first kUnitCost units standing for the work of starting a unit (the Q reload and the pipeline
+// refill, ~2.5 tiles measured), so ranges holding more unit starts get fewer tiles.
+constexpr int kUnitCost = 2;
+
+struct TcWalker {  // position in a head's stream, advanced item by item
   int rp, rows;      // current row-tile pair, number of pairs in the batch (below 2^31: prefill_tc_supported)
-  int h, off;        // KV head; tile offset of the position within its unit
-  int left;          // tiles left in the CTA's range
+  int h, off;        // KV head; cost offset of the position within its unit (tile off - kUnitCost)
+  int left;          // cost units left in the CTA's range
+  int used;          // cost units consumed so far (the next item's first tile is at range start + used)
   int pairs, cta;
   __device__ __forceinline__ bool next(const PrefillArgs& a, TcItem& it) {
     if (left <= 0) return false;
     it.u = tc_pair(a, rp, pairs);
+    if (off < kUnitCost) {  // the unit's start-up cost
+      const int skip = min(kUnitCost - off, left);
+      off += skip;
+      left -= skip;
+      used += skip;
+      if (left <= 0) return false;  // the range ends before the unit's first tile
+    }
+    const int t0 = off - kUnitCost;
     it.h = h;
-    it.t_begin = off;
-    it.n = min(it.u.n - off, left);
+    it.t_begin = t0;
+    it.n = min(it.u.n - t0, left);
 #pragma unroll
-    for (int g = 0; g < kPair; ++g) it.ng[g] = max(0, min(it.u.n_tiles[g] - off, it.n));
-    const bool opened_before = off > 0, continues = off + it.n < it.u.n;
+    for (int g = 0; g < kPair; ++g) it.ng[g] = max(0, min(it.u.n_tiles[g] - t0, it.n));
+    const bool opened_before = t0 > 0, continues = t0 + it.n < it.u.n;
     it.slot = opened_before ? 2 * cta : (continues ? 2 * cta + 1 : -1);
     left -= it.n;
     off += it.n;
-    if (off == it.u.n) {  // on to the next unit with tiles
+    used += it.n;
+    if (off == kUnitCost + it.u.n) {  // on to the next unit with tiles
       off = 0;
       while (left > 0 && ++rp < rows && tc_pair(a, rp, pairs).n == 0) {
       }
@@ -485,17 +501,21 @@ __device__ __forceinline__ void zero_padding(const PrefillArgs& a, int tid) {
   }
 }
 
-// Work range of this CTA (all threads): the per-pair tile counts are summed in per-thread chunks
-// of pairs and scanned across the block (`scratch`: 16 int64 of shared memory), then the thread
-// whose chunk holds the CTA's first tile locates it.  Returns the walker at that position, the
-// tiles of a head's stream (`total`) and the CTAs per head that share them (`ctas`).
+// Work range of this CTA (all threads): the per-pair costs (tiles + kUnitCost) are summed in
+// per-thread chunks of pairs and scanned across the block (`scratch`: 16 int64 of shared memory),
+// then the thread whose chunk holds the CTA's first position locates it.  Returns the walker at
+// that position, the cost of a head's stream (`total`) and the CTAs per head that share it
+// (`ctas`).
 __device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, int64_t* scratch, int tid, int64_t& total,
                                              int64_t& ctas) {
   const int warp = tid >> 5, lane = tid & 31;
   const int rows = (int)(a.batch * pairs);
   const int r0 = (int)((int64_t)rows * tid / kTcThreads), r1 = (int)((int64_t)rows * (tid + 1) / kTcThreads);
   int64_t mine = 0;
-  for (int rp = r0; rp < r1; ++rp) mine += tc_pair(a, rp, pairs).n;
+  for (int rp = r0; rp < r1; ++rp) {
+    const int n = tc_pair(a, rp, pairs).n;
+    mine += n > 0 ? kUnitCost + n : 0;
+  }
   int64_t x = mine;  // inclusive scan within the warp
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -511,7 +531,7 @@ __device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, in
     if (w < warp) before += v;
     total += v;
   }
-  const int64_t excl = before + x - mine;  // tiles ahead of this thread's chunk
+  const int64_t excl = before + x - mine;  // cost units ahead of this thread's chunk
   ctas = min((int64_t)(gridDim.x / a.hkv), total);
   const int64_t c = blockIdx.x / a.hkv;  // range index within the head
   const int64_t x0 = c < ctas ? c * total / ctas : 0;
@@ -521,12 +541,13 @@ __device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, in
     int64_t pos = excl;
     for (int rp = r0; rp < r1; ++rp) {
       const int n = tc_pair(a, rp, pairs).n;
-      if (x0 < pos + n) {
+      const int cost = n > 0 ? kUnitCost + n : 0;
+      if (x0 < pos + cost) {
         scratch[0] = rp;
         scratch[1] = x0 - pos;
         break;
       }
-      pos += n;
+      pos += cost;
     }
   }
   __syncthreads();
@@ -535,6 +556,7 @@ __device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, in
   w.pairs = pairs;
   w.cta = (int)blockIdx.x;
   w.left = (int)(x1 - x0);
+  w.used = 0;
   w.rp = w.left > 0 ? (int)scratch[0] : 0;
   w.h = (int)(blockIdx.x % a.hkv);
   w.off = w.left > 0 ? (int)scratch[1] : 0;
@@ -576,26 +598,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   zero_padding<T>(a, tid);
   int64_t total, ctas;
   const TcWalker walk0 = tc_start(a, pairs, reinterpret_cast<int64_t*>(smem + kOffK), tid, total, ctas);
-  if (tid == 0) {  // the unit this CTA opens and leaves unfinished, for the combine kernel
-    int64_t d0 = -1, d1 = 0, d2 = 0;
+  int64_t* const scratch = reinterpret_cast<int64_t*>(smem + kOffK);
+  if (tid == 0) {  // the CTA's tiles, and the unit it opens and leaves unfinished (for the combine)
+    int64_t d0 = -1, d1 = 0, d2 = 0, tiles = 0;
     TcWalker w = walk0;
     TcItem it;
     const int64_t r = blockIdx.x / a.hkv;
-    int64_t pos = r * total / max(ctas, (int64_t)1);
+    const int64_t x0 = r * total / max(ctas, (int64_t)1);
     while (w.next(a, it)) {
-      if (it.slot == 2 * (int)blockIdx.x + 1) {  // t_begin == 0: the unit ends at pos + its tiles
+      tiles += it.n;
+      if (it.slot == 2 * (int)blockIdx.x + 1) {  // t_begin == 0: the unit's tiles follow its first one
+        const int64_t first = x0 + w.used - it.n;  // cost position of the unit's first tile
         d0 = it.u.b * pairs + it.u.pair;
         d1 = it.h;
-        d2 = ((pos + it.u.n) * ctas - 1) / total * a.hkv + it.h;  // CTA of the unit's last tile
+        d2 = ((first + it.u.n) * ctas - 1) / total * a.hkv + it.h;  // CTA of the unit's last tile
       }
-      pos += it.n;
     }
     ws_desc[blockIdx.x * 4 + 0] = d0;
     ws_desc[blockIdx.x * 4 + 1] = d1;
     ws_desc[blockIdx.x * 4 + 2] = d2;
+    scratch[16] = tiles;  // clear of the words the start scan used
   }
-  if (walk0.left == 0) return;  // uniform for the CTA
-  const int64_t n_tiles = walk0.left;
+  __syncthreads();
+  const int64_t n_tiles = scratch[16];
+  if (n_tiles == 0) return;  // uniform for the CTA
 
   if (tid == 0) {
     mbar_init(q_full, kTma ? 1 : kLoaderThreads);
@@ -1112,7 +1138,7 @@ bool prefill_tc_supported(const PrefillArgs& a, int dtype) {
   {  // the stream of one head (pairs of the batch x their tiles) is counted in 32-bit integers
     const int64_t tpt = kTcRows / a.groups;
     const int64_t pairs = ((a.padded_len + tpt - 1) / tpt + kPair - 1) / kPair;
-    const int64_t tiles = (a.table_stride * a.block_size + a.padded_len) / kTcKv + 2;
+    const int64_t tiles = (a.table_stride * a.block_size + a.padded_len) / kTcKv + 2 + kUnitCost;
     if (a.batch * pairs * tiles >= (int64_t(1) << 31)) return false;
   }
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
