@@ -107,6 +107,32 @@ def test_prefill_tensor_core_path(shape):
     assert not got[~valid].any()
 
 
+STREAM_SHAPES = [
+    # hq, h, d, bs, starts, lens: how the persistent kernel cuts each KV head's tile stream
+    # one KV head, G = 8: ~50 cost units over the CTAs of one head, so most CTAs hold a single
+    # tile or only the start-up cost of a unit, and a long unit is merged from ~25 pieces
+    (8, 1, 128, 16, [3000, 0, 1500, 40], [16, 16, 16, 3]),
+    # G = 4, empty and one-token rows between full chunks: many short units per CTA
+    (8, 2, 128, 16, [0, 700, 1200, 0, 64, 900, 5, 500], [128, 1, 60, 0, 128, 7, 33, 0]),
+    # G = 8, 300-token chunk over 10 row-tile pairs, next to a 9000-token history; block size 32
+    (16, 2, 128, 32, [9000, 0], [300, 50]),
+]
+
+
+@pytest.mark.parametrize("shape", STREAM_SHAPES, ids=[str(s[:4]) for s in STREAM_SHAPES])
+def test_prefill_tensor_core_stream_split(shape):
+    hq, h, d, bs, starts, lens = shape
+    inp = _random_prefill(hq, h, d, bs, starts, lens, "bfloat16", seed=7)
+    out = run_prefill(inp, bs, d)
+    want = po.chunk_prefill_attention(inp["query"], inp["key_chunk"], inp["value_chunk"], inp["key_pool"],
+                                      inp["value_pool"], inp["tables_list"], starts, lens, d**-0.5)
+    length = max(lens)
+    valid = np.arange(length)[None, :] >= (length - np.asarray(lens))[:, None]
+    got = po.as_float(to_numpy(out), np.float64)
+    assert_attention_close(got[valid], want[valid], "bfloat16")
+    assert not got[~valid].any()  # padding positions, and rows without a chunk, are zeros
+
+
 def test_prefill_tensor_core_rescales_on_growing_scores():
     """Queries aligned with later keys make the running max jump by far more than 2^8 across KV
     tiles, so the TMEM accumulator rescale path runs; result must still match the oracle."""
