@@ -47,6 +47,9 @@ SEED = 1234
 # algorithmic bytes; other workloads scale it by the tokens processed (traffic grows in proportion).
 NCU_TRAFFIC_C2 = 2.296959e9 + 13.282816e6
 NCU_ALGORITHMIC_C2 = 2.217e9
+# DRAM read + write bytes of one prefill_tc_kernel launch at config 4 (ncu, profiles/prefill_tc_c4.md);
+# the same workload every run, so no scaling.
+NCU_TRAFFIC_C4 = 368.0704e6 + 17.462272e6
 
 # name -> (hq, hkv, batch, ctx_lo, ctx_hi, layer calls per step, resident layer pools, batch scales with N)
 WORKLOADS = {
@@ -320,7 +323,8 @@ def run_c4(args) -> None:
                     "algorithmic_gflop": flops / 1e9, "kernel": "prefill_tc_kernel"},
         "decode": {"ms": ms_dec, "gbs": dec_bytes / (ms_dec * 1e-3) / 1e9},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak_t, "unit": "TFLOP/s",
-                     "frac": tflops / peak_t, "traffic": None,
+                     "frac": tflops / peak_t, "traffic": NCU_TRAFFIC_C4,
+                     "traffic_unit": "bytes per launch of prefill_tc_kernel (ncu dram read+write)",
                      "peak_source": "measured" if peaks else "fallback"},
         "gpu_launches": args.steps * 2 + args.steps * 2,
         "clocks": clocks.summary(),
