@@ -980,11 +980,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
 
 // Merge the pieces of units cut by CTA boundaries.  CTA (c, g, row group) reads CTA c's
 // descriptor (the unit c opened and left unfinished, and the last CTA c1 of the same head holding
-// a piece of it) and merges row tile g's rows [16 * group, 16 * group + 16) over the pieces in
+// a piece of it) and merges row tile g's rows [8 * group, 8 * group + 8) over the pieces in
 // slots 2c + 1 and 2c' (c' = c + hkv, c + 2 hkv, ..., c1); each thread merges (row, 16-byte column chunk) items in one online pass
 // (running max, rescaled sums), so a warp reads 512 contiguous bytes of one row per piece.
 constexpr int kCombineThreads = 128;
-constexpr int kCombineRows = 16;
+constexpr int kCombineRows = 8;
 
 template <typename T>
 __global__ void __launch_bounds__(kCombineThreads) prefill_combine_kernel(const PrefillArgs a, const float* ws_o,
