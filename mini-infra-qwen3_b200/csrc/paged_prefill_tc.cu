@@ -1,9 +1,9 @@
 // Chunked-prefill paged attention on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
 // Variant: bf16 / fp16, head_dim 128, any block size, G = Hq/H_kv in {1, 2, 4, 8}.
-// Persistent CTAs (352 threads, one per SM) share the work as equal ranges of one stream of KV
-// tiles (see TcWalker below).  A unit of that stream is one (sequence, pair of tiles of 128 query
-// rows, KV head): a row tile packs 128/G chunk tokens x the G query heads of the KV head (row
+// Persistent CTAs (352 threads, one per SM) share the work as equal ranges of per-KV-head streams
+// of KV tiles, each unit start weighted as kUnitCost extra tiles (see TcWalker below).  A unit of a
+// stream is one (sequence, pair of tiles of 128 query rows, KV head): a row tile packs 128/G chunk tokens x the G query heads of the KV head (row
 // r = token r/G, head r%G); the unit's two row tiles are consecutive, so every K/V tile staged in
 // shared memory serves 2 x 128 query rows of the whole GQA group (half the L2 -> SM bytes per
 // FLOP of one row tile per CTA).  The KV range of a row tile is its history tiles, then its causal
