@@ -43,11 +43,11 @@ KV_BYTES_PER_TOKEN = 2 * HKV * D * 2  # K+V, all 8 KV heads, bf16
 SEED = 1234
 
 # DRAM traffic of one decode_split launch on config 2 from the committed ncu capture
-# (profiles/decode_split_c2.md: dram__bytes_read.sum + dram__bytes_write.sum) and that launch's
+# (ncu `dram__bytes_read.sum + dram__bytes_write.sum`, the decode_split summary under profiles/) and that launch's
 # algorithmic bytes; other workloads scale it by the tokens processed (traffic grows in proportion).
 NCU_TRAFFIC_C2 = 2.296959e9 + 13.282816e6
 NCU_ALGORITHMIC_C2 = 2.217e9
-# DRAM read + write bytes of one prefill_tc_kernel launch at config 4 (ncu, profiles/prefill_tc_c4.md);
+# DRAM read + write bytes of one prefill_tc_kernel launch at config 4 (ncu, the prefill_tc summary under profiles/);
 # the same workload every run, so no scaling.
 NCU_TRAFFIC_C4 = 368.0704e6 + 17.462272e6
 
