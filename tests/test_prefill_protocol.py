@@ -154,8 +154,10 @@ class Barrier:
             self.phases += 1
 
 
-def run_cta(walk0, seed):
-    """One CTA's roles as coroutines; ('wait', bar, k) waits for the completion of phase k."""
+def run_cta(walk0, seed, loader="tma"):
+    """One CTA's roles as coroutines; ('wait', bar, k) waits for the completion of phase k.
+    loader="tma": Q and K from warp 0, V from warp 10 (block sizes 16/32/64); loader="cp": one warp
+    stages Q, K and V with cp.async (other block sizes)."""
     rnd = random.Random(seed)
     bars = {"q_full": Barrier(1)}
     for i in range(K_STAGES):
@@ -253,7 +255,37 @@ def run_cta(walk0, seed):
                 fin += 1
                 yield ("arrive_all", f"o_free{g}")
 
-    roles = {"k": k_loader(), "v": v_loader(), "mma": mma(), "sm0": softmax(0), "sm1": softmax(1)}
+    def cp_loader():  # warp 0 alone: K(0 .. K_STAGES-1), V(0), then V(j+1), K(j + K_STAGES)
+        yield ("tma", "q_full")
+        jk = 0
+        while jk < min(n_tiles, K_STAGES):
+            yield ("tma", f"k_full{jk % K_STAGES}")
+            jk += 1
+        yield ("tma", "v_full0")
+        s_done_needed = 0
+        for j in range(n_tiles):
+            it, i = tile_items[j]
+            if i + 1 == it["n"]:
+                s_done_needed += it["ng"][0] + it["ng"][1]
+            if j + 1 < n_tiles:
+                opens = tile_items[j + 1][1] == 0  # tile j+1 opens an item
+                if j + 1 >= V_STAGES:
+                    yield ("wait", f"v_empty{(j + 1) % V_STAGES}", (j + 1) // V_STAGES - 1)
+                yield ("tma", f"v_full{(j + 1) % V_STAGES}")
+                if opens:
+                    yield ("wait", f"k_empty{j % K_STAGES}", j // K_STAGES)
+                    yield ("check_s_done", s_done_needed)
+                    yield ("tma", "q_full")
+            if jk < n_tiles:
+                if jk >= K_STAGES:
+                    yield ("wait", f"k_empty{jk % K_STAGES}", jk // K_STAGES - 1)
+                yield ("tma", f"k_full{jk % K_STAGES}")
+                jk += 1
+
+    if loader == "tma":
+        roles = {"k": k_loader(), "v": v_loader(), "mma": mma(), "sm0": softmax(0), "sm1": softmax(1)}
+    else:
+        roles = {"cp": cp_loader(), "mma": mma(), "sm0": softmax(0), "sm1": softmax(1)}
     blocked = dict.fromkeys(roles)
     done, inflight, clock, mma_clock = set(), [], 0, 0
     while len(done) < len(roles) or inflight:
@@ -330,8 +362,9 @@ def test_split_pieces_tile_every_unit():
 
 
 def test_barrier_protocol_has_no_deadlock_or_phase_slip():
-    for shape in _shapes():
-        for per_head in (18, 7, 1):
-            walkers, _, _ = split(shape, per_head)
-            for c, w in enumerate(walkers):
-                run_cta(w, seed=1000 * per_head + c)
+    for loader in ("tma", "cp"):
+        for shape in _shapes():
+            for per_head in (18, 7, 1):
+                walkers, _, _ = split(shape, per_head)
+                for c, w in enumerate(walkers):
+                    run_cta(w, seed=1000 * per_head + c, loader=loader)
