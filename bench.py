@@ -190,14 +190,16 @@ def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8, rng=None, max_
         total_t += time.perf_counter() - t0
         total_tokens += int(ctx.sum())
         n += 1
+    bytes_read = total_tokens * KV_BYTES_PER_TOKEN
     return {
-        "value": total_tokens * KV_BYTES_PER_TOKEN / total_t / 1e9,
+        "value": bytes_read / total_t / 1e9,
         "unit": "GB/s",
         "cores": threads,
         "kind": "port",
         "sample": f"{n} x {per_sample} sequences of config 2 (ctx U[{CTX_LO},{CTX_HI}]), bf16 torch-CPU "
                   f"restatement of the reference's gather + GQA expand + matmul/softmax, {total_t:.1f} s of CPU work",
         "tokens": total_tokens,
+        "bytes": bytes_read,
         "seconds": total_t,
     }
 
@@ -205,23 +207,67 @@ def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8, rng=None, max_
 def run_reference(args, budget_s: float = 150.0) -> None:
     """Reference arm: the CPU restatement of the reference's decode path on the host cores.
 
-    Each step is a bounded sample of config 2 (n_seq sequences), with n_seq sized from one probe so
-    that warmup + steps fit in about `budget_s` seconds whatever --steps is."""
+    Each step is a bounded sample of config 2 with all KV heads: 1 to 32 sequences, sized from a
+    probe (and re-sized after the warm-up steps) so that warmup + steps take about `budget_s`
+    seconds; at one sequence per step the run takes longer when --steps is large (3000 by default,
+    ~0.03 s per step on 8 host threads).  The sample (contexts, tables, a pool of its blocks,
+    queries) is drawn once and run at every step, so no step pays for drawing it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     rng = np.random.RandomState(SEED + 2)
-    probe = cpu_decode_sample(seconds=0.0, per_sample=1, rng=rng, max_samples=1)
-    n_seq = int(max(1, min(32, (budget_s / (args.steps + args.warmup)) / max(probe["seconds"], 1e-6))))
-    tokens, secs = 0, 0.0
-    for i in range(args.warmup + args.steps):
-        r = cpu_decode_sample(seconds=0.0, per_sample=n_seq, rng=rng, max_samples=1)
-        if i >= args.warmup:
-            tokens += r["tokens"]
-            secs += r["seconds"]
-    value = tokens * KV_BYTES_PER_TOKEN / secs / 1e9
+    cpu_decode_sample(seconds=0.0, per_sample=1, rng=rng, max_samples=1)  # first-call costs
+    probe = cpu_decode_sample(seconds=0.0, per_sample=4, rng=rng, max_samples=1)
+    # seconds per (token, KV head); a probe's own lengths are random, so scale to the mean context
+    per_tok_head = probe["seconds"] / max(probe["tokens"] * HKV, 1)
+    mean_ctx = (CTX_LO + CTX_HI) / 2
+    step_s = budget_s / (args.steps + args.warmup)
+    n_seq = int(max(1, min(32, step_s / max(per_tok_head * HKV * mean_ctx, 1e-12))))
+    heads = HKV
+    from oracle import paged_oracle as po
+
+    # One sample of n sequences (contexts, block tables, a pool of just their blocks, queries) is
+    # drawn once and run at every step, as each cpu_decode_sample call runs its own fresh sample.
+    gen = torch.Generator().manual_seed(SEED + 3)
+    samples = {}
+
+    def step(n, h):
+        if n not in samples:
+            ctx = rng.randint(CTX_LO, CTX_HI + 1, size=n).astype(np.int64)
+            need = -(-ctx // BS)
+            nb = 1 + int(need.sum())
+            perm = 1 + rng.permutation(nb - 1)
+            tables = np.zeros((n, int(need.max())), dtype=np.int64)
+            off = 0
+            for i in range(n):
+                tables[i, : need[i]] = perm[off : off + need[i]]
+                off += need[i]
+            samples[n] = (torch.randn((n, HQ, D), generator=gen).to(torch.bfloat16),
+                          torch.randn((nb, BS, HKV, D), generator=gen).to(torch.bfloat16),
+                          torch.randn((nb, BS, HKV, D), generator=gen).to(torch.bfloat16),
+                          torch.from_numpy(tables), torch.from_numpy(ctx))
+        q, kp, vp, tab, cx = samples[n]
+        t0 = time.perf_counter()
+        po.torch_paged_decode(q, kp, vp, tab, cx, D**-0.5)
+        return float(cx.sum()) * KV_BYTES_PER_TOKEN, time.perf_counter() - t0
+
+    t_warm = time.perf_counter()
+    for _ in range(args.warmup):
+        step(n_seq, heads)
+    # Re-size from the warm-up's wall time per step (it includes the per-call costs a small probe
+    # underestimates on hosts with many threads), so the timed steps fit the rest of the budget.
+    per_call = (time.perf_counter() - t_warm) / args.warmup
+    if per_call * args.steps > budget_s and n_seq > 1:
+        n_seq = int(max(1, n_seq * budget_s / (per_call * args.steps)))
+        step(n_seq, heads)  # the new size's pool, untimed
+    bytes_read, secs = 0.0, 0.0
+    for _ in range(args.steps):
+        b, t = step(n_seq, heads)
+        bytes_read += b
+        secs += t
+    value = bytes_read / secs / 1e9
     cb = {"value": value, "unit": "GB/s", "cores": host_threads(), "kind": "port",
-          "sample": f"{args.steps} timed steps x {n_seq} sequences of config 2 (ctx U[{CTX_LO},{CTX_HI}]), "
+          "sample": f"{args.steps} timed steps x {n_seq} sequences x {heads} KV heads of config 2 (ctx U[{CTX_LO},{CTX_HI}]), "
                     f"bf16 torch-CPU restatement of the reference's gather + GQA expand + matmul/softmax, "
                     f"{secs:.1f} s of CPU work"}
     line = {
