@@ -1,18 +1,33 @@
-"""Benchmark of the paged decode hot path (isolated paged-decode attention at
-the Qwen3-0.6B shape, bf16).
+"""Benchmark of the paged KV-cache hot path (BASELINE.json metric: paged decode KV-read GB/s as a
+fraction of HBM, and engine decode tok/s at 1/2/4/8 GPUs).
 
-One STEP = one layer's decode KV append + paged GQA decode attention over B sequences (and, with
-N > 1 ranks, the NCCL all-gather of the per-head outputs).  Weak scaling over the head partition:
-at N ranks the global batch is 256*N sequences and rank r holds KV heads [r*8/N, (r+1)*8/N), so
-every rank reads the same bytes per step as one GPU at N=1.
+Default workload: BASELINE config 5, the Qwen3-8B-shape paged-decode sweep (bf16, 32 query / 8 KV
+heads, head_dim 128, block_size 16, batch 512, contexts U[1024, 32768]).  One STEP = one decode
+step of the 36-layer model's attention: per layer call, the decode KV append + paged GQA decode
+attention of the 512 sequences (and, with N > 1 ranks, the exchange of the per-head outputs).
+The 36 layer calls cycle over 4 resident layer pools (~156 GB on one GPU; 36 resident layers would
+need ~1.3 TB).  Strong scaling over the KV-head partition: at N ranks rank r holds KV heads
+[r*8/N, (r+1)*8/N) of every sequence, so the total work is fixed and each rank reads 1/N of it.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5|c2|c3|c4]
 
-Prints ONE JSON line on rank 0.  ``value`` = KV bytes read per step by all ranks (sum of context
-lengths x 4096 B for 8 KV heads x 128 dims x K+V x bf16) / max-over-ranks device time per step.
-``e2e`` = the same metric through the public op with host (pinned) inputs copied in and the output
-copied out every step.  ``--impl reference`` times the CPU restatement of the reference's torch
-path (gather the padded history, expand GQA, matmul/softmax/matmul) on the host cores instead.
+Prints ONE JSON line on rank 0.  ``value`` = KV bytes read per step by all ranks together (sum of
+context lengths x 4096 B for 8 KV heads x 128 dims x K+V x bf16, x 36 layer calls) / the max over
+ranks of the device time per step.  Besides the contract keys the line carries:
+
+* ``per_layer_ms``: attention (append + split-K decode + combine) and exchange (all-gather of the
+  per-head outputs) of one layer call, each timed alone, and which one limits the step;
+* ``parity``: after the timed region, the output rows of a few sequences (the longest and the
+  shortest context among them) against a float32 torch reference computed on the device from the
+  same pools; with N > 1 ranks the references are gathered, so the check covers the exchange;
+* ``prefill`` / ``scatter``: the chunked-prefill tensor-core launch and the KV scatter at BASELINE
+  config 4's shapes (one GPU), each with its roofline fraction and, for the prefill, a parity check;
+* ``e2e``: the same metric through the public op with inputs copied from pinned host memory and
+  the output copied back every layer call;
+* ``cpu_baseline`` (rank 0, N = 1): the CPU restatement of the reference's torch decode path on
+  the host cores, over the first sequences of the same seeded workload.
+
+``--impl reference`` times that CPU restatement alone (rank 0; the other ranks exit at once).
 """
 
 from __future__ import annotations
@@ -35,90 +50,109 @@ for _p in (ROOT, ROOT / "mini-infra-qwen3_b200"):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-# BASELINE config 2 (the default workload; also the CPU baseline's shape)
-HQ, HKV, D, BS = 16, 8, 128, 16
-B_PER_RANK = 256
-CTX_LO, CTX_HI = 128, 4096
-KV_BYTES_PER_TOKEN = 2 * HKV * D * 2  # K+V, all 8 KV heads, bf16
+D, BS = 128, 16
 SEED = 1234
+METRIC = "paged decode KV-read GB/s"
 
-# DRAM traffic of one decode_split launch on config 2 from the committed ncu capture
-# (ncu `dram__bytes_read.sum + dram__bytes_write.sum`, the decode_split summary under profiles/) and that launch's
-# algorithmic bytes; other workloads scale it by the tokens processed (traffic grows in proportion).
-NCU_TRAFFIC_C2 = 2.296959e9 + 13.282816e6
-NCU_ALGORITHMIC_C2 = 2.217e9
-# DRAM read + write bytes of one prefill_tc_kernel launch at config 4 (ncu, the prefill_tc summary under profiles/);
-# the same workload every run, so no scaling.
-NCU_TRAFFIC_C4 = 368.0704e6 + 17.462272e6
+# DRAM read + write bytes per launch from committed ncu captures (the summaries under profiles/ give
+# the commands), with the algorithmic bytes of the captured launch, so that other sizes can be
+# scaled by the tokens processed (the traffic grows in proportion).
+NCU_DECODE = {"traffic": 2.296959e9 + 13.282816e6, "algorithmic": 2.217e9,
+              "source": "ncu dram read+write of decode_split_kernel, config 2 on one GPU; scaled by tokens"}
+NCU_PREFILL_C4 = {"traffic": 368.0704e6 + 17.462272e6,
+                  "source": "ncu dram read+write of prefill_tc_kernel at config 4"}
 
-# name -> (hq, hkv, batch, ctx_lo, ctx_hi, layer calls per step, resident layer pools, batch scales with N)
+# name -> heads, batch, contexts, layer calls per step, resident layer pools, whether the batch grows with N
 WORKLOADS = {
+    # config 5: Qwen3-8B heads, batch 512, contexts U[1024, 32768], 36 layer calls per step cycling over
+    # 4 resident layer pools; strong scaling (the KV heads are split over N ranks)
+    "c5": dict(hq=32, hkv=8, batch=512, ctx=(1024, 32768), layers=36, resident=4, weak=False,
+               name="config5_paged_decode_sweep_qwen3_8b_shape"),
     # config 2: one layer of the Qwen3-0.6B decode op; weak scaling (256 sequences per rank)
     "c2": dict(hq=16, hkv=8, batch=256, ctx=(128, 4096), layers=1, resident=1, weak=True,
                name="config2_paged_decode_op_qwen3_0.6b_shape"),
-    # config 5: Qwen3-8B heads, batch 512, contexts U[1024, 32768], 36 layer calls per step cycling over
-    # 4 resident layer pools (~142 GB per box); strong scaling (the heads are split over N ranks)
-    "c5": dict(hq=32, hkv=8, batch=512, ctx=(1024, 32768), layers=36, resident=4, weak=False,
-               name="config5_paged_decode_sweep_qwen3_8b_shape"),
 }
 
 
-def measured_peaks() -> dict:
+def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-def workload(spec: dict, world: int, rank: int, device):
-    """Seeded inputs for this rank: contexts, block tables, resident pools (own KV heads), q, new K/V."""
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+# ------------------------------------------------------------------------------------------------
+# seeded workload (shared by the GPU arm, the CPU baseline and the reference arm)
+# ------------------------------------------------------------------------------------------------
+def seeded_sequences(spec: dict, world: int) -> dict:
+    """Contexts (including the appended token), block tables (a seeded permutation of the pool's
+    blocks, null-padded), append slots and the pool size: exactly the needed blocks + 10 % free +
+    the null block.  Identical on every rank."""
     b = spec["batch"] * (world if spec["weak"] else 1)
-    h_loc = spec["hkv"] // world
     lo, hi = spec["ctx"]
     rng = np.random.RandomState(SEED)
-    ctx = rng.randint(lo, hi + 1, size=b).astype(np.int64)  # includes the appended token
+    ctx = rng.randint(lo, hi + 1, size=b).astype(np.int64)
     need = -(-ctx // BS)
     used = int(need.sum())
-    num_blocks = 1 + used + used // 10  # exactly the needed blocks + 10% free + null block
+    num_blocks = 1 + used + used // 10
     perm = rng.permutation(np.arange(1, num_blocks))[:used]
-    max_blocks = int(need.max())
-    tables = np.zeros((b, max_blocks), dtype=np.int64)
+    tables = np.zeros((b, int(need.max())), dtype=np.int64)
     offs = np.concatenate([[0], np.cumsum(need)])
     for i in range(b):
         tables[i, : need[i]] = perm[offs[i] : offs[i + 1]]
     pos = ctx - 1
     slots = tables[np.arange(b), pos // BS] * BS + pos % BS
+    return dict(b=b, ctx=ctx, tables=tables, slots=slots, num_blocks=num_blocks)
+
+
+def device_inputs(spec: dict, seqs: dict, world: int, rank: int, device) -> dict:
+    """This rank's resident pools (its own KV heads), queries and new K/V, N(0, 1) bf16."""
+    h_loc, hq_loc = spec["hkv"] // world, spec["hq"] // world
     g = torch.Generator(device=device).manual_seed(SEED + 17 * rank)
-    pools = []
-    for _ in range(spec["resident"]):
-        kp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
-        vp = torch.randn((num_blocks, BS, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
-        pools.append((kp, vp))
-    hq_loc = spec["hq"] // world
+    shape = (seqs["num_blocks"], BS, h_loc, D)
+    pools = [(torch.randn(shape, generator=g, device=device, dtype=torch.bfloat16),
+              torch.randn(shape, generator=g, device=device, dtype=torch.bfloat16)) for _ in range(spec["resident"])]
+    b = seqs["b"]
     q = torch.randn((b, hq_loc, D), generator=g, device=device, dtype=torch.bfloat16)
     kn = torch.randn((b, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
     vn = torch.randn((b, h_loc, D), generator=g, device=device, dtype=torch.bfloat16)
-    return dict(b=b, ctx=ctx, tables=tables, slots=slots, num_blocks=num_blocks, pools=pools, q=q, kn=kn, vn=vn,
-                h_loc=h_loc, hq_loc=hq_loc)
+    return dict(pools=pools, q=q, kn=kn, vn=vn, h_loc=h_loc, hq_loc=hq_loc)
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks
+# ------------------------------------------------------------------------------------------------
+def nvsmi_id(index: int) -> str:
+    """nvidia-smi --id of the CUDA device `index` (its UUID, so remapped CUDA_VISIBLE_DEVICES still
+    name the GPU that runs the work; the PCI bus id if no UUID is reported)."""
+    props = torch.cuda.get_device_properties(index)
+    uuid = str(getattr(props, "uuid", "") or "")
+    if uuid:
+        return uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    return f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons (every 100 ms) while the timed legs run."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
-        self.index = index
+        self.gpu = nvsmi_id(index)
         self.proc = None
         self.lines: list[str] = []
 
     def __enter__(self):
         if shutil.which("nvidia-smi"):
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -152,147 +186,147 @@ class ClockSampler:
                 if flag.lower().startswith("active"):
                     reasons.add(name)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "gpu": self.gpu}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm), "gpu": self.gpu}
 
 
-def host_threads() -> int:
-    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+def event_ms(fn, n: int, device) -> float:
+    """Mean device time of fn over n back-to-back calls (CUDA events on the current stream)."""
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(device)
+    return e0.elapsed_time(e1) / n
 
 
-def cpu_decode_sample(seconds: float = 12.0, per_sample: int = 8, rng=None, max_samples: int | None = None) -> dict:
-    """Time the torch-CPU restatement of the reference's decode (gather + GQA expand + matmul/softmax).
+# ------------------------------------------------------------------------------------------------
+# CPU legs: the reference's torch decode path restated (oracle), on the host cores
+# ------------------------------------------------------------------------------------------------
+def cpu_sample_inputs(spec: dict, seqs: dict, n: int, gen: torch.Generator):
+    """The first n sequences of the seeded workload with all KV heads: their contexts and block
+    tables renumbered into a pool of just their blocks, with N(0, 1) bf16 pools and queries."""
+    ctx = seqs["ctx"][:n]
+    need = -(-ctx // BS)
+    nb = 1 + int(need.sum())
+    tables = np.zeros((n, int(need.max())), dtype=np.int64)
+    perm = 1 + np.random.RandomState(SEED + 5).permutation(nb - 1)
+    off = 0
+    for i in range(n):
+        tables[i, : need[i]] = perm[off : off + need[i]]
+        off += need[i]
+    hq, hkv = spec["hq"], spec["hkv"]
+    q = torch.randn((n, hq, D), generator=gen).to(torch.bfloat16)
+    kp = torch.randn((nb, BS, hkv, D), generator=gen).to(torch.bfloat16)
+    vp = torch.randn((nb, BS, hkv, D), generator=gen).to(torch.bfloat16)
+    return q, kp, vp, torch.from_numpy(tables), torch.from_numpy(ctx)
 
-    Runs samples of `per_sample` config-2 sequences until `seconds` of CPU work (or `max_samples`)."""
+
+def cpu_decode_leg(spec: dict, seqs: dict, seconds: float, steps: int | None = None, warmup: int = 1) -> dict:
+    """Time the torch-CPU restatement of the reference's decode (padded block-table gather, GQA
+    repeat_interleave, matmul / fp32 softmax / matmul) on the first sequences of the workload.
+
+    The sample size n is chosen from a one-sequence probe so that one call takes about
+    seconds / steps; with `steps` None the calls repeat until `seconds` of CPU work."""
     from oracle import paged_oracle as po
 
     threads = host_threads()
     torch.set_num_threads(threads)
-    rng = rng if rng is not None else np.random.RandomState(SEED + 1)
-    total_tokens, total_t, n = 0, 0.0, 0
-    while (total_t < seconds or n == 0) and (max_samples is None or n < max_samples):
-        ctx = rng.randint(CTX_LO, CTX_HI + 1, size=per_sample).astype(np.int64)
-        need = -(-ctx // BS)
-        nb = 1 + int(need.sum())
-        tables = np.zeros((per_sample, int(need.max())), dtype=np.int64)
-        perm = rng.permutation(np.arange(1, nb))
-        off = 0
-        for i in range(per_sample):
-            tables[i, : need[i]] = perm[off : off + need[i]]
-            off += need[i]
-        g = torch.Generator().manual_seed(int(rng.randint(1 << 30)))
-        kp = torch.randn((nb, BS, HKV, D), generator=g).to(torch.bfloat16)
-        vp = torch.randn((nb, BS, HKV, D), generator=g).to(torch.bfloat16)
-        q = torch.randn((per_sample, HQ, D), generator=g).to(torch.bfloat16)
-        tab, cx = torch.from_numpy(tables), torch.from_numpy(ctx)
-        t0 = time.perf_counter()
-        po.torch_paged_decode(q, kp, vp, tab, cx, D**-0.5)
-        total_t += time.perf_counter() - t0
-        total_tokens += int(ctx.sum())
-        n += 1
-    bytes_read = total_tokens * KV_BYTES_PER_TOKEN
-    return {
-        "value": bytes_read / total_t / 1e9,
-        "unit": "GB/s",
-        "cores": threads,
-        "kind": "port",
-        "sample": f"{n} x {per_sample} sequences of config 2 (ctx U[{CTX_LO},{CTX_HI}]), bf16 torch-CPU "
-                  f"restatement of the reference's gather + GQA expand + matmul/softmax, {total_t:.1f} s of CPU work",
-        "tokens": total_tokens,
-        "bytes": bytes_read,
-        "seconds": total_t,
-    }
-
-
-def run_reference(args, budget_s: float = 150.0) -> None:
-    """Reference arm: the CPU restatement of the reference's decode path on the host cores.
-
-    Each step is a bounded sample of config 2 with all KV heads: 1 to 32 sequences, sized from a
-    probe (and re-sized after the warm-up steps) so that warmup + steps take about `budget_s`
-    seconds; at one sequence per step the run takes longer when --steps is large (3000 by default,
-    ~0.03 s per step on 8 host threads).  The sample (contexts, tables, a pool of its blocks,
-    queries) is drawn once and run at every step, so no step pays for drawing it."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    rng = np.random.RandomState(SEED + 2)
-    cpu_decode_sample(seconds=0.0, per_sample=1, rng=rng, max_samples=1)  # first-call costs
-    probe = cpu_decode_sample(seconds=0.0, per_sample=4, rng=rng, max_samples=1)
-    # seconds per (token, KV head); a probe's own lengths are random, so scale to the mean context
-    per_tok_head = probe["seconds"] / max(probe["tokens"] * HKV, 1)
-    mean_ctx = (CTX_LO + CTX_HI) / 2
-    step_s = budget_s / (args.steps + args.warmup)
-    n_seq = int(max(1, min(32, step_s / max(per_tok_head * HKV * mean_ctx, 1e-12))))
-    heads = HKV
-    from oracle import paged_oracle as po
-
-    # One sample of n sequences (contexts, block tables, a pool of just their blocks, queries) is
-    # drawn once and run at every step, as each cpu_decode_sample call runs its own fresh sample.
     gen = torch.Generator().manual_seed(SEED + 3)
-    samples = {}
-
-    def step(n, h):
-        if n not in samples:
-            ctx = rng.randint(CTX_LO, CTX_HI + 1, size=n).astype(np.int64)
-            need = -(-ctx // BS)
-            nb = 1 + int(need.sum())
-            perm = 1 + rng.permutation(nb - 1)
-            tables = np.zeros((n, int(need.max())), dtype=np.int64)
-            off = 0
-            for i in range(n):
-                tables[i, : need[i]] = perm[off : off + need[i]]
-                off += need[i]
-            samples[n] = (torch.randn((n, HQ, D), generator=gen).to(torch.bfloat16),
-                          torch.randn((nb, BS, HKV, D), generator=gen).to(torch.bfloat16),
-                          torch.randn((nb, BS, HKV, D), generator=gen).to(torch.bfloat16),
-                          torch.from_numpy(tables), torch.from_numpy(ctx))
-        q, kp, vp, tab, cx = samples[n]
+    kv_bytes_per_token = 2 * spec["hkv"] * D * 2
+    probe = cpu_sample_inputs(spec, seqs, 1, gen)
+    po.torch_paged_decode(*probe[:5], D**-0.5)  # first-call costs
+    t0 = time.perf_counter()
+    po.torch_paged_decode(*probe[:5], D**-0.5)
+    per_token = (time.perf_counter() - t0) / float(probe[4].sum())
+    per_call = seconds / (steps if steps else 8)
+    mean_ctx = float(seqs["ctx"].mean())
+    n = int(max(1, min(seqs["b"], per_call / max(per_token * mean_ctx, 1e-12))))
+    # host memory of one call: the padded K/V gather plus its GQA expansion, ~(H_kv + H_q) x 2 x D x 2 B
+    # per padded position per sequence; keep it under ~8 GB
+    per_seq = float(seqs["ctx"].max()) * (spec["hkv"] + spec["hq"]) * 2 * D * 2
+    n = int(max(1, min(n, 8e9 // per_seq)))
+    sample = cpu_sample_inputs(spec, seqs, n, gen)
+    for _ in range(warmup):
+        po.torch_paged_decode(*sample, D**-0.5)
+    tokens = float(sample[4].sum())
+    total, calls = 0.0, 0
+    while (steps is None and (total < seconds or calls == 0)) or (steps is not None and calls < steps):
         t0 = time.perf_counter()
-        po.torch_paged_decode(q, kp, vp, tab, cx, D**-0.5)
-        return float(cx.sum()) * KV_BYTES_PER_TOKEN, time.perf_counter() - t0
+        po.torch_paged_decode(*sample, D**-0.5)
+        total += time.perf_counter() - t0
+        calls += 1
+    value = tokens * kv_bytes_per_token * calls / total / 1e9
+    return {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{calls} calls x the first {n} of the {seqs['b']} seeded sequences of {spec['name']} "
+                      f"(ctx {int(sample[4].min())}-{int(sample[4].max())}, all {spec['hkv']} KV heads, one layer), "
+                      f"bf16 torch-CPU restatement of the reference's gather + GQA expand + matmul/softmax, "
+                      f"{total:.1f} s of CPU work; GB/s of KV read (a reduced batch: the full batch does not fit "
+                      f"the reference's padded gather in host memory)",
+            "seconds": total}
 
-    t_warm = time.perf_counter()
-    for _ in range(args.warmup):
-        step(n_seq, heads)
-    # Re-size from the warm-up's wall time per step (it includes the per-call costs a small probe
-    # underestimates on hosts with many threads), so the timed steps fit the rest of the budget.
-    per_call = (time.perf_counter() - t_warm) / args.warmup
-    if per_call * args.steps > budget_s and n_seq > 1:
-        n_seq = int(max(1, n_seq * budget_s / (per_call * args.steps)))
-        step(n_seq, heads)  # the new size's pool, untimed
-    bytes_read, secs = 0.0, 0.0
-    for _ in range(args.steps):
-        b, t = step(n_seq, heads)
-        bytes_read += b
-        secs += t
-    value = bytes_read / secs / 1e9
-    cb = {"value": value, "unit": "GB/s", "cores": host_threads(), "kind": "port",
-          "sample": f"{args.steps} timed steps x {n_seq} sequences x {heads} KV heads of config 2 (ctx U[{CTX_LO},{CTX_HI}]), "
-                    f"bf16 torch-CPU restatement of the reference's gather + GQA expand + matmul/softmax, "
-                    f"{secs:.1f} s of CPU work"}
+
+def run_reference(args, spec: dict) -> None:
+    """Reference arm: the CPU restatement of the reference's decode path on the host cores (rank 0).
+
+    Each step is one call over the first n sequences of the same seeded workload, all KV heads of
+    one layer, n sized from a probe so that warm-up + steps take about two minutes."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    seqs = seeded_sequences(spec, 1)
+    budget_s = 120.0
+    cb = cpu_decode_leg(spec, seqs, seconds=budget_s * args.steps / (args.steps + args.warmup), steps=args.steps,
+                        warmup=args.warmup)
     line = {
-        "metric": "paged decode KV-read GB/s", "value": value, "unit": "GB/s", "impl": "reference",
+        "metric": METRIC, "value": cb["value"], "unit": "GB/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config2_decode_op_cpu_sample", "seq_len": f"U[{CTX_LO},{CTX_HI}]"},
-        "cpu_baseline": cb, "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "scaling": "weak" if spec["weak"] else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": spec["name"], "global_batch": seqs["b"],
+                   "seq_len": f"U[{spec['ctx'][0]},{spec['ctx'][1]}]", "heads": f"{spec['hq']}q/{spec['hkv']}kv",
+                   "head_dim": D, "block_size": BS, "sample": cb["sample"]},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_c4(args) -> None:
-    """Config 4: chunked-prefill mixed step at the Qwen3-0.6B shape (one GPU).
+# ------------------------------------------------------------------------------------------------
+# parity of the timed path against a float32 torch reference on the device
+# ------------------------------------------------------------------------------------------------
+def decode_reference_rows(q, kp, vp, tables: np.ndarray, ctx: np.ndarray, rows, scale: float) -> torch.Tensor:
+    """float32 attention of the given sequences over their pages: [len(rows), Hq_local * D]."""
+    h = kp.shape[2]
+    g = q.shape[1] // h
+    outs = []
+    for r in rows:
+        n = int(ctx[r])
+        pages = torch.from_numpy(tables[r, : -(-n // BS)]).to(kp.device)
+        k = kp[pages].reshape(-1, h, D)[:n].float()
+        v = vp[pages].reshape(-1, h, D)[:n].float()
+        qr = q[r].float().view(h, g, D)
+        p = torch.softmax(torch.einsum("hgd,nhd->hgn", qr, k) * scale, dim=-1)
+        outs.append(torch.einsum("hgn,nhd->hgd", p, v).reshape(-1))
+    return torch.stack(outs)
 
-    16 prompts with lengths U[4096, 16384] are each at a seeded chunk index k (start = 128 k, chunk
-    = min(128, L - start), the cap token_budget 2048 // 16 candidates gives); 64 decode sequences
-    have contexts U[512, 8192].  Per layer the reference alternates a prefill step and a decode
-    step; here one "mixed step" = one chunked-prefill attention launch + one decode launch, and
-    each is also timed alone.  Prefill FLOPs are the causal algorithmic count
-    4 * chunk * (start + (chunk + 1) / 2) * Hq * D per row."""
-    from mini_infra_b200 import ops
 
-    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(device)
+def parity_rows(ctx: np.ndarray, k: int = 6) -> list[int]:
+    rng = np.random.RandomState(SEED + 9)
+    rows = {int(np.argmax(ctx)), int(np.argmin(ctx))}
+    while len(rows) < min(k, len(ctx)):
+        rows.add(int(rng.randint(len(ctx))))
+    return sorted(rows)
+
+
+# ------------------------------------------------------------------------------------------------
+# config 4 shapes: chunked-prefill launch and KV scatter sub-records (one GPU)
+# ------------------------------------------------------------------------------------------------
+def c4_inputs(device) -> dict:
+    """BASELINE config 4 at the Qwen3-0.6B shape: 16 prompts of U[4096, 16384] tokens, each at a
+    seeded chunk index k (start = 128 k, chunk = min(128, L - start), the cap token_budget 2048 // 16
+    candidates gives), and 64 decode sequences with contexts U[512, 8192]; scattered block tables."""
     rng = np.random.RandomState(SEED + 4)
     hq, hkv = 16, 8
     lens_total = rng.randint(4096, 16385, size=16)
@@ -315,48 +349,413 @@ def run_c4(args) -> None:
         dec_tab[i, : need[16 + i]] = tabs[16 + i]
     g = torch.Generator(device=device).manual_seed(SEED)
     rnd = lambda *sh: torch.randn(sh, generator=g, device=device, dtype=torch.bfloat16)  # noqa: E731
-    kp, vp = rnd(num_blocks, BS, hkv, D), rnd(num_blocks, BS, hkv, D)
     length = int(chunks.max())
-    q, kc, vc = rnd(16, length, hq, D), rnd(16, length, hkv, D), rnd(16, length, hkv, D)
-    qd = rnd(64, hq, D)
     t = lambda a: torch.from_numpy(a).to(device)  # noqa: E731
-    pre_tab_d, starts_d, chunks_d, dec_tab_d, dec_ctx_d = t(pre_tab), t(starts), t(chunks), t(dec_tab), t(dec_ctx)
+    return dict(hq=hq, hkv=hkv, starts=starts, chunks=chunks, dec_ctx=dec_ctx, pre_tab=pre_tab, dec_tab=dec_tab,
+                num_blocks=num_blocks, length=length, kp=rnd(num_blocks, BS, hkv, D), vp=rnd(num_blocks, BS, hkv, D),
+                q=rnd(16, length, hq, D), kc=rnd(16, length, hkv, D), vc=rnd(16, length, hkv, D), qd=rnd(64, hq, D),
+                pre_tab_d=t(pre_tab), starts_d=t(starts), chunks_d=t(chunks), dec_tab_d=t(dec_tab),
+                dec_ctx_d=t(dec_ctx))
+
+
+def prefill_reference_row(x: dict, i: int, scale: float) -> torch.Tensor:
+    """float32 chunked-prefill attention of row i: [chunk, Hq * D] (the row's valid positions)."""
+    s, c, length, hkv, hq = int(x["starts"][i]), int(x["chunks"][i]), x["length"], x["hkv"], x["hq"]
+    g = hq // hkv
+    pages = torch.from_numpy(x["pre_tab"][i, : -(-s // BS)]).to(x["kp"].device)
+    kh = x["kp"][pages].reshape(-1, hkv, D)[:s].float()
+    vh = x["vp"][pages].reshape(-1, hkv, D)[:s].float()
+    k = torch.cat([kh, x["kc"][i, length - c :].float()])  # [s + c, hkv, D]
+    v = torch.cat([vh, x["vc"][i, length - c :].float()])
+    q = x["q"][i, length - c :].float().view(c, hkv, g, D)
+    scores = torch.einsum("jhgd,thd->hgjt", q, k) * scale
+    allowed = torch.arange(s + c, device=k.device)[None, :] <= (s + torch.arange(c, device=k.device))[:, None]
+    scores = scores.masked_fill(~allowed, float("-inf"))
+    out = torch.einsum("hgjt,thd->jhgd", torch.softmax(scores, dim=-1), v)
+    return out.reshape(c, hq * D)
+
+
+def prefill_record(device, iters: int) -> dict:
+    """One chunked-prefill attention launch at config 4 (tcgen05 kernel + split combine): device
+    time, TFLOP/s of the causal algorithmic FLOPs 4 * chunk * (start + (chunk + 1) / 2) * Hq * D per
+    row, its fraction of the measured bf16 peak, and a parity check of two rows."""
+    from mini_infra_b200 import ops
+
+    x = c4_inputs(device)
+    out = torch.empty((16, x["length"], x["hq"] * D), dtype=torch.bfloat16, device=device)
+    scale = D**-0.5
+
+    def launch():
+        ops.paged_prefill(x["q"], x["kc"], x["vc"], x["kp"], x["vp"], x["pre_tab_d"], x["starts_d"], x["chunks_d"],
+                          scale, out=out)
+
+    for _ in range(5):
+        launch()
+    ms = event_ms(launch, iters, device)
+    starts, chunks = x["starts"], x["chunks"]
+    flops = float(np.sum(4.0 * chunks * (starts + (chunks + 1) / 2.0))) * x["hq"] * D
+    tflops = flops / (ms * 1e-3) / 1e12
+    pk = peaks()
+    err = 0.0
+    for i in (int(np.argmax(starts)), int(np.argmin(chunks))):
+        c = int(chunks[i])
+        want = prefill_reference_row(x, i, scale)
+        err = max(err, float((out[i, x["length"] - c :].float() - want).abs().max()))
+    status = ops.read_status(device)
+    return {"ms": ms, "tflops": tflops, "frac": tflops / pk["bf16_tflops"], "peak_tflops": pk["bf16_tflops"],
+            "peak_source": pk["source"], "algorithmic_gflop": flops / 1e9,
+            "kv_gb": float(np.sum(starts + chunks)) * 2 * x["hkv"] * D * 2 / 1e9,
+            "kernel": "prefill_tc_kernel + prefill_combine_kernel", "iters": iters,
+            "traffic": NCU_PREFILL_C4["traffic"], "traffic_source": NCU_PREFILL_C4["source"],
+            "parity": {"max_abs": err, "tol": 2e-2, "ok": bool(err <= 2e-2 and status == 0), "rows": 2,
+                       "status_bits": status, "reference": "float32 torch on the device"}}
+
+
+def scatter_record(device, iters: int) -> dict:
+    """KV scatter at config 4's chunk size (16 rows x 128 tokens, 8 KV heads, D 128, bf16): the
+    reference's write_prefill (mi_kv_scatter with host-built slots) and store_prefill with the slots
+    computed on the device (mi_kv_store_chunks).  16 source buffers and 16 disjoint destination block
+    sets rotate, so each launch reads and writes lines outside L2.  Bytes per launch = K+V read +
+    written + the index arrays."""
+    from mini_infra_b200 import ops
+
+    rng = np.random.RandomState(SEED + 6)
+    rows, chunk, hkv, rot = 16, 128, 8, 16
+    blocks_per_row = chunk // BS
+    num_blocks = 1 + rows * blocks_per_row * rot * 2
+    g = torch.Generator(device=device).manual_seed(SEED + 6)
+    kp = torch.zeros((num_blocks, BS, hkv, D), dtype=torch.bfloat16, device=device)
+    vp = torch.zeros_like(kp)
+    # sources as the model hands them over: [B, L, H, D] buffers seen as [B, H, L, D]
+    srcs = [(torch.randn((rows, chunk, hkv, D), generator=g, device=device, dtype=torch.bfloat16).transpose(1, 2),
+             torch.randn((rows, chunk, hkv, D), generator=g, device=device, dtype=torch.bfloat16).transpose(1, 2))
+            for _ in range(rot)]
+    perm = 1 + rng.permutation(num_blocks - 1)
+    tables, slot_sets = [], []
+    tok_rows = np.repeat(np.arange(rows), chunk)
+    tok_pos = np.tile(np.arange(chunk), rows)
+    for r in range(rot):
+        tab = perm[r * rows * blocks_per_row : (r + 1) * rows * blocks_per_row].reshape(rows, blocks_per_row)
+        tables.append(torch.from_numpy(np.ascontiguousarray(tab)).to(device))
+        slot_sets.append(torch.from_numpy(tab[tok_rows, tok_pos // BS] * BS + tok_pos % BS).to(device))
+    rows_d = torch.from_numpy(tok_rows.astype(np.int64)).to(device)
+    pos_d = torch.from_numpy(tok_pos.astype(np.int64)).to(device)
+    lens_d = torch.full((rows,), chunk, dtype=torch.long, device=device)
+    starts_d = torch.zeros((rows,), dtype=torch.long, device=device)
+    state = {"i": 0}
+
+    def scatter():
+        i = state["i"] = (state["i"] + 1) % rot
+        ops.kv_scatter(srcs[i][0], srcs[i][1], rows_d, pos_d, slot_sets[i], kp, vp)
+
+    def store():
+        i = state["i"] = (state["i"] + 1) % rot
+        ops.kv_store_chunks(srcs[i][0], srcs[i][1], lens_d, starts_d, tables[i], kp, vp)
+
+    tokens = rows * chunk
+    kv = tokens * 2 * hkv * D * 2
+    pk = peaks()
+    res = {"tokens": tokens, "iters": iters, "kernels": "kv_scatter_kernel, kv_store_chunks_kernel",
+           "l2": "16 rotating source buffers and destination block sets (128 MiB of sources)"}
+    for name, fn, idx_bytes in (("write_prefill", scatter, tokens * 8 * 3),
+                                ("store_prefill", store, rows * 8 * (2 + blocks_per_row))):
+        for _ in range(rot):
+            fn()
+        ms = event_ms(fn, iters, device)
+        nbytes = 2 * kv + idx_bytes
+        res[name] = {"ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                     "bytes_per_launch": nbytes}
+    # bit-exact check of the last launch's destination rows against its source
+    i = state["i"]
+    want = srcs[i][0].transpose(1, 2).reshape(tokens, hkv, D)
+    got = kp.view(-1, hkv, D)[slot_sets[i]]
+    res["bit_exact"] = bool(torch.equal(got, want))
+    res["peak_gbs"] = pk["hbm_gbs"]
+    res["peak_source"] = pk["source"]
+    return res
+
+
+def cpu_scatter_leg(seconds: float = 5.0) -> dict:
+    """The reference's write_prefill (advanced-index gather + index_copy_ of K and V) on host cores
+    at the scatter sub-record's size."""
+    from oracle import paged_oracle as po
+
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    rows, chunk, hkv = 16, 128, 8
+    num_blocks = 1 + rows * chunk // BS * 4
+    gen = torch.Generator().manual_seed(SEED + 7)
+    key = torch.randn((rows, hkv, chunk, D), generator=gen).to(torch.bfloat16)
+    value = torch.randn((rows, hkv, chunk, D), generator=gen).to(torch.bfloat16)
+    kp = torch.zeros((num_blocks, BS, hkv, D), dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    rows_t = torch.arange(rows).repeat_interleave(chunk)
+    pos_t = torch.arange(chunk).repeat(rows)
+    slots = torch.from_numpy(1 * BS + np.random.RandomState(SEED + 7).permutation((num_blocks - 1) * BS)[: rows * chunk])
+    po.torch_write_prefill(kp, vp, key, value, rows_t, pos_t, slots)
+    total, calls = 0.0, 0
+    while total < seconds or calls == 0:
+        t0 = time.perf_counter()
+        po.torch_write_prefill(kp, vp, key, value, rows_t, pos_t, slots)
+        total += time.perf_counter() - t0
+        calls += 1
+    nbytes = 2 * rows * chunk * 2 * hkv * D * 2 + rows * chunk * 8 * 3
+    return {"value": nbytes * calls / total / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{calls} calls of the torch-CPU restatement of write_prefill (16 x 128 tokens, 8 KV heads, bf16)"}
+
+
+# ------------------------------------------------------------------------------------------------
+# the decode sweep (configs 5 and 2)
+# ------------------------------------------------------------------------------------------------
+def run_decode(args, spec: dict) -> None:
+    from mini_infra_b200 import ops
+    from mini_infra_b200.model.qwen3 import HeadPartition, gather_heads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=device)
+        group = dist.group.WORLD
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if spec["hkv"] % world:
+        raise SystemExit(f"{spec['hkv']} KV heads cannot be split over {world} ranks")
+    part = HeadPartition(rank, world, group)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, steps) -> float:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    # sub-records at config 4's shapes first, in their own memory, freed before the sweep's pools
+    sub_prefill = sub_scatter = None
+    if not args.no_subrecords:
+        sub_prefill = prefill_record(device, iters=200)
+        sub_scatter = scatter_record(device, iters=500)
+        torch.cuda.empty_cache()
+    barrier()
+
+    seqs = seeded_sequences(spec, world)
+    x = device_inputs(spec, seqs, world, rank, device)
+    b, hq_loc, h_loc = seqs["b"], x["hq_loc"], x["h_loc"]
+    tables = torch.from_numpy(seqs["tables"]).to(device)
+    ctx = torch.from_numpy(seqs["ctx"]).to(device)
+    slots = torch.from_numpy(seqs["slots"]).to(device)
+    scale = D**-0.5
+    out = torch.empty((b, hq_loc * D), dtype=torch.bfloat16, device=device)
+    pools = x["pools"]
+    ws = ops.workspace(device, ops.decode_workspace_bytes(b, hq_loc, pools[0][0], tables.shape[1]))
+    layers = spec["layers"]
+    holder = {}
+
+    def attention(layer: int):
+        kp, vp = pools[layer % len(pools)]
+        ops.paged_decode(x["q"], kp, vp, tables, ctx, scale, key_new=x["kn"], value_new=x["vn"], slot_mapping=slots,
+                         out=out, ws=ws)
+
+    def step():
+        for layer in range(layers):
+            attention(layer)
+            holder["gathered"] = gather_heads(out, part)
+
+    for _ in range(args.warmup):
+        step()
+    with ClockSampler(local) as clocks:
+        ms = timed(step, args.steps)
+        # per-layer legs, each alone: the attention (append + split-K + combine) and the exchange
+        state = {"l": 0}
+
+        def attn_leg():
+            state["l"] += 1
+            attention(state["l"])
+
+        n_leg = max(min(args.steps * layers, 1000), 10)
+        attn_ms = timed(attn_leg, n_leg)
+        exch_ms = timed(lambda: gather_heads(out, part), n_leg) if world > 1 else 0.0
+
+        # roofline of the attention launch alone (split-K kernel + combine, no append)
+        def decode_only():
+            state["l"] += 1
+            kp, vp = pools[state["l"] % len(pools)]
+            ops.paged_decode(x["q"], kp, vp, tables, ctx, scale, out=out, ws=ws)
+
+        ms_launch = timed(decode_only, n_leg)
+
+        # end to end through the public op: pinned host inputs -> device -> op -> pinned host output
+        h_q = x["q"].cpu().pin_memory()
+        h_kn, h_vn = x["kn"].cpu().pin_memory(), x["vn"].cpu().pin_memory()
+        meta = torch.cat([slots.cpu(), ctx.cpu(), tables.cpu().reshape(-1)]).pin_memory()
+        gathered_shape = holder["gathered"].shape
+        h_out = torch.empty(gathered_shape, dtype=out.dtype).pin_memory()
+        d_q, d_kn, d_vn = torch.empty_like(x["q"]), torch.empty_like(x["kn"]), torch.empty_like(x["vn"])
+        d_meta = torch.empty(meta.shape, dtype=torch.long, device=device)
+
+        def e2e_step():
+            d_meta.copy_(meta, non_blocking=True)
+            sl, cx, tb = d_meta[:b], d_meta[b : 2 * b], d_meta[2 * b :].view(b, -1)
+            for layer in range(layers):
+                kp, vp = pools[layer % len(pools)]
+                d_q.copy_(h_q, non_blocking=True)
+                d_kn.copy_(h_kn, non_blocking=True)
+                d_vn.copy_(h_vn, non_blocking=True)
+                ops.paged_decode(d_q, kp, vp, tb, cx, scale, key_new=d_kn, value_new=d_vn, slot_mapping=sl, out=out,
+                                 ws=ws)
+                h_out.copy_(gather_heads(out, part), non_blocking=True)
+
+        e2e_step()
+        ms_e2e = timed(e2e_step, max(min(args.steps, 50), 3))
+    kv_token_bytes = 2 * spec["hkv"] * D * 2  # K+V of every KV head, bf16
+    kv_bytes_global = float(seqs["ctx"].sum()) * kv_token_bytes * layers  # all ranks together read every head once
+    value = kv_bytes_global / (ms * 1e-3) / 1e9
+    h2d = meta.numel() * 8 + layers * (h_q.numel() + h_kn.numel() + h_vn.numel()) * 2
+    d2h = layers * h_out.numel() * 2
+    e2e_value = kv_bytes_global / (ms_e2e * 1e-3) / 1e9
+    alg_bytes = (float(seqs["ctx"].sum()) * 2 * h_loc * D * 2  # K+V of this rank's heads
+                 + b * hq_loc * D * 2 * 2 + tables.numel() * 8 + b * 8)  # q + out + tables + ctx
+    achieved = alg_bytes / (ms_launch * 1e-3) / 1e9
+    pk = peaks()
+
+    # parity: one more layer call on pool 0 (append included), then rows against float32 torch
+    ops.read_status(device)
+    attention(0)
+    gathered = gather_heads(out, part)
+    rows = parity_rows(seqs["ctx"])
+    ref = decode_reference_rows(x["q"], pools[0][0], pools[0][1], seqs["tables"], seqs["ctx"], rows, scale)
+    if world > 1:
+        all_ref = torch.empty((world * len(rows), ref.shape[1]), dtype=ref.dtype, device=device)
+        torch.distributed.all_gather_into_tensor(all_ref, ref.contiguous())
+        ref = all_ref.view(world, len(rows), -1).transpose(0, 1).reshape(len(rows), -1)
+    err = float((gathered[rows].float() - ref).abs().max())
+    status = ops.read_status(device)
+    err = max_over_ranks(err)
+    status = int(max_over_ranks(float(status)))
+    parity = {"max_abs": err, "tol": 2e-2, "ok": bool(err <= 2e-2 and status == 0), "rows": rows,
+              "ctx": [int(seqs["ctx"][r]) for r in rows], "status_bits": status,
+              "reference": "float32 torch on the device from the same pools"
+                           + (", references all-gathered across ranks (checks the exchange)" if world > 1 else "")}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_decode_leg(spec, seqs, seconds=12.0)
+        cpu.pop("seconds", None)
+        if sub_scatter is not None:
+            sub_scatter["cpu_baseline"] = cpu_scatter_leg()
+    if rank == 0:
+        limiter = "attention (HBM-bound decode)" if attn_ms >= 4 * exch_ms else "exchange (all-gather)"
+        traffic = alg_bytes * NCU_DECODE["traffic"] / NCU_DECODE["algorithmic"]
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak" if spec["weak"] else "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) pools, queries and new K/V; seeded contexts and block tables)",
+            "config": {
+                "workload": spec["name"],
+                "global_batch": b, "seq_len": f"U[{spec['ctx'][0]},{spec['ctx'][1]}]",
+                "heads": f"{spec['hq']}q/{spec['hkv']}kv", "kv_heads_per_gpu": h_loc, "head_dim": D,
+                "block_size": BS, "layer_calls_per_step": layers, "resident_layer_pools": spec["resident"],
+                "pool_blocks_per_layer": seqs["num_blocks"],
+                "pool_gb_per_rank": round(2 * spec["resident"] * seqs["num_blocks"] * BS * h_loc * D * 2 / 1e9, 2),
+                "kv_gb_per_step": round(kv_bytes_global / 1e9, 2),
+                "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU",
+                "l2": "inputs larger than L2 (every layer call reads >= 2 GB of pool per rank)",
+                "step": "per layer call: append + paged decode (split-K + combine)"
+                        + (" + all-gather of the per-head outputs" if world > 1 else ""),
+            },
+            "per_layer_ms": {"step": ms / layers, "attention": attn_ms, "exchange": exch_ms, "limiter": limiter},
+            "roofline": {
+                "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
+                "traffic": traffic, "traffic_source": NCU_DECODE["source"],
+                "algorithmic_bytes_per_launch": alg_bytes,
+                "kernel": "decode_split_kernel + decode_combine_kernel", "ms_per_launch": ms_launch,
+            },
+            "parity": parity,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "gpu_launches": 3 * layers * args.steps,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "prefill": sub_prefill,
+            "scatter": sub_scatter,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------------------------
+# config 4 line: chunked-prefill + decode mixed step
+# ------------------------------------------------------------------------------------------------
+def run_c4(args) -> None:
+    """Config 4: per layer the reference alternates a prefill step and a decode step; here one
+    "mixed step" = one chunked-prefill attention launch + one decode launch, each also timed alone."""
+    from mini_infra_b200 import ops
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    x = c4_inputs(device)
+    hq, hkv, length = x["hq"], x["hkv"], x["length"]
     out_p = torch.empty((16, length, hq * D), dtype=torch.bfloat16, device=device)
     out_d = torch.empty((64, hq * D), dtype=torch.bfloat16, device=device)
-    ws = ops.workspace(device, ops.decode_workspace_bytes(64, hq, kp, dec_tab.shape[1]))
+    ws = ops.workspace(device, ops.decode_workspace_bytes(64, hq, x["kp"], x["dec_tab"].shape[1]))
 
     def prefill():
-        ops.paged_prefill(q, kc, vc, kp, vp, pre_tab_d, starts_d, chunks_d, D**-0.5, out=out_p)
+        ops.paged_prefill(x["q"], x["kc"], x["vc"], x["kp"], x["vp"], x["pre_tab_d"], x["starts_d"], x["chunks_d"],
+                          D**-0.5, out=out_p)
 
     def decode():
-        ops.paged_decode(qd, kp, vp, dec_tab_d, dec_ctx_d, D**-0.5, out=out_d, ws=ws)
+        ops.paged_decode(x["qd"], x["kp"], x["vp"], x["dec_tab_d"], x["dec_ctx_d"], D**-0.5, out=out_d, ws=ws)
 
     def mixed():
         prefill()
         decode()
 
-    def timed(fn, n):
-        torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(n):
-            fn()
-        e1.record()
-        torch.cuda.synchronize(device)
-        return e0.elapsed_time(e1) / n
-
     for _ in range(args.warmup):
         mixed()
     with ClockSampler(device.index or 0) as clocks:
-        ms_mixed = timed(mixed, args.steps)
-    ms_pre = timed(prefill, args.steps)
-    ms_dec = timed(decode, args.steps)
+        ms_mixed = event_ms(mixed, args.steps, device)
+        ms_pre = event_ms(prefill, args.steps, device)
+        ms_dec = event_ms(decode, args.steps, device)
+    starts, chunks, dec_ctx = x["starts"], x["chunks"], x["dec_ctx"]
     flops = float(np.sum(4.0 * chunks * (starts + (chunks + 1) / 2.0))) * hq * D
     pre_bytes = float(np.sum(starts + chunks)) * 2 * hkv * D * 2 + 2 * 16 * length * hq * D * 2
     dec_bytes = float(dec_ctx.sum()) * 2 * hkv * D * 2
     tflops = flops / (ms_pre * 1e-3) / 1e12
-    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-    peak_t = float(peaks.get("bf16_tflops", 1590.0))
+    pk = peaks()
     line = {
         "metric": "chunked-prefill attention TFLOP/s", "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_mixed, "higher_is_better": True,
@@ -368,16 +767,18 @@ def run_c4(args) -> None:
         "prefill": {"ms": ms_pre, "tflops": tflops, "gbs": pre_bytes / (ms_pre * 1e-3) / 1e9,
                     "algorithmic_gflop": flops / 1e9, "kernel": "prefill_tc_kernel"},
         "decode": {"ms": ms_dec, "gbs": dec_bytes / (ms_dec * 1e-3) / 1e9},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak_t, "unit": "TFLOP/s",
-                     "frac": tflops / peak_t, "traffic": NCU_TRAFFIC_C4,
-                     "traffic_unit": "bytes per launch of prefill_tc_kernel (ncu dram read+write)",
-                     "peak_source": "measured" if peaks else "fallback"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / pk["bf16_tflops"], "traffic": NCU_PREFILL_C4["traffic"],
+                     "traffic_source": NCU_PREFILL_C4["source"], "peak_source": pk["source"]},
         "gpu_launches": args.steps * 2 + args.steps * 2,
         "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------
+# config 3 line: the whole engine
+# ------------------------------------------------------------------------------------------------
 def c3_requests(num: int, seed: int, max_new: int, rate_per_s: float = 32.0, lo: int = 32, hi: int = 2048):
     """Config 3 workload: Poisson arrivals (rate 32/s on the logical clock), prompt lengths
     log-uniform in [32, 2048], token ids uniform in [1000, 100000), greedy max_new tokens."""
@@ -414,7 +815,7 @@ def run_c3(args) -> None:
     with N ranks the model is KV-head partitioned (strong scaling: same requests)."""
     import datetime
 
-    from mini_infra_b200.core import BatchingMethod, PagedCacheConfig, SchedulerConfig
+    from mini_infra_b200.core import BatchingMethod, ChunkedPrefillConfig, PagedCacheConfig, SchedulerConfig
     from mini_infra_b200.engine import EngineConfig, run_scheduler
     from mini_infra_b200.model import QWEN3_0_6B, HeadPartition, Qwen3Config, build_model
 
@@ -432,8 +833,6 @@ def run_c3(args) -> None:
     cfg = Qwen3Config(**QWEN3_0_6B, torch_dtype="bfloat16")
     model = build_model(cfg, seed=0, device=device, dtype=torch.bfloat16, partition=HeadPartition(rank, world, group),
                         generator_device="cuda")
-    from mini_infra_b200.core import ChunkedPrefillConfig
-
     policy = {"prefill-first": None, "chunked": ChunkedPrefillConfig(C3_TOKEN_BUDGET),
               "mixed": ChunkedPrefillConfig(C3_TOKEN_BUDGET, mixed=True)}[args.policy]
     engine = EngineConfig(PagedCacheConfig(block_size=16), BatchingMethod.CONTINUOUS,
@@ -464,7 +863,9 @@ def run_c3(args) -> None:
             "latency_ms": c3_latency(results),
             "engine": {"decode_tokens": dec_tokens, "decode_ms": dec_ms, "throughput_tok_s": out_tokens * 1000.0 / busy_ms,
                        "busy_ms": busy_ms, "prefill_steps": sum(r.schedule_metrics.num_prefill_steps for r in results),
-                       "decode_steps": sum(r.schedule_metrics.num_decode_steps for r in results)},
+                       "decode_steps": sum(r.schedule_metrics.num_decode_steps for r in results),
+                       "mean_decode_batch": dec_tokens / max(1, sum(r.schedule_metrics.num_decode_steps
+                                                                   for r in results))},
             "e2e": {"value": out_tokens * 1000.0 / sum(r.e2e_wall_ms for r in results),
                     "unit": "tok/s (all generated tokens over the engine's wall clock)",
                     "h2d_bytes_per_step": sum(r.extra["h2d_bytes"] for r in results) / steps,
@@ -481,11 +882,14 @@ def run_c3(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 3000 for c2, 20 for c5)")
-    ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 20 for c2, 3 for c5)")
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 20 for c5, 3000 for c2)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 3 for c5, 20 for c2)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c3", "c4"], default="c2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c3", "c4"], default="c5")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch (small cases for ncu captures; not a bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true", help="skip the prefill / scatter sub-records")
     ap.add_argument("--policy", choices=["prefill-first", "chunked", "mixed"], default="prefill-first",
                     help="config 3 batching policy (chunked / mixed: token budget %d)" % C3_TOKEN_BUDGET)
     args = ap.parse_args()
@@ -499,7 +903,10 @@ def main() -> None:
         args.warmup = args.warmup or 5
         run_c4(args)
         return
-    spec = WORKLOADS[args.workload]
+    spec = dict(WORKLOADS[args.workload])
+    if args.batch is not None:
+        spec["batch"] = args.batch
+        spec["name"] += f"_batch{args.batch}"
     if args.steps is None:
         args.steps = 3000 if spec["layers"] == 1 else 20
     if args.warmup is None:
@@ -507,166 +914,9 @@ def main() -> None:
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
-        run_reference(args)
+        run_reference(args, spec)
         return
-
-    from mini_infra_b200 import ops
-    from mini_infra_b200.model.qwen3 import HeadPartition, gather_heads
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    group = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-        group = dist.group.WORLD
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    if spec["hkv"] % world:
-        raise SystemExit(f"{spec['hkv']} KV heads cannot be split over {world} ranks")
-    part = HeadPartition(rank, world, group)
-
-    w = workload(spec, world, rank, device)
-    b, hq_loc, h_loc = w["b"], w["hq_loc"], w["h_loc"]
-    tables = torch.from_numpy(w["tables"]).to(device)
-    ctx = torch.from_numpy(w["ctx"]).to(device)
-    slots = torch.from_numpy(w["slots"]).to(device)
-    scale = D**-0.5
-    out = torch.empty((b, hq_loc * D), dtype=torch.bfloat16, device=device)
-    pools = w["pools"]
-    ws = ops.workspace(device, ops.decode_workspace_bytes(b, hq_loc, pools[0][0], tables.shape[1]))
-    layers = spec["layers"]
-
-    def step():
-        for layer in range(layers):
-            kp, vp = pools[layer % len(pools)]
-            ops.paged_decode(w["q"], kp, vp, tables, ctx, scale, key_new=w["kn"], value_new=w["vn"],
-                             slot_mapping=slots, out=out, ws=ws)
-            gather_heads(out, part)
-
-    def attn_only():
-        ops.paged_decode(w["q"], pools[0][0], pools[0][1], tables, ctx, scale, out=out, ws=ws)
-
-    def barrier():
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize(device)
-
-    def timed(fn, steps) -> float:
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            fn()
-        e1.record()
-        barrier()
-        ms = e0.elapsed_time(e1) / steps
-        if world > 1:
-            t = torch.tensor([ms], device=device, dtype=torch.float64)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    for _ in range(args.warmup):
-        step()
-    with ClockSampler(local) as clocks:
-        ms = timed(step, args.steps)
-    kv_token_bytes = 2 * spec["hkv"] * D * 2  # K+V of every KV head, bf16
-    kv_bytes_global = float(w["ctx"].sum()) * kv_token_bytes * layers  # all ranks together read every head once
-    value = kv_bytes_global / (ms * 1e-3) / 1e9
-
-    # roofline of the attention launch alone (split-K kernel + combine): algorithmic bytes per launch
-    for _ in range(3):
-        attn_only()
-    n_attn = max(min(args.steps // 2, 1000), 10)
-    ms_attn = timed(attn_only, n_attn)
-    alg_bytes = (float(w["ctx"].sum()) * 2 * h_loc * D * 2  # K+V of this rank's heads
-                 + b * hq_loc * D * 2 * 2 + tables.numel() * 8 + b * 8)  # q + out + tables + ctx
-    achieved = alg_bytes / (ms_attn * 1e-3) / 1e9
-    peaks = measured_peaks()
-
-    # end to end through the public op: pinned host inputs -> device -> op -> pinned host output
-    h_q = w["q"].cpu().pin_memory()
-    h_kn, h_vn = w["kn"].cpu().pin_memory(), w["vn"].cpu().pin_memory()
-    meta = torch.cat([slots.cpu(), ctx.cpu(), tables.cpu().reshape(-1)]).pin_memory()
-    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    d_q, d_kn, d_vn = torch.empty_like(w["q"]), torch.empty_like(w["kn"]), torch.empty_like(w["vn"])
-    d_meta = torch.empty(meta.shape, dtype=torch.long, device=device)
-
-    def e2e_step():
-        d_meta.copy_(meta, non_blocking=True)
-        sl, cx, tb = d_meta[:b], d_meta[b : 2 * b], d_meta[2 * b :].view(b, -1)
-        for layer in range(layers):
-            kp, vp = pools[layer % len(pools)]
-            d_q.copy_(h_q, non_blocking=True)
-            d_kn.copy_(h_kn, non_blocking=True)
-            d_vn.copy_(h_vn, non_blocking=True)
-            ops.paged_decode(d_q, kp, vp, tb, cx, scale, key_new=d_kn, value_new=d_vn, slot_mapping=sl, out=out,
-                             ws=ws)
-            gather_heads(out, part)
-            h_out.copy_(out, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    ms_e2e = timed(e2e_step, max(min(args.steps // 2, 1000), 5))
-    h2d = meta.numel() * 8 + layers * (h_q.numel() + h_kn.numel() + h_vn.numel()) * 2
-    d2h = layers * h_out.numel() * 2
-    e2e_value = kv_bytes_global / (ms_e2e * 1e-3) / 1e9
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_decode_sample()
-    if rank == 0:
-        line = {
-            "metric": "paged decode KV-read GB/s",
-            "value": value,
-            "unit": "GB/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms,
-            "higher_is_better": True,
-            "scaling": "weak" if spec["weak"] else "strong",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic",
-            "config": {
-                "workload": spec["name"],
-                "global_batch": b, "seq_len": f"U[{spec['ctx'][0]},{spec['ctx'][1]}]",
-                "heads": f"{spec['hq']}q/{spec['hkv']}kv", "head_dim": D, "block_size": BS,
-                "layer_calls_per_step": layers, "resident_layer_pools": spec["resident"],
-                "pool_blocks_per_layer": w["num_blocks"],
-                "pool_gb_per_rank": round(2 * spec["resident"] * w["num_blocks"] * BS * h_loc * D * 2 / 1e9, 2),
-                "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU",
-                "l2": "inputs larger than L2 (every layer call reads >= 2 GB of pool)",
-                "step": "per layer call: append + paged decode (split-K + combine)"
-                        + (" + NCCL all-gather" if world > 1 else ""),
-            },
-            "roofline": {
-                "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
-                "traffic": NCU_TRAFFIC_C2 if args.workload == "c2" and world == 1
-                else alg_bytes * NCU_TRAFFIC_C2 / NCU_ALGORITHMIC_C2,
-                "traffic_unit": "bytes per launch (ncu dram read+write; scaled from config 2 by tokens "
-                                "unless workload c2 on one GPU)",
-                "kernel": "decode_split_kernel + decode_combine_kernel", "ms_per_launch": ms_attn,
-            },
-            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": ms_e2e},
-            "gpu_launches": 3 * layers * args.steps,
-            "clocks": clocks.summary(),
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    run_decode(args, spec)
 
 
 if __name__ == "__main__":

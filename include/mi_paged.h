@@ -121,15 +121,17 @@ int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, 
 /*
  * mi_paged_decode_static_scratch — mi_paged_decode for callers that cannot allocate device memory.
  * No counterpart in the reference: it exists for callers of this library that have no way to
- * provide the split-K workspace — code issuing the decode while a CUDA graph is being captured
- * (cudaMalloc is not capturable), hosts binding the C ABI without a device allocator of their own,
- * and loops that cannot afford cudaMalloc's implicit synchronisation.  Same arguments and results
- * as mi_paged_decode minus the workspace: the split-K partials go to a file-scope device array of
+ * provide the split-K workspace — hosts binding the C ABI without a device allocator of their own
+ * (a C, Go or JNI program has no caching allocator to take a workspace from) and loops that cannot
+ * afford cudaMalloc's implicit device synchronisation.  Same arguments and results as
+ * mi_paged_decode minus the workspace: the split-K partials go to a file-scope device array of
  * MI_STATIC_SCRATCH_BYTES that every GPU loading the library holds until the process exits.
  * Nothing is allocated.  A call whose partials would exceed the array is rejected with
  * MI_ERR_UNSUPPORTED (use mi_paged_decode then).  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress, with that device current): make it before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race and must be serialised.
+ * device address (cudaGetSymbolAddress, with that device current) and caches it: make that first
+ * call before any stream capture, and make no call after a cudaDeviceReset of that device (the
+ * cached address then names a released module).  All calls share the array and it keeps the last
+ * call's contents: calls that overlap on the GPU race and must be serialised by the caller.
  */
 #define MI_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
 int mi_paged_decode_static_scratch(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,

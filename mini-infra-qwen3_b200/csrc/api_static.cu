@@ -1,8 +1,7 @@
 // mi_paged_decode_static_scratch: the paged decode entry point for callers that cannot allocate
 // device memory on the call path.
 //
-// Who needs it: code that issues the decode while a CUDA graph is being captured (cudaMalloc is
-// not capturable), hosts that bind the C ABI without any device allocator of their own (a C, Go or
+// Who needs it: hosts that bind the C ABI without any device allocator of their own (a C, Go or
 // JNI caller has no caching allocator to hand a workspace from), and latency-critical loops that
 // cannot afford cudaMalloc's implicit device synchronisation.  The regular entry point
 // (mi_paged_decode) needs a caller-provided split-K workspace; this one uses a fixed scratch array
@@ -13,10 +12,12 @@
 // name to a kernel (in host code that name is only a stand-in for the device symbol); the device
 // address is looked up once per device with cudaGetSymbolAddress, with that device current, the
 // first time this entry point runs on it — so make the first call on each device before any
-// stream capture begins.  All calls share the array and it keeps the previous call's contents:
-// nothing in it needs to start at zero (each split partial the combine step reads is written by
-// the same call first), but calls that overlap on the GPU — two streams, or two host threads —
-// race on it and must be serialised by the caller.
+// stream capture begins.  The cached address outlives a cudaDeviceReset of that device, after which
+// it names a released module: this entry point must not be called on a device after resetting it.
+// All calls share the array and it keeps the previous call's contents: nothing in it needs to
+// start at zero (each split partial the combine step reads is written by the same call first), but
+// calls that overlap on the GPU — two streams, or two host threads — race on it and must be
+// serialised by the caller.
 #include <mutex>
 
 #include "common.cuh"

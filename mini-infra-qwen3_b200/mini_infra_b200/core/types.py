@@ -1,6 +1,6 @@
 """Control-plane configuration and result types (no torch).
 
-Mirrors the reference's ``core/types.py`` (``PagedCacheConfig`` :47-66 in the survey numbering,
+Mirrors the reference's ``core/types.py`` (``PagedCacheConfig`` at core/types.py:47-66,
 ``ChunkedPrefillConfig``, ``SchedulerConfig``, ``BatchingMethod``, the string parsers) so that
 configuration code written for the reference runs unchanged.  Only the kinds the paged path
 needs are accepted; ``dense-kv-cache`` parses (for config compatibility) but the engine here

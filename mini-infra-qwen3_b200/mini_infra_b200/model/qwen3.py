@@ -95,16 +95,9 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
-        """RMSNorm(x), or RMSNorm(x + residual) with the sum written back into `residual`."""
-        if x.is_cuda:
-            return ops.rmsnorm(x, self.weight, self.eps, residual)
-        if residual is not None:
-            residual.copy_(x + residual)
-            x = residual
-        dtype = x.dtype
-        xf = x.float()
-        normed = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + self.eps)
-        return self.weight * normed.to(dtype)
+        """RMSNorm(x), or RMSNorm(x + residual) with the sum written back into `residual` (CUDA
+        only, like every op of this package)."""
+        return ops.rmsnorm(x, self.weight, self.eps, residual)
 
 
 class RotaryEmbedding(nn.Module):
@@ -252,8 +245,6 @@ class Qwen3MLP(nn.Module):
         self.packed_gate_up: torch.Tensor | None = None  # set by pack_projections_
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if not x.is_cuda:
-            return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
         x2 = x.reshape(-1, x.shape[-1])
         gate, up = _packed_linear(x2, (self.gate_proj.weight, self.up_proj.weight), self.packed_gate_up)
         return self.down_proj(ops.silu_mul(gate, up)).view(*x.shape[:-1], -1)

@@ -37,6 +37,11 @@ def packed_length(bucket: int, width: int) -> int:
     return 4 * bucket + bucket * width
 
 
+def workspace_bytes_for(buckets: Sequence[int], num_q_heads: int, k_pool: torch.Tensor, width: int) -> int:
+    """Split-K workspace that covers a decode step of every bucket at this table width."""
+    return max(ops.decode_workspace_bytes(n, num_q_heads, k_pool, width) for n in buckets)
+
+
 @dataclass
 class _Graph:
     bucket: int
@@ -57,10 +62,13 @@ class DecodeGraphSet:
         self.buckets = tuple(sorted(buckets))
         self._graphs: dict[int, _Graph] = {}
         self._mempool = torch.cuda.graph_pool_handle()
-        # size the decode workspace for the largest bucket before any capture
+        # Size the decode workspace for every bucket before any capture.  The split planner gives
+        # small batches more splits per row, so the largest bucket's need is not assumed to cover
+        # the others; a workspace that grew between two captures would leave the earlier graphs on
+        # the old buffer (kept alive by ops.workspace, so still correct, but no longer shared).
         attn = model.model.layers[0].self_attn  # type: ignore[attr-defined]
-        ops.workspace(self.device, ops.decode_workspace_bytes(self.buckets[-1], attn.num_heads, self.kv_pools[0][0],
-                                                              self.width), slot="decode")
+        ops.workspace(self.device, workspace_bytes_for(self.buckets, attn.num_heads, self.kv_pools[0][0], self.width),
+                      slot="decode")
 
     def bucket_for(self, batch: int, width: int) -> int | None:
         """Smallest bucket holding `batch` rows, or None when the step must run eagerly."""

@@ -299,9 +299,19 @@ def torch_paged_decode(query, key_pool, value_pool, block_tables, context_lens, 
     return torch.matmul(probs, v).transpose(1, 2).contiguous().view(b, hq * d)
 
 
+def torch_write_prefill(key_pool, value_pool, key, value, token_rows, token_positions, slot_mapping) -> None:
+    """The reference's write_prefill as the same torch CPU op sequence (worker/paged_kv_cache.py:88-95):
+    per pool, ``pool.view(-1, H, D).index_copy_(0, slots, src[rows, :, positions, :])``.  key/value
+    [B, H_kv, L, D]; index tensors int64 [T].  Used as the timed CPU baseline of the scatter."""
+    n, bs, h, d = key_pool.shape
+    key_pool.view(n * bs, h, d).index_copy_(0, slot_mapping, key[token_rows, :, token_positions, :])
+    value_pool.view(n * bs, h, d).index_copy_(0, slot_mapping, value[token_rows, :, token_positions, :])
+
+
 __all__ = [
     "NULL_BLOCK_ID",
     "torch_paged_decode",
+    "torch_write_prefill",
     "append_decode",
     "as_float",
     "bf16_to_f32",

@@ -57,3 +57,18 @@ def test_decode_workspace_plan_is_host_only_and_sane():
     assert lib.mi_paged_decode_workspace_size(256, 16, 8, 128, 256, 16, nat.MI_F32) == 0
     bigger = lib.mi_paged_decode_workspace_size(512, 32, 8, 128, 2048, 16, nat.MI_BF16)
     assert bigger > small
+
+
+def test_decode_graph_workspace_covers_every_bucket():
+    """The split planner gives small batches more splits per row, so the workspace a set of decode
+    graphs pre-sizes is the maximum over its buckets (not assumed to be the largest bucket's need)."""
+    import torch
+
+    from mini_infra_b200 import ops
+    from mini_infra_b200.worker.decode_graphs import BUCKETS, workspace_bytes_for
+
+    for hq, hkv, width in ((16, 8, 32), (16, 8, 256), (32, 8, 2048), (4, 1, 2048)):
+        pool = torch.empty((8, 16, hkv, 128), dtype=torch.bfloat16, device="meta")
+        size = workspace_bytes_for(BUCKETS, hq, pool, width)
+        needs = [ops.decode_workspace_bytes(n, hq, pool, width) for n in BUCKETS]
+        assert size == max(needs) and all(size >= n for n in needs)
