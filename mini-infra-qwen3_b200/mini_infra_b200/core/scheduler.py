@@ -98,7 +98,7 @@ class RunningQueue:
 
     def __init__(self, capacity: int):
         if capacity < 1:
-            raise ValueError("capacity must be positive")
+            raise ValueError(f"capacity must be positive (必须大于 0), got {capacity}")
         self.capacity = capacity
         self._running: list[RequestState] = []
         self._free_slots = list(range(capacity))
@@ -138,7 +138,7 @@ class RunningQueue:
 
     def admit(self, states: Sequence[RequestState], clock_ms: float) -> list[RequestState]:
         if len(states) > len(self._free_slots):
-            raise ValueError(f"not enough batch slots: need {len(states)}, have {len(self._free_slots)}")
+            raise ValueError(f"not enough batch slots (可用 batch slot 不足): need {len(states)}, have {len(self._free_slots)}")
         for s in states:
             s.status = RequestStatus.RUNNING
             s.admitted_ms = clock_ms
@@ -303,7 +303,7 @@ class IterationScheduler:
         if self.kv_cache_manager is None:
             return
         if not self.kv_cache_manager.allocate_slots(state.request.request_idx, num_new_tokens):
-            raise RuntimeError("paged KV cache out of blocks (no preemption); increase num_blocks")
+            raise RuntimeError("paged KV cache out of blocks (物理块已耗尽; there is no preemption): increase num_blocks")
 
     def _reserved_blocks(self) -> int:
         assert self.kv_cache_manager is not None
