@@ -168,6 +168,29 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
                      int64_t padded_len, int num_q_heads, float scale, void* out, void* workspace,
                      size_t workspace_bytes, int dtype, void* stream);
 
+/*
+ * mi_decode_rows — the packed decode-step inputs of PagedRunner.prepare_decode_inputs
+ * (worker/paged_runner.py:138-166: per sequence [token, position, slot, position + 1, block table
+ * null-padded]) built on the device from a device mirror of the block tables, so a step uploads
+ * O(batch) integers instead of O(batch x max_blocks).
+ *
+ *   tables   [table_rows, table_stride] int64 on the device: one row per batch slot, holding that
+ *            slot's sequence's block table; entries are written only through `deltas`
+ *   deltas   [num_deltas, 3] int64 (row, column, block id): table entries added since the last
+ *            call, applied first
+ *   rows     [batch, 3] int64 (table row, token, position) of the step's sequences
+ *   out      int64, written as ids [n] | positions [n] | slots [n] | context lengths [n] |
+ *            tables [n, width]: row b < batch gets its token and position, slot
+ *            tables[row][pos / bs] * bs + pos % bs, context pos + 1 and the first
+ *            ceil((pos + 1) / bs) entries of its table row (the rest 0, the null block); rows
+ *            batch <= b < n are padding (token 0, position 0, slot 0, context 1, null table).
+ * Bit-exact with the host packing.  Out-of-range rows, columns or lengths are skipped and set
+ * MI_STATUS_BAD_INDEX / MI_STATUS_BAD_LENGTH.
+ */
+int mi_decode_rows(const int64_t* rows, int64_t batch, const int64_t* deltas, int64_t num_deltas, int64_t* tables,
+                   int64_t table_rows, int64_t table_stride, int64_t* out, int64_t n, int64_t width, int block_size,
+                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,4 +7,5 @@
 #include "layer_ops.cu"
 #include "api.cu"
 #include "api_layers.cu"
+#include "decode_meta.cu"
 #include "api_static.cu"

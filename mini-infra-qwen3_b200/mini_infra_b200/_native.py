@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _I64P, _P, _P, _I64P, _P, _P, _L, _I, _I, _I, _P, _L, _P, _P, _L, _L, _I, ctypes.c_float, _P, _P,
          ctypes.c_size_t, _I, _P],
     ),
+    "mi_decode_rows": (_I, [_P, _L, _P, _L, _P, _L, _L, _P, _L, _L, _I, _P]),
     # include/mi_layers.h
     "mi_rmsnorm": (_I, [_P, _L, _P, _L, _P, _L, _P, _P, _L, _L, _I, ctypes.c_float, _I, _P]),
     "mi_qk_norm_rope": (

@@ -1,9 +1,11 @@
 """Paged backend (reference ``engine/paged_schedule_backend.py``): glues scheduler, runner and pool.
 
 Per prefill step: chunk forward (model_ms, StepTimer), then ``store_prefill`` timed as cache_ms
-(host wall clock between two synchronisations).  Per decode step: host packing + H2D timed as
-cache_ms, then the decode forward (model_ms) — a CUDA-graph replay per batch bucket unless
-``cuda_graphs=False`` (a bucket's first step captures its graph before the timing starts).  Per
+(host wall clock between two synchronisations).  Per decode step: the step inputs built on the
+device from the slot-indexed block-table mirror (``PagedRunner.prepare_decode_rows``: O(batch)
+host work and upload) timed as cache_ms, then the decode forward (model_ms) — a CUDA-graph
+replay per batch bucket unless ``cuda_graphs=False`` (a bucket's first step captures its graph
+before the timing starts).  Per
 mixed step (mixed chunked prefill): one forward over decode rows and chunks (model_ms), then the
 chunks' ``store_prefill`` as cache_ms.  ``accessed_kv_cache_tokens`` counts history tokens
 read: sum of chunk starts (prefill) and sum of context lengths (decode).
@@ -61,6 +63,8 @@ class PagedScheduleBackend:
             device=self.device,
         )
         self.kv_cache_manager = KVCacheManager(self.block_size, num_blocks)
+        # decode inputs are built on the device from a slot-indexed mirror of the block tables
+        self.runner.enable_device_tables(max_running_requests, largest)
         if cuda_graphs and self.device.type == "cuda":
             # decode tables never exceed the largest request; round the graphs' width up to a power of two
             self.runner.enable_decode_graphs(self.pool.kv_pools, 1 << max(4, (largest - 1).bit_length()))
@@ -98,7 +102,8 @@ class PagedScheduleBackend:
         self.runner.warm_decode_graph(len(tables), max(len(t) for t in tables))  # first use of a bucket: capture
         synchronize(self.device)
         t0 = time.perf_counter()
-        ids, pos, md = self.runner.prepare_decode_inputs(
+        ids, pos, md = self.runner.prepare_decode_rows(
+            [(s.batch_slot_idx, s.request.request_idx) for s in scheduled],
             tables,
             last_tokens=[s.generated[-1] for s in scheduled],
             positions=[s.cache_length for s in scheduled],

@@ -407,3 +407,38 @@ def read_status(device: torch.device | None = None, clear: bool = True) -> int:
     rc = nat.load().mi_read_status(ctypes.byref(value), 1 if clear else 0, _stream(dev))
     nat.check(rc, "mi_read_status")
     return int(value.value)
+
+
+def decode_rows(
+    rows: torch.Tensor,
+    deltas: torch.Tensor | None,
+    tables: torch.Tensor,
+    out: torch.Tensor,
+    n: int,
+    width: int,
+    block_size: int,
+) -> torch.Tensor:
+    """Packed decode-step inputs built on the device (``mi_decode_rows``).
+
+    rows [B, 3] int64 (table row, token, position); deltas [D, 3] int64 (row, column, block id)
+    applied to the device tables [R, S] first; out (int64, >= 4n + n*width elements) receives
+    ids | positions | slots | context lengths | tables [n, width] (rows >= B are padding)."""
+    device = _require_cuda("decode_rows", rows, deltas, tables, out)
+    if tables.dtype != torch.int64 or tables.ndim != 2 or not tables.is_contiguous():
+        raise ValueError("tables must be a contiguous int64 [rows, stride] tensor")
+    if out.dtype != torch.int64 or not out.is_contiguous() or out.numel() < 4 * n + n * width:
+        raise ValueError(f"out must be a contiguous int64 tensor of at least {4 * n + n * width} elements")
+    rows = _index(rows, "rows")
+    if rows.numel() % 3:
+        raise ValueError("rows must be [batch, 3]")
+    nd = 0
+    if deltas is not None and deltas.numel():
+        deltas = _index(deltas, "deltas")
+        if deltas.numel() % 3:
+            raise ValueError("deltas must be [count, 3]")
+        nd = deltas.numel() // 3
+    rc = nat.load().mi_decode_rows(
+        _ptr(rows), rows.numel() // 3, _ptr(deltas if nd else None), nd, _ptr(tables), tables.shape[0],
+        tables.shape[1], _ptr(out), n, width, block_size, _stream(device))
+    nat.check(rc, "mi_decode_rows")
+    return out

@@ -16,6 +16,9 @@ tables).  Attention reads history in place from the pools; nothing gathers the h
   With ``enable_decode_graphs`` the packed rows are padded to a batch bucket and copied into
   that bucket's static input buffer, and the step replays the bucket's CUDA graph
   (``worker/decode_graphs.py``); otherwise it runs eagerly.
+* ``prepare_decode_rows`` — the same inputs built on the device (``enable_device_tables``): the
+  block tables live in a slot-indexed device mirror (``worker/block_tables.py``) that receives
+  only new entries, so the host work per step is O(batch), not O(batch x max_blocks).
 * ``run_mixed_step`` — decode rows and prefill chunks in one forward (the mixed chunked-prefill
   policy; no reference counterpart): one packed upload, projections over all tokens, one decode
   and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.
@@ -29,9 +32,11 @@ from typing import NamedTuple
 import numpy as np
 import torch
 
+from mini_infra_b200 import ops
 from mini_infra_b200.device import StepTimer
 from mini_infra_b200.model.qwen3 import ChunkPrefillMetadata, MixedMetadata, PagedAttentionMetadata
 from mini_infra_b200.worker.base_runner import BaseModelRunner, PrefillOutput
+from mini_infra_b200.worker.block_tables import DeviceBlockTables
 from mini_infra_b200.worker.decode_graphs import DecodeGraphSet, packed_length
 from mini_infra_b200.worker.kv_cache import KVCache
 from mini_infra_b200.worker.paged_kv_cache import PagedKVCachePool
@@ -62,9 +67,9 @@ def padded_width(longest: int) -> int:
     return -(-longest // step) * step
 
 
-def _to_device(values: list[int], device: torch.device) -> torch.Tensor:
+def _to_device(values: list[int] | np.ndarray, device: torch.device) -> torch.Tensor:
     """One pinned host buffer -> one asynchronous H2D copy."""
-    host = torch.tensor(values, dtype=torch.long)
+    host = torch.from_numpy(values) if isinstance(values, np.ndarray) else torch.tensor(values, dtype=torch.long)
     if device.type == "cuda":
         host = host.pin_memory()
     return host.to(device, non_blocking=True)
@@ -77,7 +82,12 @@ class PagedRunner(BaseModelRunner):
     d2h_bytes = 0
     graph_replays = 0  # decode steps served by a CUDA-graph replay
     decode_graphs: DecodeGraphSet | None = None
+    device_tables: DeviceBlockTables | None = None
     _graph_step: tuple[int, int, int] | None = None  # (bucket, batch, static buffer address)
+
+    def enable_device_tables(self, capacity: int, width: int) -> None:
+        """Build decode inputs on the device from a mirror of `capacity` slot rows of `width` blocks."""
+        self.device_tables = DeviceBlockTables(capacity, width, self.device)
 
     def enable_decode_graphs(self, kv_pools, width: int) -> None:
         """Replay decode steps of at most `width` table blocks from CUDA graphs over `kv_pools`."""
@@ -97,7 +107,7 @@ class PagedRunner(BaseModelRunner):
         if bucket is not None:
             g.static_inputs(bucket)
 
-    def _upload(self, values: list[int]) -> torch.Tensor:
+    def _upload(self, values: list[int] | np.ndarray) -> torch.Tensor:
         self.h2d_bytes += 8 * len(values)
         return _to_device(values, self.device)
 
@@ -192,6 +202,44 @@ class PagedRunner(BaseModelRunner):
             context_lens=packed[3 * b : 4 * b],
         )
         return packed[:b].view(b, 1), packed[b : 2 * b].view(b, 1), metadata
+
+    def prepare_decode_rows(
+        self,
+        row_keys: Sequence[tuple[int, int]],
+        block_tables: Sequence[Sequence[int]],
+        last_tokens: Sequence[int],
+        positions: Sequence[int],
+        block_size: int,
+    ) -> tuple[torch.Tensor, torch.Tensor, PagedAttentionMetadata]:
+        """``prepare_decode_inputs`` with the packing done on the device: row_keys[i] = (batch slot,
+        sequence key) of row i.  Uploads (slot, token, position) per row and the table entries
+        added since the slot's last step; one kernel writes ids, positions, slots, context lengths
+        and null-padded tables (into the bucket's static buffer when a decode graph serves the
+        step).  Same values as ``prepare_decode_inputs``."""
+        dt = self.device_tables
+        if dt is None:
+            raise RuntimeError("prepare_decode_rows needs enable_device_tables first")
+        b = len(block_tables)
+        max_blocks = max(len(t) for t in block_tables)
+        host, nrows, ndeltas = dt.step_inputs(row_keys, block_tables, last_tokens, positions)
+        up = self._upload(host)
+        rows, deltas = up[: 3 * nrows].view(nrows, 3), up[3 * nrows :].view(ndeltas, 3)
+        g = self.decode_graphs
+        bucket = g.bucket_for(b, max_blocks) if g is not None else None
+        if bucket is not None:
+            n, w = bucket, g.width
+            packed = g.static_inputs(n)
+            self._graph_step = (n, b, packed.data_ptr())
+        else:
+            n, w = b, max_blocks
+            packed = torch.empty(packed_length(n, w), dtype=torch.long, device=self.device)
+        ops.decode_rows(rows, deltas, dt.tables, packed, n, w, block_size)
+        metadata = PagedAttentionMetadata(
+            slot_mapping=packed[2 * n : 2 * n + b],
+            block_tables=packed[4 * n : 4 * n + b * w].view(b, w),
+            context_lens=packed[3 * n : 3 * n + b],
+        )
+        return packed[:b].view(b, 1), packed[n : n + b].view(b, 1), metadata
 
     def run_mixed_step(
         self,
