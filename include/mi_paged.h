@@ -142,6 +142,51 @@ int mi_paged_decode_static_scratch(const void* q, const int64_t* q_strides, cons
                                    void* out, int64_t out_stride, int dtype, void* stream);
 
 /*
+ * mi_paged_decode_exchange — mi_paged_decode on a KV-head partition with the exchange of the
+ * attention outputs fused in.  Replaces, for a rank of `world` that holds query heads
+ * [rank*num_q_heads, (rank+1)*num_q_heads) (num_q_heads is this rank's count), the decode call
+ * followed by the NCCL all-gather of the per-head outputs and the reordering into global head
+ * order (the reference runs on one device and has no exchange: model/qwen3.py:219-255 produces the
+ * [batch, all heads * head_dim] rows that o_proj reads).  The combine kernel stores row b of its
+ * local query head j straight into every rank's gathered buffer at
+ *   gathered[p] + b * gathered_stride + (rank * num_q_heads + j) * head_dim   (elements, p < world)
+ * with plain stores over NVLink (no multicast), then a one-warp barrier kernel stores epoch e into
+ * flags[p][rank] of every peer p (release, system scope) and waits (acquire) until every peer has
+ * stored e into flags[rank][p]; e = *epoch + 1, written back to *epoch.  After the call (in stream
+ * order) gathered[rank] holds all ranks' heads in global order.
+ *
+ *   gathered  [world] pointers valid in this process (peers' through mi_peer_open): each rank's
+ *             [batch, gathered_stride >= world*num_q_heads*head_dim] buffer, 16-byte aligned rows
+ *   flags     [world] pointers: each rank's [world] uint32 flag array, zero before the first call
+ *   epoch     this rank's uint32 call counter (device), zero before the first call
+ *   timeout_ns  bound of the barrier's wait; a peer that does not arrive in time sets
+ *             MI_STATUS_TIMEOUT and the call returns (the gathered rows are then incomplete)
+ * Every rank must make the same calls in the same order.  A rank may store into a peer's buffer
+ * while that peer still reads the previous call's rows, so consecutive calls must alternate
+ * between two buffers.  bf16/fp16 on the tensor-core decode path only (else MI_ERR_UNSUPPORTED).
+ */
+int mi_paged_decode_exchange(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,
+                             const int64_t* new_strides, const int64_t* slot_mapping, void* k_pool, void* v_pool,
+                             int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                             const int64_t* block_tables, int64_t table_stride, int64_t max_blocks_per_seq,
+                             const int64_t* context_lens, int64_t batch, int num_q_heads, float scale,
+                             void* const* gathered, int64_t gathered_stride, unsigned int* const* flags,
+                             unsigned int* epoch, int rank, int world, int64_t timeout_ns, void* workspace,
+                             size_t workspace_bytes, int dtype, void* stream);
+
+/*
+ * Peer memory for mi_paged_decode_exchange (no counterpart in the single-device reference).
+ * mi_peer_handle writes the CUDA IPC handle (MI_PEER_HANDLE_BYTES) of the allocation holding `ptr`
+ * and ptr's offset into it; another process of the same node opens it with mi_peer_open (a pointer
+ * valid in that process, peer access enabled) and releases it with mi_peer_close.  Nothing is
+ * allocated; the exporting process keeps the buffer alive until every peer has closed it.
+ */
+#define MI_PEER_HANDLE_BYTES 64
+int mi_peer_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+int mi_peer_open(const void* handle, int64_t offset, void** ptr_out);
+int mi_peer_close(void* ptr, int64_t offset);
+
+/*
  * mi_paged_prefill — varlen chunked-prefill attention for one layer.  Replaces, for
  * PagedRunner.run_prefill_chunk_step (worker/paged_runner.py:32-102), the all-layer history
  * gather (gather_blocks), torch.cat(history, chunk) (model/qwen3.py:328-329), the padded causal

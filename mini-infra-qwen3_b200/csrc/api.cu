@@ -282,12 +282,27 @@ size_t mi_paged_decode_workspace_size(int64_t batch, int num_q_heads, int num_kv
   return mi::plan_decode(batch, num_q_heads, num_kv_heads, head_dim, max_blocks_per_seq, block_size, dtype).ws_bytes;
 }
 
-int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,
-                    const int64_t* new_strides, const int64_t* slot_mapping, void* k_pool, void* v_pool,
-                    int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
-                    const int64_t* block_tables, int64_t table_stride, int64_t max_blocks_per_seq,
-                    const int64_t* context_lens, int64_t batch, int num_q_heads, float scale, void* out,
-                    int64_t out_stride, void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Where the decode output goes: `out` (world == 0), or every rank's gathered buffer followed by the
+// peer barrier (mi_paged_decode_exchange).
+struct DecodeExchange {
+  int world = 0;
+  int rank = 0;
+  int64_t gathered_sb = 0;  // bytes
+  char* gathered[mi::kMaxPeers] = {};
+  mi::PeerBarrierArgs barrier{};
+};
+
+int paged_decode_impl(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,
+                      const int64_t* new_strides, const int64_t* slot_mapping, void* k_pool, void* v_pool,
+                      int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                      const int64_t* block_tables, int64_t table_stride, int64_t max_blocks_per_seq,
+                      const int64_t* context_lens, int64_t batch, int num_q_heads, float scale, void* out,
+                      int64_t out_stride, void* workspace, size_t workspace_bytes, int dtype, void* stream,
+                      const DecodeExchange& ex) {
   if (int rc = check_pool_geometry(num_blocks, block_size, num_kv_heads, head_dim, dtype)) return rc;
   if (batch < 0) return fail(MI_ERR_INVALID, "batch < 0");
   if (batch == 0) return MI_OK;
@@ -296,7 +311,7 @@ int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, 
     return fail(MI_ERR_INVALID, "num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)", num_q_heads,
                 num_kv_heads);
   if (head_dim > 256) return fail(MI_ERR_UNSUPPORTED, "head_dim %d > 256", head_dim);
-  if (!q || !q_strides || !k_pool || !v_pool || !block_tables || !context_lens || !out)
+  if (!q || !q_strides || !k_pool || !v_pool || !block_tables || !context_lens || (!out && ex.world == 0))
     return fail(MI_ERR_INVALID, "mi_paged_decode: null pointer argument");
   if (max_blocks_per_seq < 1 || table_stride < max_blocks_per_seq)
     return fail(MI_ERR_INVALID, "block table needs at least one column (max_blocks=%lld, stride=%lld)",
@@ -318,6 +333,10 @@ int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, 
                     (q_strides[1] * es) % 4 == 0 && num_blocks * block_size < (int64_t(1) << 31);
     if (!ok) plan = mi::plan_decode(batch, num_q_heads, num_kv_heads, head_dim, max_blocks_per_seq, block_size, -1);
   }
+  if (ex.world > 0 && !plan.use_mma)
+    return fail(MI_ERR_UNSUPPORTED,
+                "mi_paged_decode_exchange: needs the tensor-core decode path (bf16/fp16, head_dim 64/128, "
+                "block size 16/32, at most 8 query heads per KV head, 16-byte aligned pools)");
   mi::DecodeArgs a{};
   a.q = static_cast<const char*>(q);
   a.q_sb = q_strides[0] * es;
@@ -342,6 +361,10 @@ int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, 
   a.max_parts = plan.max_splits * plan.parts_per_split;
   a.out = static_cast<char*>(out);
   a.out_sb = out_stride * es;
+  a.world = ex.world;
+  a.rank = ex.rank;
+  a.gathered_sb = ex.gathered_sb;
+  for (int p = 0; p < mi::kMaxPeers; ++p) a.gathered[p] = ex.gathered[p];
   CUtensorMap tk, tv;
   if (plan.use_mma) {
     if (!workspace || workspace_bytes < plan.ws_bytes || !aligned(workspace, 256))
@@ -354,7 +377,67 @@ int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, 
     if (int rc = pool_tensor_map(v_pool, num_blocks, block_size, num_kv_heads, head_dim, dtype, &tv)) return rc;
   }
   cudaError_t e = mi::launch_paged_decode(a, plan, &tk, &tv, dtype, s);
-  return e == cudaSuccess ? MI_OK : cuda_fail(e, "mi_paged_decode launch");
+  if (e != cudaSuccess) return cuda_fail(e, "mi_paged_decode launch");
+  if (ex.world > 0) {
+    e = mi::launch_peer_barrier(ex.barrier, s);
+    if (e != cudaSuccess) return cuda_fail(e, "mi_paged_decode_exchange: peer barrier launch");
+  }
+  return MI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mi_paged_decode(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,
+                    const int64_t* new_strides, const int64_t* slot_mapping, void* k_pool, void* v_pool,
+                    int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                    const int64_t* block_tables, int64_t table_stride, int64_t max_blocks_per_seq,
+                    const int64_t* context_lens, int64_t batch, int num_q_heads, float scale, void* out,
+                    int64_t out_stride, void* workspace, size_t workspace_bytes, int dtype, void* stream) {
+  return paged_decode_impl(q, q_strides, k_new, v_new, new_strides, slot_mapping, k_pool, v_pool, num_blocks,
+                           block_size, num_kv_heads, head_dim, block_tables, table_stride, max_blocks_per_seq,
+                           context_lens, batch, num_q_heads, scale, out, out_stride, workspace, workspace_bytes,
+                           dtype, stream, DecodeExchange{});
+}
+
+int mi_paged_decode_exchange(const void* q, const int64_t* q_strides, const void* k_new, const void* v_new,
+                             const int64_t* new_strides, const int64_t* slot_mapping, void* k_pool, void* v_pool,
+                             int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                             const int64_t* block_tables, int64_t table_stride, int64_t max_blocks_per_seq,
+                             const int64_t* context_lens, int64_t batch, int num_q_heads, float scale,
+                             void* const* gathered, int64_t gathered_stride, unsigned int* const* flags,
+                             unsigned int* epoch, int rank, int world, int64_t timeout_ns, void* workspace,
+                             size_t workspace_bytes, int dtype, void* stream) {
+  if (world < 2 || world > mi::kMaxPeers || rank < 0 || rank >= world)
+    return fail(MI_ERR_INVALID, "mi_paged_decode_exchange: rank %d of world %d (2..%d ranks)", rank, world,
+                mi::kMaxPeers);
+  if (!gathered || !flags || !epoch || timeout_ns <= 0)
+    return fail(MI_ERR_INVALID, "mi_paged_decode_exchange: null pointer argument or non-positive timeout");
+  const int es = elem_size(dtype);
+  if (es != 2) return fail(MI_ERR_INVALID, "mi_paged_decode_exchange: bf16 or fp16 only");
+  if (gathered_stride < (int64_t)world * num_q_heads * head_dim)
+    return fail(MI_ERR_INVALID, "mi_paged_decode_exchange: gathered rows of %lld elements hold less than %d ranks x "
+                "%d heads x %d", (long long)gathered_stride, world, num_q_heads, head_dim);
+  DecodeExchange ex;
+  ex.world = world;
+  ex.rank = rank;
+  ex.gathered_sb = gathered_stride * es;
+  for (int p = 0; p < world; ++p) {
+    if (!gathered[p] || !flags[p] || !aligned(gathered[p], 16) || !aligned(flags[p], 4))
+      return fail(MI_ERR_INVALID, "mi_paged_decode_exchange: rank %d's buffers are null or misaligned", p);
+    ex.gathered[p] = static_cast<char*>(gathered[p]);
+    ex.barrier.flags[p] = flags[p];
+  }
+  if (ex.gathered_sb % 16) return fail(MI_ERR_INVALID, "mi_paged_decode_exchange: row stride not 16-byte aligned");
+  ex.barrier.epoch = epoch;
+  ex.barrier.rank = rank;
+  ex.barrier.world = world;
+  ex.barrier.timeout_ns = (uint64_t)timeout_ns;
+  return paged_decode_impl(q, q_strides, k_new, v_new, new_strides, slot_mapping, k_pool, v_pool, num_blocks,
+                           block_size, num_kv_heads, head_dim, block_tables, table_stride, max_blocks_per_seq,
+                           context_lens, batch, num_q_heads, scale, nullptr, 0, workspace, workspace_bytes, dtype,
+                           stream, ex);
 }
 
 size_t mi_paged_prefill_workspace_size(int64_t batch, int64_t padded_len, int num_q_heads, int num_kv_heads,

@@ -60,6 +60,8 @@ cudaError_t launch_kv_gather_blocks(const GatherArgs& a, int64_t items, int vec_
 // ------------------------------------------------------------------------------------------
 // Paged decode
 // ------------------------------------------------------------------------------------------
+constexpr int kMaxPeers = 8;  // ranks of a KV-head partition reachable by peer stores
+
 struct DecodeArgs {
   const char* q;
   int64_t q_sb, q_sh;  // bytes
@@ -83,7 +85,26 @@ struct DecodeArgs {
   float* ws_ml;      // [batch, hq, max_parts, 2]
   char* out;
   int64_t out_sb;    // bytes
+  // Exchange of the output rows over a KV-head partition (mi_paged_decode_exchange): with
+  // world > 0 the combine writes row b of local query head j to every rank's gathered buffer,
+  // gathered[p] + b * gathered_sb + ((rank * hq + j) * head_dim) elements, instead of to `out`.
+  int world;
+  int rank;
+  int64_t gathered_sb;  // bytes
+  char* gathered[kMaxPeers];
 };
+
+// The barrier that follows an exchange: rank r stores epoch e into flags[p][r] of every peer p
+// (release, system scope), then waits (acquire, bounded by timeout_ns) until flags[r][p] >= e for
+// every peer; e = *epoch + 1, written back to *epoch.
+struct PeerBarrierArgs {
+  unsigned int* flags[kMaxPeers];
+  unsigned int* epoch;
+  int rank;
+  int world;
+  uint64_t timeout_ns;
+};
+cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, cudaStream_t s);
 
 struct DecodePlan {
   bool use_mma;

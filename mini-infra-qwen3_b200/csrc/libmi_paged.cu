@@ -8,4 +8,5 @@
 #include "api.cu"
 #include "api_layers.cu"
 #include "decode_meta.cu"
+#include "peer.cu"
 #include "api_static.cu"

@@ -14,6 +14,7 @@
 // Scalar kernel (every other case, incl. fp32): one warp per (sequence, query head), lanes split
 //   head_dim, single pass online softmax in fp32, reads the pool directly through the table.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -282,9 +283,52 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeArgs a)
     l_all = warp_sum(l_all);
   }
   const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
-  T* dst = reinterpret_cast<T*>(a.out + b * a.out_sb) + (int64_t)hq * D + lane * PER_LANE;
+  if (a.world == 0) {
+    T* dst = reinterpret_cast<T*>(a.out + b * a.out_sb) + (int64_t)hq * D + lane * PER_LANE;
 #pragma unroll
-  for (int i = 0; i < PER_LANE; ++i) dst[i] = Elem<T>::from_f(acc[i] * inv);
+    for (int i = 0; i < PER_LANE; ++i) dst[i] = Elem<T>::from_f(acc[i] * inv);
+    return;
+  }
+  // Exchange: the row slice goes to every rank's gathered buffer (peer stores over NVLink), one
+  // vector store per lane and destination; the system-scope fence orders them before the barrier
+  // kernel's release of this rank's flag.
+  static_assert(PER_LANE * sizeof(T) == 8 || PER_LANE * sizeof(T) == 4, "16-bit rows of 64 or 128");
+  using Vec = typename std::conditional<PER_LANE * sizeof(T) == 8, uint2, uint32_t>::type;
+  union {
+    Vec v;
+    T e[PER_LANE];
+  } pk;
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) pk.e[i] = Elem<T>::from_f(acc[i] * inv);
+  const int64_t col = ((int64_t)a.rank * a.hq + hq) * D + lane * PER_LANE;
+  for (int p = 0; p < a.world; ++p)
+    *reinterpret_cast<Vec*>(reinterpret_cast<T*>(a.gathered[p] + b * a.gathered_sb) + col) = pk.v;
+  __threadfence_system();
+}
+
+// Barrier after an exchange: one warp, lane p signals and then waits for peer p.
+__global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerBarrierArgs a) {
+  const int p = threadIdx.x;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  const unsigned int e = *reinterpret_cast<volatile unsigned int*>(a.epoch) + 1u;
+  if (p < a.world && p != a.rank) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[p] + a.rank), "r"(e) : "memory");
+    const unsigned int* mine = a.flags[a.rank] + p;
+    const uint64_t start = globaltimer_ns();
+    while (true) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int)(v - e) >= 0) break;
+      if (globaltimer_ns() - start > a.timeout_ns) {
+        record_status(MI_STATUS_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncwarp();
+  if (p == 0) *a.epoch = e;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 // Generic single-pass kernel: one warp per (sequence, query head); any dtype, head_dim <= 256,
@@ -401,6 +445,11 @@ cudaError_t launch_split_t(const DecodeArgs& a, const DecodePlan& p, const CUten
 }
 
 }  // namespace
+
+cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, cudaStream_t s) {
+  peer_barrier_kernel<<<1, 32, 0, s>>>(a);
+  return cudaGetLastError();
+}
 
 DecodePlan plan_decode(int64_t batch, int hq, int hkv, int head_dim, int64_t max_blocks, int block_size, int dtype) {
   DecodePlan p{};

@@ -40,6 +40,14 @@ SIGNATURES: dict[str, tuple] = {
         _I,
         [_P, _I64P, _P, _P, _I64P, _P, _P, _P, _L, _I, _I, _I, _P, _L, _L, _P, _L, _I, ctypes.c_float, _P, _L, _I, _P],
     ),
+    "mi_paged_decode_exchange": (
+        _I,
+        [_P, _I64P, _P, _P, _I64P, _P, _P, _P, _L, _I, _I, _I, _P, _L, _L, _P, _L, _I, ctypes.c_float, _P, _L, _P, _P,
+         _I, _I, _L, _P, ctypes.c_size_t, _I, _P],
+    ),
+    "mi_peer_handle": (_I, [_P, _P, _I64P]),
+    "mi_peer_open": (_I, [_P, _L, ctypes.POINTER(ctypes.c_void_p)]),
+    "mi_peer_close": (_I, [_P, _L]),
     "mi_paged_prefill_workspace_size": (ctypes.c_size_t, [_L, _L, _I, _I, _I, _L, _I, _I]),
     "mi_paged_prefill": (
         _I,
