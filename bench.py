@@ -15,8 +15,11 @@ Prints ONE JSON line on rank 0.  ``value`` = KV bytes read per step by all ranks
 context lengths x 4096 B for 8 KV heads x 128 dims x K+V x bf16, x 36 layer calls) / the max over
 ranks of the device time per step.  Besides the contract keys the line carries:
 
-* ``per_layer_ms``: attention (append + split-K decode + combine) and exchange (all-gather of the
-  per-head outputs) of one layer call, each timed alone, and which one limits the step;
+* ``per_layer_ms``: one layer call's attention of the local heads (append + split-K decode +
+  combine) and, with N > 1, the same with the exchange of the per-head outputs fused in (the
+  combine stores every row into every rank's buffer over NVLink, then a flag barrier), each timed
+  alone; their difference is the exchange's cost, beside an NCCL all-gather + reorder of the same
+  rows for comparison (``--nccl-exchange`` uses that instead);
 * ``parity``: after the timed region, the output rows of a few sequences (the longest and the
   shortest context among them) against a float32 torch reference computed on the device from the
   same pools; with N > 1 ranks the references are gathered, so the check covers the exchange;
@@ -572,31 +575,53 @@ def run_decode(args, spec: dict) -> None:
     ws = ops.workspace(device, ops.decode_workspace_bytes(b, hq_loc, pools[0][0], tables.shape[1]))
     layers = spec["layers"]
     holder = {}
+    # N > 1: the decode's combine kernel stores every output row into every rank's gathered buffer
+    # (peer stores over NVLink, then a flag barrier); --nccl-exchange: NCCL all-gather + reorder
+    ex = None
+    if world > 1 and not args.nccl_exchange:
+        from mini_infra_b200.exchange import PeerExchange
 
-    def attention(layer: int):
+        ex = PeerExchange(group, rank, world, max_rows=b, width=spec["hq"] * D, dtype=torch.bfloat16, device=device)
+
+    def attention_local(layer: int):  # append + split-K + combine of this rank's heads into `out`
         kp, vp = pools[layer % len(pools)]
         ops.paged_decode(x["q"], kp, vp, tables, ctx, scale, key_new=x["kn"], value_new=x["vn"], slot_mapping=slots,
                          out=out, ws=ws)
 
+    def attention(layer: int) -> torch.Tensor:  # the same, plus the exchange: all heads, global order
+        if ex is None:
+            attention_local(layer)
+            return gather_heads(out, part)
+        kp, vp = pools[layer % len(pools)]
+        return ops.paged_decode_exchange(x["q"], kp, vp, tables, ctx, scale, ex, layer % 2, key_new=x["kn"],
+                                         value_new=x["vn"], slot_mapping=slots, ws=ws)
+
     def step():
         for layer in range(layers):
-            attention(layer)
-            holder["gathered"] = gather_heads(out, part)
+            holder["gathered"] = attention(layer)
 
     for _ in range(args.warmup):
         step()
     with ClockSampler(local) as clocks:
         ms = timed(step, args.steps)
-        # per-layer legs, each alone: the attention (append + split-K + combine) and the exchange
+        # per-layer legs, each alone: the attention of the local heads, the attention with the
+        # exchange, and (N > 1) the NCCL all-gather + reorder for comparison
         state = {"l": 0}
 
-        def attn_leg():
+        def local_leg():
+            state["l"] += 1
+            attention_local(state["l"])
+
+        def full_leg():
             state["l"] += 1
             attention(state["l"])
 
         n_leg = max(min(args.steps * layers, 1000), 10)
-        attn_ms = timed(attn_leg, n_leg)
-        exch_ms = timed(lambda: gather_heads(out, part), n_leg) if world > 1 else 0.0
+        n_leg += n_leg % 2  # an even count keeps the exchange's buffers alternating
+        attn_ms = timed(local_leg, n_leg)
+        full_ms = timed(full_leg, n_leg) if world > 1 else attn_ms
+        exch_ms = max(full_ms - attn_ms, 0.0)
+        nccl_ms = timed(lambda: gather_heads(out, part), n_leg) if world > 1 else 0.0
 
         # roofline of the attention launch alone (split-K kernel + combine, no append)
         def decode_only():
@@ -623,9 +648,14 @@ def run_decode(args, spec: dict) -> None:
                 d_q.copy_(h_q, non_blocking=True)
                 d_kn.copy_(h_kn, non_blocking=True)
                 d_vn.copy_(h_vn, non_blocking=True)
-                ops.paged_decode(d_q, kp, vp, tb, cx, scale, key_new=d_kn, value_new=d_vn, slot_mapping=sl, out=out,
-                                 ws=ws)
-                h_out.copy_(gather_heads(out, part), non_blocking=True)
+                if ex is None:
+                    ops.paged_decode(d_q, kp, vp, tb, cx, scale, key_new=d_kn, value_new=d_vn, slot_mapping=sl,
+                                     out=out, ws=ws)
+                    gathered_out = gather_heads(out, part)
+                else:
+                    gathered_out = ops.paged_decode_exchange(d_q, kp, vp, tb, cx, scale, ex, layer % 2, key_new=d_kn,
+                                                             value_new=d_vn, slot_mapping=sl, ws=ws)
+                h_out.copy_(gathered_out, non_blocking=True)
 
         e2e_step()
         ms_e2e = timed(e2e_step, max(min(args.steps, 50), 3))
@@ -642,8 +672,7 @@ def run_decode(args, spec: dict) -> None:
 
     # parity: one more layer call on pool 0 (append included), then rows against float32 torch
     ops.read_status(device)
-    attention(0)
-    gathered = gather_heads(out, part)
+    gathered = attention(0)
     rows = parity_rows(seqs["ctx"])
     ref = decode_reference_rows(x["q"], pools[0][0], pools[0][1], seqs["tables"], seqs["ctx"], rows, scale)
     if world > 1:
@@ -666,7 +695,7 @@ def run_decode(args, spec: dict) -> None:
         if sub_scatter is not None:
             sub_scatter["cpu_baseline"] = cpu_scatter_leg()
     if rank == 0:
-        limiter = "attention (HBM-bound decode)" if attn_ms >= 4 * exch_ms else "exchange (all-gather)"
+        limiter = "attention (HBM-bound decode)" if attn_ms >= 4 * exch_ms else "exchange"
         traffic = alg_bytes * NCU_DECODE["traffic"] / NCU_DECODE["algorithmic"]
         line = {
             "metric": METRIC,
@@ -692,9 +721,15 @@ def run_decode(args, spec: dict) -> None:
                 "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU",
                 "l2": "inputs larger than L2 (every layer call reads >= 2 GB of pool per rank)",
                 "step": "per layer call: append + paged decode (split-K + combine)"
-                        + (" + all-gather of the per-head outputs" if world > 1 else ""),
+                        + ((" + NCCL all-gather of the per-head outputs" if ex is None else
+                            " with the per-head outputs stored into every rank's buffer (peer stores + barrier)")
+                           if world > 1 else ""),
             },
-            "per_layer_ms": {"step": ms / layers, "attention": attn_ms, "exchange": exch_ms, "limiter": limiter},
+            "per_layer_ms": {"step": ms / layers, "attention": attn_ms, "attention_with_exchange": full_ms,
+                             "exchange": exch_ms, "limiter": limiter,
+                             "exchange_kind": ("none" if world == 1 else "NCCL all-gather + reorder copy" if ex is None
+                                               else "fused: combine stores into every rank's buffer + flag barrier"),
+                             "nccl_all_gather_and_reorder": nccl_ms},
             "roofline": {
                 "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
@@ -705,7 +740,7 @@ def run_decode(args, spec: dict) -> None:
             "parity": parity,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e},
-            "gpu_launches": 3 * layers * args.steps,
+            "gpu_launches": (3 + (ex is not None)) * layers * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "prefill": sub_prefill,
@@ -713,6 +748,8 @@ def run_decode(args, spec: dict) -> None:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        if ex is not None:
+            ex.close()
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
@@ -890,6 +927,8 @@ def main() -> None:
                     help="override the workload's batch (small cases for ncu captures; not a bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true", help="skip the prefill / scatter sub-records")
+    ap.add_argument("--nccl-exchange", action="store_true",
+                    help="N > 1: exchange the per-head outputs with the NCCL all-gather instead of peer stores")
     ap.add_argument("--policy", choices=["prefill-first", "chunked", "mixed"], default="prefill-first",
                     help="config 3 batching policy (chunked / mixed: token budget %d)" % C3_TOKEN_BUDGET)
     args = ap.parse_args()

@@ -38,6 +38,7 @@ class PagedScheduleBackend:
         batching_method: BatchingMethod = BatchingMethod.CONTINUOUS,
         pad_token_id: int = 0,
         cuda_graphs: bool = True,
+        peer_exchange: bool = True,
     ) -> None:
         self.model = model
         self.device = next(model.parameters()).device
@@ -65,6 +66,21 @@ class PagedScheduleBackend:
         self.kv_cache_manager = KVCacheManager(self.block_size, num_blocks)
         # decode inputs are built on the device from a slot-indexed mirror of the block tables
         self.runner.enable_device_tables(max_running_requests, largest)
+        part = getattr(model, "partition", None)
+        if part is not None and part.world > 1:
+            # Decode outputs exchanged by peer stores, with rows for the largest decode step (kept on
+            # the model across runs: detach_peer_exchange before the process group goes), or by
+            # the NCCL all-gather (peer_exchange=False).
+            from mini_infra_b200.exchange import attach_peer_exchange, detach_peer_exchange
+            from mini_infra_b200.worker.decode_graphs import BUCKETS
+
+            rows = max(max_running_requests, BUCKETS[-1])
+            current = model.model.layers[0].self_attn.exchange  # type: ignore[attr-defined]
+            if current is not None and (not peer_exchange or current.max_rows < rows):
+                detach_peer_exchange(model)
+                current = None
+            if peer_exchange and current is None:
+                attach_peer_exchange(model, rows, self.block_size)
         if cuda_graphs and self.device.type == "cuda":
             # decode tables never exceed the largest request; round the graphs' width up to a power of two
             self.runner.enable_decode_graphs(self.pool.kv_pools, 1 << max(4, (largest - 1).bit_length()))

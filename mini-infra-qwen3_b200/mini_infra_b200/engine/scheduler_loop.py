@@ -95,10 +95,13 @@ def run_scheduler(
     pad_token_id: int = 0,
     stop_on_eos: bool = True,
     cuda_graphs: bool = True,
+    peer_exchange: bool = True,
 ) -> ScheduleResult:
     """Run the requests through the paged engine; returns sequences, events and metrics.
 
-    ``cuda_graphs`` replays decode steps from per-batch-bucket CUDA graphs (False: eager)."""
+    ``cuda_graphs`` replays decode steps from per-batch-bucket CUDA graphs (False: eager).
+    ``peer_exchange`` (head-partitioned bf16/fp16 models): decode outputs are exchanged by the
+    decode kernel's peer stores (``exchange.PeerExchange``); False keeps the NCCL all-gather."""
     if not requests:
         raise ValueError("requests must not be empty")
     mrr = config.scheduler_config.max_running_requests or len(requests)
@@ -110,7 +113,7 @@ def run_scheduler(
     if config.batching_method not in (BatchingMethod.CONTINUOUS, BatchingMethod.FIXED):
         raise ValueError(f"paged-kv-cache supports continuous or fixed batching, got {config.batching_method.value}")
     backend = PagedScheduleBackend(model, requests, mrr, config.kv_cache_config, config.batching_method, pad_token_id,
-                                   cuda_graphs=cuda_graphs)
+                                   cuda_graphs=cuda_graphs, peer_exchange=peer_exchange)
     try:
         return _run_loop(backend, requests, mrr, config, eos_token_id, stop_on_eos)
     finally:

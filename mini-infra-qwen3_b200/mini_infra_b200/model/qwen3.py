@@ -26,7 +26,9 @@ Present K/V returned by prefill are [B, H_kv, L, D] views (the reference's ``KVC
 
 Head partition (``tp_world > 1``): the layer keeps query heads [r*Hq/P, (r+1)*Hq/P) and KV heads
 [r*H/P, (r+1)*H/P); its pools hold only those KV heads; the attention output is all-gathered
-over the process group before the replicated o_proj.
+over the process group before the replicated o_proj — on decode, when a ``PeerExchange`` is
+attached (``exchange.attach_peer_exchange``), by the decode kernel's own stores into every rank's
+buffer (no NCCL call, no reordering copy), otherwise by NCCL.
 """
 
 from __future__ import annotations
@@ -180,6 +182,9 @@ class Qwen3Attention(nn.Module):
         self.q_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
         self.k_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
         self.packed_qkv: torch.Tensor | None = None  # set by pack_projections_
+        # decode output exchange by peer stores (exchange.attach_peer_exchange); None: NCCL all-gather
+        self.exchange = None
+        self.exchange_slot = 0
 
     def forward(self, x, cos, sin, kv_pool: PastKeyValue | None, metadata):
         """x [B, L, hidden], cos/sin [B, L, D] -> (o_proj output [B, L, hidden], present)."""
@@ -196,6 +201,12 @@ class Qwen3Attention(nn.Module):
             q_out, _, _ = ops.qk_norm_rope(q, k, v, self.q_norm.weight, self.k_norm.weight, cos2, sin2, self.q_norm.eps,
                                            self.num_heads, self.num_kv_heads, kv_out=False,
                                            slot_mapping=metadata.slot_mapping, k_pool=key_pool, v_pool=value_pool)
+            ex = self.exchange
+            if ex is not None and b <= ex.max_rows:
+                # the combine stores every rank's rows into every rank's buffer: already in global order
+                attn = ops.paged_decode_exchange(q_out, key_pool, value_pool, metadata.block_tables,
+                                                 metadata.context_lens, self.scaling, ex, self.exchange_slot)
+                return self.o_proj(attn.view(b, length, -1)), kv_pool
             attn = ops.paged_decode(q_out, key_pool, value_pool, metadata.block_tables, metadata.context_lens,
                                     self.scaling)
             present = kv_pool

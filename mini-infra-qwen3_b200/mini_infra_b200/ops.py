@@ -185,6 +185,45 @@ def decode_workspace_bytes(batch: int, num_q_heads: int, k_pool: torch.Tensor, m
                                                          dtype_code(k_pool.dtype)))
 
 
+def _decode_common(query, k_pool, v_pool, block_tables, context_lens, key_new, value_new, slot_mapping, name):
+    """Argument checks shared by the decode entry points; returns the checked tensors and sizes."""
+    n, bs, h, d = _check_pool(k_pool, v_pool)
+    if query.ndim != 3 or query.shape[2] != d or query.dtype != k_pool.dtype:
+        raise ValueError(f"query must be [B, Hq, {d}] {k_pool.dtype}, got {tuple(query.shape)} {query.dtype}")
+    query = _rows_contiguous_last(query)
+    b, hq, _ = query.shape
+    tables = block_tables if block_tables.stride(-1) == 1 else block_tables.contiguous()
+    if tables.dtype != torch.int64 or tables.ndim != 2 or tables.shape[0] != b:
+        raise ValueError(f"block_tables must be int64 [B, max_blocks], got {tuple(tables.shape)} {tables.dtype}")
+    ctx = _index(context_lens, "context_lens")
+    if ctx.numel() != b:
+        raise ValueError(f"context_lens has {ctx.numel()} entries for batch {b}")
+    if hq % h:
+        raise ValueError(f"{hq} query heads are not a multiple of {h} KV heads")
+    new_strides = None
+    if (key_new is None) != (value_new is None) or (key_new is None) != (slot_mapping is None):
+        raise ValueError("key_new, value_new and slot_mapping go together")
+    if key_new is not None:
+        if key_new.shape != (b, h, d) or value_new.shape != (b, h, d) or slot_mapping.numel() != b:
+            raise ValueError(f"key_new/value_new must be [{b}, {h}, {d}] with one slot per row")
+        key_new, value_new = _rows_contiguous_last(key_new), _rows_contiguous_last(value_new)
+        if key_new.stride() != value_new.stride():
+            value_new = value_new.contiguous()
+            key_new = key_new.contiguous()
+        new_strides = nat.i64_array([key_new.stride(0), key_new.stride(1)])
+        slot_mapping = _index(slot_mapping, "slot_mapping")
+    return query, tables, ctx, key_new, value_new, slot_mapping, new_strides, (n, bs, h, d, b, hq)
+
+
+def _decode_workspace(lib, device, b, hq, h, d, max_blocks, bs, code, ws):
+    need = int(lib.mi_paged_decode_workspace_size(b, hq, h, d, max_blocks, bs, code))
+    if ws is None:
+        ws = workspace(device, need)
+    base = ws.data_ptr()
+    aligned = (base + 255) & ~255
+    return ctypes.c_void_p(aligned), ws.numel() * ws.element_size() - (aligned - base)
+
+
 def paged_decode(
     query: torch.Tensor,
     k_pool: torch.Tensor,
@@ -204,52 +243,63 @@ def paged_decode(
     """
     device = _require_cuda("paged_decode", query, k_pool, v_pool, block_tables, context_lens, key_new, value_new,
                            slot_mapping, out)
-    n, bs, h, d = _check_pool(k_pool, v_pool)
-    if query.ndim != 3 or query.shape[2] != d or query.dtype != k_pool.dtype:
-        raise ValueError(f"query must be [B, Hq, {d}] {k_pool.dtype}, got {tuple(query.shape)} {query.dtype}")
-    query = _rows_contiguous_last(query)
-    b, hq, _ = query.shape
-    tables = block_tables if block_tables.stride(-1) == 1 else block_tables.contiguous()
-    if tables.dtype != torch.int64 or tables.ndim != 2 or tables.shape[0] != b:
-        raise ValueError(f"block_tables must be int64 [B, max_blocks], got {tuple(tables.shape)} {tables.dtype}")
-    ctx = _index(context_lens, "context_lens")
-    if ctx.numel() != b:
-        raise ValueError(f"context_lens has {ctx.numel()} entries for batch {b}")
-    if hq % h:
-        raise ValueError(f"{hq} query heads are not a multiple of {h} KV heads")
+    query, tables, ctx, key_new, value_new, slot_mapping, new_strides, (n, bs, h, d, b, hq) = _decode_common(
+        query, k_pool, v_pool, block_tables, context_lens, key_new, value_new, slot_mapping, "paged_decode")
     if out is None:
         out = torch.empty((b, hq * d), dtype=query.dtype, device=device)
     elif out.shape != (b, hq * d) or out.dtype != query.dtype or out.stride(-1) != 1:
         raise ValueError(f"out must be [{b}, {hq * d}] {query.dtype} with contiguous rows")
-    new_strides = None
-    if (key_new is None) != (value_new is None) or (key_new is None) != (slot_mapping is None):
-        raise ValueError("key_new, value_new and slot_mapping go together")
-    if key_new is not None:
-        if key_new.shape != (b, h, d) or value_new.shape != (b, h, d) or slot_mapping.numel() != b:
-            raise ValueError(f"key_new/value_new must be [{b}, {h}, {d}] with one slot per row")
-        key_new, value_new = _rows_contiguous_last(key_new), _rows_contiguous_last(value_new)
-        if key_new.stride() != value_new.stride():
-            value_new = value_new.contiguous()
-            key_new = key_new.contiguous()
-        new_strides = nat.i64_array([key_new.stride(0), key_new.stride(1)])
-        slot_mapping = _index(slot_mapping, "slot_mapping")
     max_blocks = tables.shape[1]
     lib = nat.load()
     code = dtype_code(k_pool.dtype)
-    need = int(lib.mi_paged_decode_workspace_size(b, hq, h, d, max_blocks, bs, code))
-    if ws is None:
-        ws = workspace(device, need)
-    base = ws.data_ptr()
-    aligned = (base + 255) & ~255
-    avail = ws.numel() * ws.element_size() - (aligned - base)
+    ws_ptr, avail = _decode_workspace(lib, device, b, hq, h, d, max_blocks, bs, code, ws)
     rc = lib.mi_paged_decode(
         _ptr(query), nat.i64_array([query.stride(0), query.stride(1)]), _ptr(key_new), _ptr(value_new), new_strides,
         _ptr(slot_mapping), _ptr(k_pool), _ptr(v_pool), n, bs, h, d, _ptr(tables), tables.stride(0), max_blocks,
-        _ptr(ctx), b, hq, float(scale), _ptr(out), out.stride(0), ctypes.c_void_p(aligned), avail, code,
-        _stream(device),
+        _ptr(ctx), b, hq, float(scale), _ptr(out), out.stride(0), ws_ptr, avail, code, _stream(device),
     )
     nat.check(rc, "mi_paged_decode")
     return out
+
+
+def paged_decode_exchange(
+    query: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_tables: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: float,
+    exchange,
+    slot: int,
+    key_new: torch.Tensor | None = None,
+    value_new: torch.Tensor | None = None,
+    slot_mapping: torch.Tensor | None = None,
+    ws: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``paged_decode`` on a KV-head partition with the output exchange fused in
+    (``mi_paged_decode_exchange``): returns this rank's gathered buffer `slot` as [B, world * Hq * D]
+    in global head order (query [B, Hq, D] holds this rank's Hq heads).  Every rank of `exchange`
+    must make the same calls in the same order, alternating `slot` between 0 and 1."""
+    device = _require_cuda("paged_decode_exchange", query, k_pool, v_pool, block_tables, context_lens, key_new,
+                           value_new, slot_mapping)
+    query, tables, ctx, key_new, value_new, slot_mapping, new_strides, (n, bs, h, d, b, hq) = _decode_common(
+        query, k_pool, v_pool, block_tables, context_lens, key_new, value_new, slot_mapping, "paged_decode_exchange")
+    if b > exchange.max_rows or exchange.world * hq * d != exchange.width or query.dtype != exchange.dtype:
+        raise ValueError(f"a decode of {b} rows x {hq} heads x {d} ({query.dtype}) does not fit the exchange "
+                         f"({exchange.max_rows} rows of {exchange.width} {exchange.dtype})")
+    max_blocks = tables.shape[1]
+    lib = nat.load()
+    code = dtype_code(k_pool.dtype)
+    ws_ptr, avail = _decode_workspace(lib, device, b, hq, h, d, max_blocks, bs, code, ws)
+    rc = lib.mi_paged_decode_exchange(
+        _ptr(query), nat.i64_array([query.stride(0), query.stride(1)]), _ptr(key_new), _ptr(value_new), new_strides,
+        _ptr(slot_mapping), _ptr(k_pool), _ptr(v_pool), n, bs, h, d, _ptr(tables), tables.stride(0), max_blocks,
+        _ptr(ctx), b, hq, float(scale), exchange.gathered_ptrs(slot), exchange.width, exchange.flag_ptrs(),
+        ctypes.c_void_p(exchange.epoch_ptr()), exchange.rank, exchange.world, exchange.timeout_ns, ws_ptr, avail, code,
+        _stream(device),
+    )
+    nat.check(rc, "mi_paged_decode_exchange")
+    return exchange.gathered(slot, b)
 
 
 def paged_prefill(
