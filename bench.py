@@ -458,13 +458,21 @@ def scatter_record(device, iters: int) -> dict:
     tokens = rows * chunk
     kv = tokens * 2 * hkv * D * 2
     pk = peaks()
-    res = {"tokens": tokens, "iters": iters, "kernels": "kv_scatter_kernel, kv_store_chunks_kernel",
-           "l2": "16 rotating source buffers and destination block sets (128 MiB of sources)"}
+    per_graph = 4 * rot
+    res = {"tokens": tokens, "launches": iters * per_graph, "kernels": "kv_scatter_kernel, kv_store_chunks_kernel",
+           "l2": "16 rotating source buffers and destination block sets (128 MiB of sources)",
+           "timing": f"CUDA graph of {per_graph} launches replayed {iters} times (a launch is a few us of device "
+                     "work, less than the host's per-call cost, so eager launches would time the host)"}
     for name, fn, idx_bytes in (("write_prefill", scatter, tokens * 8 * 3),
                                 ("store_prefill", store, rows * 8 * (2 + blocks_per_row))):
         for _ in range(rot):
             fn()
-        ms = event_ms(fn, iters, device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(per_graph):
+                fn()
+        graph.replay()
+        ms = event_ms(graph.replay, iters, device) / per_graph
         nbytes = 2 * kv + idx_bytes
         res[name] = {"ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
                      "bytes_per_launch": nbytes}
@@ -559,7 +567,7 @@ def run_decode(args, spec: dict) -> None:
     sub_prefill = sub_scatter = None
     if not args.no_subrecords:
         sub_prefill = prefill_record(device, iters=200)
-        sub_scatter = scatter_record(device, iters=500)
+        sub_scatter = scatter_record(device, iters=20)
         torch.cuda.empty_cache()
     barrier()
 
@@ -925,6 +933,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c3", "c4"], default="c5")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch (small cases for ncu captures; not a bench line)")
+    ap.add_argument("--resident", type=int, default=None,
+                    help="override the resident layer pools (small cases for ncu captures; not a bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true", help="skip the prefill / scatter sub-records")
     ap.add_argument("--nccl-exchange", action="store_true",
@@ -946,6 +956,9 @@ def main() -> None:
     if args.batch is not None:
         spec["batch"] = args.batch
         spec["name"] += f"_batch{args.batch}"
+    if args.resident is not None:
+        spec["resident"] = args.resident
+        spec["name"] += f"_resident{args.resident}"
     if args.steps is None:
         args.steps = 3000 if spec["layers"] == 1 else 20
     if args.warmup is None:
