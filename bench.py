@@ -842,6 +842,22 @@ def c3_requests(num: int, seed: int, max_new: int, rate_per_s: float = 32.0, lo:
 C3_TOKEN_BUDGET = 2048
 
 
+def c3_phases(results) -> dict:
+    """Per phase: steps, mean / p95 of step ms, and the mean model / cache-management / scheduler ms."""
+    out = {}
+    for phase in ("prefill", "decode", "mixed"):
+        ev = [e for r in results for e in r.events if e.phase.value == phase]
+        if not ev:
+            continue
+        step = np.array([e.step_ms for e in ev])
+        out[phase] = {"steps": len(ev), "step_ms_mean": round(float(step.mean()), 4),
+                      "step_ms_p95": round(float(np.percentile(step, 95)), 4),
+                      "model_ms_mean": round(float(np.mean([e.model_ms for e in ev])), 4),
+                      "cache_ms_mean": round(float(np.mean([e.cache_management_ms for e in ev])), 4),
+                      "scheduler_ms_mean": round(float(np.mean([e.scheduler_ms for e in ev])), 4)}
+    return out
+
+
 def c3_latency(results) -> dict:
     """TTFT and inter-token latency percentiles (logical-clock ms) over all requests of all runs."""
     ttft, itl = [], []
@@ -908,6 +924,7 @@ def run_c3(args) -> None:
                        "policy": str(policy) if policy else "prefill-first",
                        "parallelism": f"kv-head partition x{world}" if world > 1 else "single GPU"},
             "latency_ms": c3_latency(results),
+            "phases": c3_phases(results),
             "engine": {"decode_tokens": dec_tokens, "decode_ms": dec_ms, "throughput_tok_s": out_tokens * 1000.0 / busy_ms,
                        "busy_ms": busy_ms, "prefill_steps": sum(r.schedule_metrics.num_prefill_steps for r in results),
                        "decode_steps": sum(r.schedule_metrics.num_decode_steps for r in results),
