@@ -954,6 +954,9 @@ def main() -> None:
                     help="override the workload's batch (small cases for ncu captures; not a bench line)")
     ap.add_argument("--resident", type=int, default=None,
                     help="override the resident layer pools (small cases for ncu captures; not a bench line)")
+    ap.add_argument("--shard", type=int, default=None,
+                    help="one GPU runs one rank's share of an N-way KV-head partition (its heads, every sequence; "
+                         "for captures and A/B tests of the per-rank shapes; not a bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-subrecords", action="store_true", help="skip the prefill / scatter sub-records")
     ap.add_argument("--nccl-exchange", action="store_true",
@@ -978,6 +981,12 @@ def main() -> None:
     if args.resident is not None:
         spec["resident"] = args.resident
         spec["name"] += f"_resident{args.resident}"
+    if args.shard is not None:
+        if spec["hkv"] % args.shard or args.gpus != 1:
+            raise SystemExit(f"--shard {args.shard} needs one GPU and a divisor of {spec['hkv']} KV heads")
+        spec["hq"] //= args.shard
+        spec["hkv"] //= args.shard
+        spec["name"] += f"_shard{args.shard}"
     if args.steps is None:
         args.steps = 3000 if spec["layers"] == 1 else 20
     if args.warmup is None:

@@ -2,9 +2,10 @@
 //
 // Split kernel (bf16/fp16, head_dim 64/128, block_size a multiple of 16, G <= 8):
 //   grid = (splits, kv-head blocks, batch); 4 consumer warps + 1 TMA producer warp per CTA.
-//   The producer walks the split's pages of the block table and stages each page of each KV head
-//   with non-multicast TMA tensor loads ([64 x 1 x block_size] boxes, 128-byte swizzle) into an
-//   NSTAGE-deep shared-memory ring guarded by full/empty mbarriers.  Each consumer warp owns one
+//   The producer warp walks the split's pages of the block table and stages each page of each KV
+//   head with non-multicast TMA tensor loads ([64 x 1 x block_size] boxes, 128-byte swizzle), one
+//   box per lane, into an NSTAGE-deep shared-memory ring guarded by full/empty mbarriers; each lane
+//   reads its next page's block id one stage ahead.  Each consumer warp owns one
 //   KV head: its G query heads sit in mma.sync A fragments (rows = query heads), QK^T and PV run as
 //   m16n8k16 tensor-core tiles with fp32 accumulation, and the online softmax (exp2 domain) keeps
 //   its row max/sum in registers with quad shuffles.  Each warp writes an unnormalised partial
@@ -79,36 +80,47 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
   bool aborted = false;
 
   if (warp == kConsumerWarps) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer: one box per lane ----------------
+    // A stage is TG pages x HB heads x {K, V} x kChunks boxes of [64 x 1 x BS]; lane L issues box L
+    // (page L / kBoxesPerPage).  Each lane loads the block id of its page one stage ahead, so the
+    // table reads overlap the wait for a free stage instead of sitting between the wait and the
+    // copies.
+    constexpr int kBoxesPerPage = HB * 2 * S::kChunks;
+    static_assert(TG * kBoxesPerPage <= 32, "one box per lane");
+    const int my_page = lane / kBoxesPerPage;
+    const int rem = lane - my_page * kBoxesPerPage;
+    const int hl = rem / (2 * S::kChunks);
+    const bool is_v = (rem / S::kChunks) & 1;
+    const int c = rem % S::kChunks;
+    const bool has_box = my_page < TG;
+    const int64_t* table = a.block_tables + b * a.table_stride;
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      const int64_t* table = a.block_tables + b * a.table_stride;
-      for (int it = 0; it < n_iter; ++it) {
-        const int st = it % NST;
-        if (it >= NST) mbar_wait(&empty_bar[st], ((it / NST) - 1) & 1, aborted);
-        uint8_t* stage = smem + st * S::kStageBytes;
-        const int64_t first = page_begin + (int64_t)it * TG;
-        const int npg = (int)min((int64_t)TG, page_end - first);
-        mbar_arrive_expect_tx(&full_bar[st], (uint32_t)(npg * HB * 2 * S::kHeadPageBytes));
-        for (int t = 0; t < npg; ++t) {
-          int64_t blk = table[first + t];
-          if (blk < 0 || blk >= a.num_blocks) {
-            record_status(MI_STATUS_BAD_BLOCK);
-            blk = a.num_blocks;  // outside the tensor map: TMA fills zeros
-          }
-          const int row0 = (int)(blk * BS);
-          for (int hl = 0; hl < HB; ++hl) {
-            const int h = head_block * HB + hl;
-            uint8_t* kdst = stage + ((t * HB + hl) * 2) * S::kHeadPageBytes;
-            uint8_t* vdst = kdst + S::kHeadPageBytes;
-#pragma unroll
-            for (int c = 0; c < S::kChunks; ++c) {
-              tma_load_3d(kdst + c * S::kChunkBytes, &tm_k, &full_bar[st], c * 64, h, row0);
-              tma_load_3d(vdst + c * S::kChunkBytes, &tm_v, &full_bar[st], c * 64, h, row0);
-            }
-          }
+    }
+    int64_t next_blk = 0;
+    if (has_box && page_begin + my_page < page_end) next_blk = table[page_begin + my_page];
+    for (int it = 0; it < n_iter; ++it) {
+      const int st = it % NST;
+      if (it >= NST) {
+        mbar_wait(&empty_bar[st], ((it / NST) - 1) & 1, aborted);
+        aborted = __any_sync(0xffffffffu, aborted);
+      }
+      const int64_t first = page_begin + (int64_t)it * TG;
+      const int npg = (int)min((int64_t)TG, page_end - first);
+      int64_t blk = next_blk;
+      const int64_t ahead = first + TG + my_page;  // this lane's page of the next stage
+      if (has_box && it + 1 < n_iter && ahead < page_end) next_blk = table[ahead];
+      if (lane == 0) mbar_arrive_expect_tx(&full_bar[st], (uint32_t)(npg * HB * 2 * S::kHeadPageBytes));
+      __syncwarp();
+      if (has_box && my_page < npg) {
+        if (blk < 0 || blk >= a.num_blocks) {
+          record_status(MI_STATUS_BAD_BLOCK);
+          blk = a.num_blocks;  // outside the tensor map: TMA fills zeros
         }
+        uint8_t* dst = smem + st * S::kStageBytes + ((my_page * HB + hl) * 2 + (is_v ? 1 : 0)) * S::kHeadPageBytes +
+                       c * S::kChunkBytes;
+        tma_load_3d(dst, is_v ? &tm_v : &tm_k, &full_bar[st], c * 64, head_block * HB + hl, (int)(blk * BS));
       }
     }
     return;
