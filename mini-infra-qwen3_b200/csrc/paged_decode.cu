@@ -321,6 +321,9 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeArgs a)
 // Barrier after an exchange: one warp, lane p signals and then waits for peer p.
 __global__ void __launch_bounds__(32) peer_barrier_kernel(const PeerBarrierArgs a) {
   const int p = threadIdx.x;
+  // Launched as a programmatic dependent of the combine kernel: placed while the combine drains,
+  // it waits here for the combine's completion (its peer stores performed) before signalling.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("fence.acq_rel.sys;" ::: "memory");
   const unsigned int e = *reinterpret_cast<volatile unsigned int*>(a.epoch) + 1u;
   if (p < a.world && p != a.rank) {
@@ -459,8 +462,16 @@ cudaError_t launch_split_t(const DecodeArgs& a, const DecodePlan& p, const CUten
 }  // namespace
 
 cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, cudaStream_t s) {
-  peer_barrier_kernel<<<1, 32, 0, s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, peer_barrier_kernel, a);
 }
 
 DecodePlan plan_decode(int64_t batch, int hq, int hkv, int head_dim, int64_t max_blocks, int block_size, int dtype) {
