@@ -60,7 +60,7 @@ METRIC = "paged decode KV-read GB/s"
 # DRAM read + write bytes per launch from committed ncu captures (the summaries under profiles/ give
 # the commands), with the algorithmic bytes of the captured launch, so that other sizes can be
 # scaled by the tokens processed (the traffic grows in proportion).
-NCU_DECODE = {"traffic": 1.129783e9 + 10.924544e6, "algorithmic": 1.129404160e9,
+NCU_DECODE = {"traffic": 1.129850e9 + 11.344896e6, "algorithmic": 1.129404160e9,
               "source": "ncu dram read+write of decode_split_kernel at the config-5 shape (batch 16, one "
                         "resident pool; profiles/decode_split_c5.md) / that launch's algorithmic bytes, "
                         "times this launch's algorithmic bytes"}
