@@ -368,3 +368,220 @@ def test_barrier_protocol_has_no_deadlock_or_phase_slip():
                 walkers, _, _ = split(shape, per_head)
                 for c, w in enumerate(walkers):
                     run_cta(w, seed=1000 * per_head + c, loader=loader)
+
+
+# ------------------------------------------------------------------------------------------------
+# The CTA-pair kernel (`prefill_tc2_kernel`): a unit's two row tiles live in the two CTAs of a
+# cluster; the leader (rank 0) issues M = 256 MMAs for both; each CTA stages half of every K tile
+# (its keys) and half of every V tile (its head dims); TMA bytes of both CTAs complete on the
+# leader's full barriers (the leader posts the expected bytes); commits arrive on both CTAs'
+# barriers; each CTA's softmax signals the leader's p_full / o_free (its 8 warps arrive in the
+# kernel, in lockstep per tile through the quadrant barriers, modelled as one arrival per CTA).
+# Each CTA holds two S/P buffers (tile c of the CTA's stream in buffer c % 2, one s_full / p_full
+# per buffer; S(i + 2) is issued right after PV(i), which reads P(i) from the same buffer), two Q
+# buffers (item m in m % 2; item m + 2's Q loads once every S of item m is done) and two O
+# buffers (item m in m % 2, one o_free per buffer).
+# ------------------------------------------------------------------------------------------------
+def run_pair(walk0, seed):
+    rnd = random.Random(seed)
+    bars = {}
+    for cta in range(2):
+        for i in range(K_STAGES):
+            bars[f"k_empty{i}@{cta}"] = Barrier(1)
+        for i in range(V_STAGES):
+            bars[f"v_empty{i}@{cta}"] = Barrier(1)
+        for b in range(2):
+            bars[f"s_full{b}@{cta}"] = Barrier(1)
+        bars[f"o_done@{cta}"] = Barrier(1)
+        bars[f"o_final@{cta}"] = Barrier(1)
+    # the leader's barriers that both CTAs feed
+    for i in range(K_STAGES):
+        bars[f"k_full{i}@0"] = Barrier(1)
+    for i in range(V_STAGES):
+        bars[f"v_full{i}@0"] = Barrier(1)
+    for b in range(2):  # per S buffer, per Q buffer, per O buffer
+        bars[f"p_full{b}@0"] = Barrier(2)
+        bars[f"q_full{b}@0"] = Barrier(1)
+        bars[f"o_free{b}@0"] = Barrier(2)
+    tx = {}  # pending transaction bytes per leader barrier phase: expected minus arrived
+    items = []
+    w = walk0.copy()
+    while (it := w.next()) is not None:
+        items.append(it)
+    n_tiles = sum(it["n"] for it in items)
+    if n_tiles == 0:
+        return
+    tile_items = [(it, i) for it in items for i in range(it["n"])]
+
+    def k_loader(cta):  # Q of items 0 and 1, then this CTA's half of every K tile, Q(m + 2) after item m
+        def load(bar, nbytes):
+            if cta == 0:
+                yield ("expect", bar, 2 * nbytes)
+            yield ("tma", bar, nbytes)
+        for m in range(min(2, len(items))):
+            yield from load(f"q_full{m % 2}@0", 32)
+        for j in range(min(n_tiles, K_STAGES)):
+            yield from load(f"k_full{j % K_STAGES}@0", 16)
+        m = 0
+        for j in range(n_tiles):
+            it, i = tile_items[j]
+            item_end = i + 1 == it["n"]
+            if item_end or j + K_STAGES < n_tiles:
+                yield ("wait", f"k_empty{j % K_STAGES}@{cta}", j // K_STAGES)
+            if item_end:
+                if m + 2 < len(items):  # into the buffer item m used: every S of item m is done
+                    yield ("check_s_done", cta, j + 1)
+                    yield from load(f"q_full{m % 2}@0", 32)
+                m += 1
+            if j + K_STAGES < n_tiles:
+                yield from load(f"k_full{(j + K_STAGES) % K_STAGES}@0", 16)
+        for j in range(max(0, n_tiles - K_STAGES), n_tiles):  # tail
+            yield ("wait", f"k_empty{j % K_STAGES}@{cta}", j // K_STAGES)
+
+    def v_loader(cta):
+        for j in range(n_tiles):
+            if j >= V_STAGES:
+                yield ("wait", f"v_empty{j % V_STAGES}@{cta}", j // V_STAGES - 1)
+            if cta == 0:
+                yield ("expect", f"v_full{j % V_STAGES}@0", 32)
+            yield ("tma", f"v_full{j % V_STAGES}@0", 16)
+        for j in range(max(0, n_tiles - V_STAGES), n_tiles):  # tail
+            yield ("wait", f"v_empty{j % V_STAGES}@{cta}", j // V_STAGES)
+
+    def mma():  # the leader's MMA warp
+        c, j0 = 0, 0
+        for k, it in enumerate(items):
+            n = it["n"]
+
+            def commit(name):
+                yield ("commit", name)  # multicast: both CTAs' copies
+
+            def issue_s(i):
+                yield ("s_issue", c + i)
+                yield from commit(f"s_full{(c + i) % 2}")
+                yield from commit(f"k_empty{(j0 + i) % K_STAGES}")
+
+            yield ("wait", f"q_full{k % 2}@0", k // 2)
+            yield ("wait", f"k_full{j0 % K_STAGES}@0", j0 // K_STAGES)
+            yield from issue_s(0)
+            if n > 1:
+                yield ("wait", f"k_full{(j0 + 1) % K_STAGES}@0", (j0 + 1) // K_STAGES)
+                yield from issue_s(1)
+            for i in range(n):
+                yield ("wait", f"p_full{(c + i) % 2}@0", (c + i) // 2)
+                yield ("wait", f"v_full{(j0 + i) % V_STAGES}@0", (j0 + i) // V_STAGES)
+                if i == 0 and k >= 2:
+                    yield ("wait", f"o_free{k % 2}@0", k // 2 - 1)
+                if i == 0:
+                    yield ("o_write", k)
+                yield ("pv_issue", c + i)
+                yield from commit("o_done")
+                yield from commit(f"v_empty{(j0 + i) % V_STAGES}")
+                if i + 1 == n:
+                    yield from commit("o_final")
+                if i + 2 < n:
+                    yield ("wait", f"k_full{(j0 + i + 2) % K_STAGES}@0", (j0 + i + 2) // K_STAGES)
+                    yield from issue_s(i + 2)
+            c += n
+            j0 += n
+
+    def softmax(cta):
+        c = 0
+        for k, it in enumerate(items):
+            n = it["n"]
+            for i in range(n):
+                yield ("wait", f"s_full{(c + i) % 2}@{cta}", (c + i) // 2)
+                yield ("s_read", c + i)
+                if i > 0 and rnd.random() < 0.3:
+                    yield ("wait", f"o_done@{cta}", c + i - 1)
+                yield ("arrive", f"p_full{(c + i) % 2}@0")
+            c += n
+            yield ("wait", f"o_final@{cta}", k)
+            yield ("o_read", cta, k)
+            yield ("arrive", f"o_free{k % 2}@0")
+
+    roles = {"k0": k_loader(0), "k1": k_loader(1), "v0": v_loader(0), "v1": v_loader(1), "mma": mma(),
+             "sm0": softmax(0), "sm1": softmax(1)}
+    blocked = dict.fromkeys(roles)
+    done, inflight, clock, mma_clock = set(), [], 0, 0
+    s_issued, pv_issued, o_read = [], set(), set()
+
+    def complete_tx(bar, nbytes):
+        tx[bar] = tx.get(bar, 0) - nbytes
+        if tx[bar] == 0 and bars[bar].pending == 0 and tx.get(bar + "#armed"):
+            tx[bar + "#armed"] = False
+            bars[bar].phases += 1
+
+    while len(done) < len(roles) or inflight:
+        progressed = False
+        order = list(roles)
+        rnd.shuffle(order)
+        for r in order:
+            while r not in done:
+                if blocked[r] is not None:
+                    _, bar, phase = blocked[r]
+                    seen = bars[bar].phases
+                    assert seen < phase + 2, f"{r} waits for phase {phase} of {bar}, already {seen} done"
+                    if seen < phase + 1:
+                        break
+                    blocked[r] = None
+                try:
+                    ev = next(roles[r])
+                except StopIteration:
+                    done.add(r)
+                    break
+                progressed = True
+                kind = ev[0]
+                if kind == "wait":
+                    blocked[r] = ev
+                elif kind == "expect":  # the leader's arrive.expect_tx: arms the phase
+                    tx[ev[1]] = tx.get(ev[1], 0) + ev[2]
+                    tx[ev[1] + "#armed"] = True
+                    if tx[ev[1]] == 0:
+                        tx[ev[1] + "#armed"] = False
+                        bars[ev[1]].phases += 1
+                elif kind == "tma":
+                    inflight.append((clock + rnd.randint(1, 60), "tx", ev[1], ev[2]))
+                elif kind == "check_s_done":
+                    assert len(s_issued) >= ev[2] and mma_clock <= clock + 1000, "Q reloaded early"
+                    done_s = bars[f"s_full0@{ev[1]}"].phases + bars[f"s_full1@{ev[1]}"].phases
+                    assert done_s >= ev[2], f"Q reloaded while {ev[2] - done_s} S MMAs were in flight"
+                elif kind == "s_issue":  # S(v) overwrites buffer v % 2: PV(v - 2) must have been issued
+                    assert ev[1] < 2 or (ev[1] - 2) in pv_issued, f"S({ev[1]}) issued before PV({ev[1] - 2})"
+                    s_issued.append(ev[1])
+                elif kind == "pv_issue":
+                    pv_issued.add(ev[1])
+                elif kind == "o_write":  # item k's first PV overwrites O buffer k % 2: item k - 2 read out
+                    assert ev[1] < 2 or {(0, ev[1] - 2), (1, ev[1] - 2)} <= o_read, f"O of item {ev[1] - 2} overwritten"
+                elif kind == "o_read":
+                    o_read.add((ev[1], ev[2]))
+                elif kind == "s_read":
+                    later = [v for v in s_issued if v > ev[1] and v % 2 == ev[1] % 2]
+                    assert ev[1] in s_issued and not later, f"softmax reads tile {ev[1]} over S {later}"
+                elif kind == "commit":  # both CTAs' copies, in issue order
+                    mma_clock = max(mma_clock, clock) + rnd.randint(0, 20)
+                    inflight.append((mma_clock, "arrive", f"{ev[1]}@0", 0))
+                    inflight.append((mma_clock, "arrive", f"{ev[1]}@1", 0))
+                elif kind == "arrive":
+                    bars[ev[1]].arrive()
+                if rnd.random() < 0.3:
+                    break
+        clock += 1
+        inflight.sort(key=lambda x: x[0])
+        while inflight and inflight[0][0] <= clock:
+            _, what, bar, nbytes = inflight.pop(0)
+            if what == "tx":
+                complete_tx(bar, nbytes)
+            else:
+                bars[bar].arrive()
+            progressed = True
+        assert progressed or inflight or len(done) == len(roles), \
+            f"deadlock: {[(r, blocked[r]) for r in roles if r not in done]}"
+
+
+def test_pair_barrier_protocol_has_no_deadlock_or_phase_slip():
+    for shape in _shapes():
+        for per_head in (9, 4, 1):
+            walkers, _, _ = split(shape, per_head)
+            for c, w in enumerate(walkers):
+                run_pair(w, seed=77 * per_head + c)
