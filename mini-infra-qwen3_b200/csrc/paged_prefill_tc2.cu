@@ -34,22 +34,25 @@
 namespace mi {
 namespace {
 
-constexpr int kP2SoftmaxWarps = 8;               // two per TMEM lane quadrant: each thread owns half a row
+constexpr int kP2SoftmaxWarps = 8;               // two sets of 4 (one warp per TMEM lane quadrant each)
 constexpr int kP2Threads = 32 * (3 + kP2SoftmaxWarps);
 constexpr int kP2VLoaderWarp = kFirstSoftmaxWarp + kP2SoftmaxWarps;
-constexpr int kP2Stages = 4;                      // depth of the K and of the V ring
+constexpr int kP2StagesK = 5;                     // depth of the K ring: K(i + 2) is needed with V(i)
+constexpr int kP2StagesV = 4;                     // depth of the V ring
 constexpr int kP2Half = 64;                       // keys (K) or head dims (V) a CTA stages per tile
 constexpr int kP2KBytes = kP2Half * 128 * 2;      // 16 KiB: 64 keys x 128 dims, two 8 KiB regions
 constexpr int kP2KRegion = kP2Half * 128;         // 8 KiB: 64 rows x 64 dims
 constexpr int kP2VBytes = kTcKv * kP2Half * 2;    // 16 KiB: 128 keys x 64 dims, one region
 constexpr int kP2OffQ = 0;                        // two Q buffers of 32 KiB
 constexpr int kP2OffK = kP2OffQ + 2 * kQBytes;
-constexpr int kP2OffV = kP2OffK + kP2Stages * kP2KBytes;
-constexpr int kP2OffBar = kP2OffV + kP2Stages * kP2VBytes;
-constexpr int kP2OffXchg = kP2OffBar + 256;       // row maxima [2][2][128] and row sums [2][128] of the halves
-constexpr int kP2SmemBytes = kP2OffXchg + 3 * 2 * kTcRows * 4 + 1024;  // + alignment slack (~196 KiB)
+constexpr int kP2OffV = kP2OffK + kP2StagesK * kP2KBytes;
+constexpr int kP2OffBar = kP2OffV + kP2StagesV * kP2VBytes;
+constexpr int kP2OffXchg = kP2OffBar + 256;       // row maxima and row sums [2 sets][128] for the merge
+constexpr int kP2SmemBytes = kP2OffXchg + 2 * 2 * kTcRows * 4 + 1024;  // + alignment slack (~195 KiB)
 static_assert(kP2SmemBytes <= 232448, "shared memory above the 227 KiB a CTA may use");
-constexpr uint32_t kP2TmemO = 256;                // S buffers at 0 and 128, O buffers at 256 and 384
+constexpr int kPolyEvery = 0;                     // every kPolyEvery-th exponential pair by exp2_poly (0: none)
+constexpr int kP2HalfKeys = 64;                   // keys of a half tile: one S buffer, N of its S MMA
+constexpr uint32_t kP2TmemO = 256;                // S buffers 2h + k % 2 at 64 (2h + k % 2); O_0 / O_1 at 256 / 384
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -70,6 +73,25 @@ __device__ __forceinline__ void cluster_sync_all() {
 // by the tcgen05 fences around it).
 __device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2^x on the FMA and integer pipes, for the share of the softmax exponentials taken off the
+// MUFU unit (whose rate, 16 results per clock per SM, otherwise sets the softmax time).  Method:
+// Cody-Waite range reduction x = j + f, j = round(x) (adding 1.5 * 2^23 rounds to an integer
+// held in the low mantissa bits), f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose
+// coefficients were fitted to the relative error on [-0.5, 0.5] by iteratively reweighted least
+// squares (Lawson's algorithm); 2^j by adding j to the exponent field.  Maximum relative error
+// 7.5e-5 in fp32 (P is rounded to 16 bits after, relative step 2^-8).  x is clamped at -125
+// (-inf from masking included) so the exponent stays normal: 2^-125 stands in for 0, which no
+// row with a visible key can tell from 0.  x <= 8 here (the rescale threshold).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;  // 1.5 * 2^23: round to nearest
+  const float j = t - 12582912.f;
+  const float f = x - j;
+  float p = fmaf(0.05517132f, f, 0.24261054f);
+  p = fmaf(p, f, 0.69326097f);
+  p = fmaf(p, f, 0.99992812f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 // Named barrier of the two softmax warps that share a TMEM lane quadrant.
 __device__ __forceinline__ void pair_sync(uint32_t id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
@@ -115,28 +137,32 @@ __device__ __forceinline__ void tma_pair_4d(void* dst, const CUtensorMap* map, u
 }
 
 // One loader warp's stream of its CTA's K or V halves over the cluster's items.  Lane q holds the
-// block id of page q of the next tile's part this CTA stages (loaded one tile ahead); a tile goes
-// out as one TMA box per lane.
+// block id of page q of the part of a tile this CTA stages, for the next kAhead tiles (a FIFO in
+// registers: the table reads are issued kAhead tiles before their TMA boxes, so a loader that
+// finds its ring stages free issues back to back instead of once per global-load latency); a
+// tile goes out as one TMA box per lane.
 //   K half: keys [128 t + 64 rank, + 64): 64 / bs pages x 2 dim halves (history), or 2 boxes of
 //           64 tokens x 64 dims (chunk); stage = two 8 KiB regions (dims 0-63, 64-127) of 64 rows.
 //   V half: all 128 keys, dims [64 rank, + 64): 128 / bs pages (history) or 2 boxes of 64 tokens
 //           (chunk); stage = one 16 KiB region of 128 rows.
+constexpr int64_t kNoPage = INT64_MIN;  // the lane's page is not history: the box reads zeros
 struct PairLoader {
-  TcCursor c;
-  int64_t pend;
-  bool pend_valid;
+  TcCursor c;  // the next tile to issue
+  TcCursor f;  // the next tile to read block ids for
+  int64_t p0, p1, p2, p3;  // block ids of tiles c, c + 1, c + 2, c + 3 (this lane's page)
   int lane, shift, rank;
   bool is_v;
   __device__ __forceinline__ int pages(const PrefillArgs& a) const { return (is_v ? kTcKv : kP2Half) / a.block_size; }
-  __device__ __forceinline__ void fetch(const PrefillArgs& a) {
-    pend_valid = false;
-    if (!c.valid || lane >= pages(a)) return;
-    const int t = c.it.t_begin + c.i;
-    const int pos0 = t * kTcKv + (is_v ? 0 : rank * kP2Half) + lane * a.block_size;
-    if (t < c.it.u.row.hist_tiles && pos0 < c.it.u.row.start) {
-      pend = a.block_tables[c.it.u.b * a.table_stride + (pos0 >> shift)];
-      pend_valid = true;
+  __device__ __forceinline__ int64_t fetch(const PrefillArgs& a) {
+    int64_t id = kNoPage;
+    if (f.valid && lane < pages(a)) {
+      const int t = f.it.t_begin + f.i;
+      const int pos0 = t * kTcKv + (is_v ? 0 : rank * kP2Half) + lane * a.block_size;
+      if (t < f.it.u.row.hist_tiles && pos0 < f.it.u.row.start)
+        id = a.block_tables[f.it.u.b * a.table_stride + (pos0 >> shift)];
     }
+    if (f.valid) f.advance(a);
+    return id;
   }
   __device__ __forceinline__ void init(const TcWalker& w0, const PrefillArgs& a, int lane_, int shift_, int rank_,
                                        bool is_v_) {
@@ -145,15 +171,19 @@ struct PairLoader {
     rank = rank_;
     is_v = is_v_;
     c.init(w0, a);
-    fetch(a);
+    f.init(w0, a);
+    p0 = fetch(a);
+    p1 = fetch(a);
+    p2 = fetch(a);
+    p3 = fetch(a);
   }
   __device__ __forceinline__ void issue(const PrefillArgs& a, const CUtensorMap& pool_map, const CUtensorMap& chunk_map,
                                         uint8_t* dst, uint64_t* full_local, uint32_t full_leader) {
     const int np = pages(a);
     int my_row = (int)(a.num_blocks * a.block_size);  // past the pool: TMA reads zeros
-    if (lane < np && pend_valid) {
-      if (pend < 0 || pend >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
-      else my_row = (int)(pend * a.block_size);
+    if (lane < np && p0 != kNoPage) {
+      if (p0 < 0 || p0 >= a.num_blocks) record_status(MI_STATUS_BAD_BLOCK);
+      else my_row = (int)(p0 * a.block_size);
     }
     const int t = c.it.t_begin + c.i;
     const bool hist = t < c.it.u.row.hist_tiles;
@@ -178,7 +208,10 @@ struct PairLoader {
       }
     }
     c.advance(a);
-    fetch(a);
+    p0 = p1;
+    p1 = p2;
+    p2 = p3;
+    p3 = fetch(a);
   }
 };
 
@@ -193,19 +226,19 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kP2OffBar);
   // leader-side barriers (both CTAs' TMA bytes, or one arrival per softmax warp of both CTAs)
   uint64_t* q_full = bars + 0;                 // [2] per Q buffer
-  uint64_t* k_full = q_full + 2;               // [kP2Stages]
-  uint64_t* v_full = k_full + kP2Stages;       // [kP2Stages]
-  uint64_t* p_full = v_full + kP2Stages;       // [2] per S buffer
-  uint64_t* o_free = p_full + 2;               // [2] per O buffer
+  uint64_t* k_full = q_full + 2;               // [kP2StagesK]
+  uint64_t* v_full = k_full + kP2StagesK;      // [kP2StagesV]
+  uint64_t* p_full = v_full + kP2StagesV;      // [4] per S buffer 2h + k % 2
+  uint64_t* o_free = p_full + 4;               // both O accumulators read out
   // barriers of each CTA, arrived on by the leader's multicast commits
-  uint64_t* k_empty = o_free + 2;              // [kP2Stages]
-  uint64_t* v_empty = k_empty + kP2Stages;     // [kP2Stages]
-  uint64_t* s_full = v_empty + kP2Stages;      // [2]
-  uint64_t* o_done = s_full + 2;
-  uint64_t* o_final = o_done + 1;
+  uint64_t* k_empty = o_free + 1;              // [kP2StagesK]
+  uint64_t* v_empty = k_empty + kP2StagesK;    // [kP2StagesV]
+  uint64_t* s_full = v_empty + kP2StagesV;     // [4] per S buffer
+  uint64_t* o_done = s_full + 4;               // [2] per set: one phase per PV into O_set
+  uint64_t* o_final = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
-  float* xmax = reinterpret_cast<float*>(smem + kP2OffXchg);  // [2 tile parity][2 halves][128 rows]
-  float* xsum = xmax + 2 * 2 * kTcRows;                       // [2 halves][128 rows]
+  float* xmax = reinterpret_cast<float*>(smem + kP2OffXchg);  // [2 sets][128 rows]
+  float* xsum = xmax + 2 * kTcRows;                           // [2 sets][128 rows]
 
   asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent of the previous kernel
   const int tid = threadIdx.x;
@@ -249,19 +282,23 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
   if (n_tiles == 0) return;  // uniform for the cluster: both CTAs walk the same items
 
   if (tid == 0) {
-    for (int i = 0; i < kP2Stages; ++i) {
+    for (int i = 0; i < kP2StagesK; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kP2StagesV; ++i) {
+      mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
+    }
+    for (int b = 0; b < 4; ++b) {
+      mbar_init(&p_full[b], 2 * 4);  // the 4 warps of one set, in both CTAs
+      mbar_init(&s_full[b], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&q_full[b], 1);
-      mbar_init(&p_full[b], 2 * kP2SoftmaxWarps);
-      mbar_init(&o_free[b], 2 * kP2SoftmaxWarps);
-      mbar_init(&s_full[b], 1);
+      mbar_init(&o_done[b], 1);
     }
-    mbar_init(o_done, 1);
+    mbar_init(o_free, 2 * kP2SoftmaxWarps);
     mbar_init(o_final, 1);
     fence_mbar_init();
   }
@@ -304,14 +341,15 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
                     it.h * G, it.u.row.first + tok0, it.u.b);
       }
     };
+    const int stages = is_v ? kP2StagesV : kP2StagesK;
     auto issue = [&](int64_t j) {
-      const int st = (int)(j % kP2Stages);
+      const int st = (int)(j % stages);
       ld.issue(a, is_v ? maps.v_pool : maps.k_pool, is_v ? maps.v_chunk : maps.k_chunk, ring + st * stage_bytes,
                &full[st], mapa_rank(&full[st], 0));
     };
     if (is_v) {
       for (int64_t j = 0; j < n_tiles; ++j) {
-        if (j >= kP2Stages) mbar_wait_warp(&empty[j % kP2Stages], ((j / kP2Stages) - 1) & 1, aborted);
+        if (j >= kP2StagesV) mbar_wait_warp(&empty[j % kP2StagesV], ((j / kP2StagesV) - 1) & 1, aborted);
         issue(j);
       }
     } else {
@@ -324,77 +362,87 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
       for (int k = 0; k < 2 && wq.next(a, qi); ++k) load_q(qi, nq++);
       TcCursor cq;
       cq.init(walk0, a);
-      for (int64_t j = 0; j < min(n_tiles, (int64_t)kP2Stages); ++j) issue(j);
+      for (int64_t j = 0; j < min(n_tiles, (int64_t)kP2StagesK); ++j) issue(j);
       for (int64_t j = 0; j < n_tiles; ++j) {
         const bool item_end = cq.last_of_item();
         cq.advance(a);
-        if (item_end || j + kP2Stages < n_tiles)
-          mbar_wait_warp(&empty[j % kP2Stages], (j / kP2Stages) & 1, aborted);
+        if (item_end || j + kP2StagesK < n_tiles)
+          mbar_wait_warp(&empty[j % kP2StagesK], (j / kP2StagesK) & 1, aborted);
         if (item_end && wq.next(a, qi)) load_q(qi, nq++);
-        if (j + kP2Stages < n_tiles) issue(j + kP2Stages);
+        if (j + kP2StagesK < n_tiles) issue(j + kP2StagesK);
       }
     }
     // tail: every commit that frees a stage of this CTA has landed before the CTA may exit
-    for (int64_t j = max((int64_t)0, n_tiles - kP2Stages); j < n_tiles; ++j)
-      mbar_wait_warp(&empty[j % kP2Stages], (j / kP2Stages) & 1, aborted);
+    for (int64_t j = max((int64_t)0, n_tiles - stages); j < n_tiles; ++j)
+      mbar_wait_warp(&empty[j % stages], (j / stages) & 1, aborted);
   } else if (warp == kMmaWarp) {
     if (rank == 0) {
       // ---------------- MMA issuer (leader): M = 256 over both CTAs' row tiles ----------------
+      // Per tile k of the stream and half h: S_h(k) = Q K_h(k)^T (N = 64 keys: 32 from each CTA's
+      // K piece h) into buffer 2h + k % 2, O_h += P_h(k) V_h(k) (K = the same 64 keys).
       constexpr bool kBf16 = !std::is_same<T, __half>::value;
-      const uint32_t idesc_qk = idesc_f16(kBf16, false, 2 * kTcRows, kTcKv);
+      const uint32_t idesc_qk = idesc_f16(kBf16, false, 2 * kTcRows, kP2HalfKeys);
       const uint32_t idesc_pv = idesc_f16(kBf16, true, 2 * kTcRows, kTcDim);
       const uint64_t dk = desc_kmajor(sbase + kP2OffK);
       const uint64_t dv = desc_mnmajor(sbase + kP2OffV);
       TcWalker w = walk0;
       TcItem it;
       int64_t j0 = 0;  // the cluster's tile index of the item's first tile
-      int c = 0;       // tiles so far: tile c of the stream uses S buffer c % 2
-      int items = 0;   // item m uses Q buffer m % 2 and O buffer m % 2
+      int c = 0;       // tiles so far (tile k of the stream uses S buffers 2h + k % 2)
+      int items = 0;   // item m uses Q buffer m % 2
       while (w.next(a, it)) {
         const int n = it.n;
         const int qb = items & 1;
         const uint64_t dq = desc_kmajor(sbase + kP2OffQ + qb * kQBytes);
-        const uint32_t o_tmem = tmem + kP2TmemO + (uint32_t)qb * 128;
-        auto issue_s = [&](int i) {  // S(i) = Q K(i)^T (both row tiles) into buffer (c + i) % 2
+        auto issue_s = [&](int i, int h) {  // S_h(i) into buffer 2h + (c + i) % 2
           const int64_t jj = j0 + i;
-          const int ks = (int)(jj % kP2Stages);
-          const int b = (c + i) & 1;
+          const int ks = (int)(jj % kP2StagesK);
+          const int bb = 2 * h + ((c + i) & 1);
           tc_fence_after();
-          const uint64_t dks = dk + (uint64_t)((ks * kP2KBytes) >> 4);
+          // this CTA's piece h: rows [32 h, 32 h + 32) of both 64-dimension regions of the K stage
+          const uint64_t dks = dk + (uint64_t)((ks * kP2KBytes + h * 32 * 128) >> 4);
 #pragma unroll
           for (int s = 0; s < kTcDim / 16; ++s)
-            umma_pair_ss(tmem + b * 128, dq + (uint64_t)(((s >> 2) * kQRegion + (s & 3) * 32) >> 4),
+            umma_pair_ss(tmem + bb * kP2HalfKeys, dq + (uint64_t)(((s >> 2) * kQRegion + (s & 3) * 32) >> 4),
                          dks + (uint64_t)(((s >> 2) * kP2KRegion + (s & 3) * 32) >> 4), idesc_qk, s > 0 ? 1u : 0u);
-          umma_commit_pair(&s_full[b]);
-          umma_commit_pair(&k_empty[ks]);
+          umma_commit_pair(&s_full[bb]);
+          if (h == 1) umma_commit_pair(&k_empty[ks]);  // the stage's last S
         };
         mbar_wait_warp(&q_full[qb], (items >> 1) & 1, aborted);
-        mbar_wait_warp(&k_full[j0 % kP2Stages], (j0 / kP2Stages) & 1, aborted);
-        issue_s(0);
-        if (n > 1) {
-          mbar_wait_warp(&k_full[(j0 + 1) % kP2Stages], ((j0 + 1) / kP2Stages) & 1, aborted);
-          issue_s(1);
+        for (int i = 0; i < min(n, 2); ++i) {
+          mbar_wait_warp(&k_full[(j0 + i) % kP2StagesK], ((j0 + i) / kP2StagesK) & 1, aborted);
+          issue_s(i, 0);
+          issue_s(i, 1);
         }
         for (int i = 0; i < n; ++i) {
-          const int b = (c + i) & 1;
+          const int k = c + i;
           const int64_t jj = j0 + i;
-          mbar_wait_warp(&p_full[b], ((c + i) >> 1) & 1, aborted);  // both CTAs' P(i) in TMEM
-          mbar_wait_warp(&v_full[jj % kP2Stages], (jj / kP2Stages) & 1, aborted);
-          // O buffer qb was last read out by the epilogue of item items - 2
-          if (i == 0 && items >= 2) mbar_wait_warp(&o_free[qb], ((items >> 1) - 1) & 1, aborted);
-          tc_fence_after();
-          const int vs = (int)(jj % kP2Stages);
+          const int vs = (int)(jj % kP2StagesV);
+          mbar_wait_warp(&v_full[vs], (jj / kP2StagesV) & 1, aborted);
+          // both O accumulators read out by the previous item's epilogue
+          if (i == 0 && items > 0) mbar_wait_warp(o_free, (items - 1) & 1, aborted);
           const uint64_t dvs = dv + (uint64_t)((vs * kP2VBytes) >> 4);
 #pragma unroll
-          for (int s = 0; s < kTcKv / 16; ++s)  // P: 16-bit pairs in the first 64 columns of buffer b
-            umma_pair_ts(o_tmem, tmem + b * 128 + s * 8, dvs + (uint64_t)((s * 2048) >> 4), idesc_pv,
-                         (i > 0 || s > 0) ? 1u : 0u);
-          umma_commit_pair(o_done);
-          umma_commit_pair(&v_empty[vs]);
-          if (i + 1 == n) umma_commit_pair(o_final);
-          if (i + 2 < n) {
-            mbar_wait_warp(&k_full[(jj + 2) % kP2Stages], ((jj + 2) / kP2Stages) & 1, aborted);
-            issue_s(i + 2);
+          for (int h = 0; h < 2; ++h) {
+            const int bb = 2 * h + (k & 1);
+            mbar_wait_warp(&p_full[bb], (k >> 1) & 1, aborted);  // set h's P(k) in both CTAs' TMEM
+            tc_fence_after();
+            // k-step s covers S_h columns [16 s, 16 s + 16): keys 64 (s / 2) + 32 h + 16 (s % 2) + [0, 16)
+#pragma unroll
+            for (int s = 0; s < kP2HalfKeys / 16; ++s)
+              umma_pair_ts(tmem + kP2TmemO + h * 128, tmem + bb * kP2HalfKeys + s * 8,
+                           dvs + (uint64_t)((((s >> 1) * 64 + 32 * h + (s & 1) * 16) * 128) >> 4), idesc_pv,
+                           (i > 0 || s > 0) ? 1u : 0u);
+            umma_commit_pair(&o_done[h]);
+            if (h == 1) {
+              umma_commit_pair(&v_empty[vs]);
+              if (i + 1 == n) umma_commit_pair(o_final);
+            }
+            if (i + 2 < n) {
+              if (h == 0)
+                mbar_wait_warp(&k_full[(jj + 2) % kP2StagesK], ((jj + 2) / kP2StagesK) & 1, aborted);
+              issue_s(i + 2, h);
+            }
           }
         }
         c += n;
@@ -403,19 +451,22 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
       }
     }
   } else if (warp >= kFirstSoftmaxWarp && warp < kFirstSoftmaxWarp + kP2SoftmaxWarps) {
-    // ------- softmax: thread <-> (row = TMEM lane of this CTA's row tile, half of the columns) -------
+    // ------- softmax set `set` (= h): half h of every tile, i.e. S_h columns j <-> tile keys
+    // 64 (j / 32) + 32 h + j % 32; thread <-> row (TMEM lane) of this CTA's row tile; running max /
+    // sum and O accumulator O_h of its own, merged with the other set's in the item's epilogue ----
     const int g = (int)rank;
-    const int hw = (warp - kFirstSoftmaxWarp) >> 2;  // this thread's 64 of the tile's 128 key columns
+    const int set = (warp - kFirstSoftmaxWarp) >> 2;
     const int quad = warp & 3;                        // TMEM lane quadrant this warp may access
     const int r = quad * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    const uint32_t bar_id = 1 + (uint32_t)quad;       // the two warps of one quadrant (one per half)
+    const uint32_t bar_id = 1 + (uint32_t)quad;       // the two warps of one quadrant (one per set)
     const float scale = a.scale_log2;
-    const uint32_t p_full_leader[2] = {mapa_rank(&p_full[0], 0), mapa_rank(&p_full[1], 0)};
-    const uint32_t o_free_leader[2] = {mapa_rank(&o_free[0], 0), mapa_rank(&o_free[1], 0)};
+    const uint32_t o_addr = tmem + kP2TmemO + (uint32_t)set * 128 + lane_base;
+    const uint32_t p_full_leader[2] = {mapa_rank(&p_full[2 * set], 0), mapa_rank(&p_full[2 * set + 1], 0)};
+    const uint32_t o_free_leader = mapa_rank(o_free, 0);
     TcWalker w = walk0;
     TcItem it;
-    int c = 0, items = 0;
+    int c = 0, items = 0;  // tiles of the stream (barrier phases), items
     while (w.next(a, it)) {
       const TcPair& u = it.u;
       const int n = it.n;  // every tile of the unit's union range (tiles past this row tile's range are masked)
@@ -424,11 +475,11 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
       const bool row_valid = my_tok < (g ? u.tok_end[1] : u.tok_end[0]);
       const int start = u.row.start;
       const int hist_tiles = u.row.hist_tiles;
-      const uint32_t o_col = kP2TmemO + (uint32_t)(items & 1) * 128 + (uint32_t)hw * 64;
       float m_ref = -INFINITY, l_run = 0.f;
       for (int i = 0; i < n; ++i) {
         const int t = it.t_begin + i;
-        const int b = (c + i) & 1;
+        const int k = c + i;
+        const int par = k & 1;
         bool full;
         int lim;
         if (t < hist_tiles) {
@@ -439,22 +490,22 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
           lim = row_valid ? (int)my_tok + 1 - k0 : 0;
           full = k0 + kTcKv <= (int)my_tok0 + 1;
         }
-        lim -= hw * 64;  // in this half's columns
+        lim -= 32 * set;  // column j of chunk cc is visible while 64 cc + j < lim
+        const uint32_t s_addr = tmem + (uint32_t)(2 * set + par) * kP2HalfKeys + lane_base;
         bool ab = aborted;
-        mbar_wait(&s_full[b], ((c + i) >> 1) & 1, ab);
+        mbar_wait(&s_full[2 * set + par], (k >> 1) & 1, ab);
         aborted = ab;
         tc_fence_after();
-        const uint32_t s_addr = tmem + b * 128 + lane_base;
         uint32_t sr[2][32];
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) tmem_ld32_async(s_addr + hw * 64 + cc * 32, sr[cc]);
+        for (int cc = 0; cc < 2; ++cc) tmem_ld32_async(s_addr + cc * 32, sr[cc]);
         tmem_wait_ld();
         if (!full) {
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              if (cc * 32 + e >= lim) sr[cc][e] = 0xff800000u;
+              if (cc * 64 + e >= lim) sr[cc][e] = 0xff800000u;
           }
         }
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -464,16 +515,7 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
           for (int e = 0; e < 32; e += 2)
             mx[(e >> 1) & 3] = fmax3(mx[(e >> 1) & 3], __uint_as_float(sr[cc][e]), __uint_as_float(sr[cc][e + 1]));
         }
-        // the row maximum over both halves: exchanged through shared memory (buffer by tile
-        // parity: a half writes tile i + 2's value only after the pair barrier of tile i + 1,
-        // which its partner reaches after reading tile i's); the barrier also orders both
-        // halves' S loads before either's P stores, which overwrite S columns of the other half
-        const int par = (c + i) & 1;
-        xmax[(par * 2 + hw) * kTcRows + r] = fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]);
-        tc_fence_before();
-        pair_sync(bar_id);
-        tc_fence_after();
-        const float tile_max = fmaxf(xmax[(par * 2 + hw) * kTcRows + r], xmax[(par * 2 + (hw ^ 1)) * kTcRows + r]) * scale;
+        const float tile_max = fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]) * scale;
         const float m_new = fmaxf(m_ref, tile_max);
         const bool need = i > 0 && m_ref != -INFINITY && m_new > m_ref + kRescaleLog2;
         const float alpha = need ? fast_exp2(m_ref - m_new) : 1.f;
@@ -490,87 +532,112 @@ __global__ void __launch_bounds__(kP2Threads, 1) prefill_tc2_kernel(const Prefil
           uint32_t pw[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[cc][2 * j]), scale, neg_m));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[cc][2 * j + 1]), scale, neg_m));
+            const float x0 = fmaf(__uint_as_float(sr[cc][2 * j]), scale, neg_m);
+            const float x1 = fmaf(__uint_as_float(sr[cc][2 * j + 1]), scale, neg_m);
+            // kPolyEvery-th pairs on the FMA pipe, the rest on MUFU
+            const bool poly = kPolyEvery > 0 && (j % kPolyEvery) == kPolyEvery - 1;
+            const float p0 = poly ? exp2_poly(x0) : fast_exp2(x0);
+            const float p1 = poly ? exp2_poly(x1) : fast_exp2(x1);
             ps[j & 3] += p0 + p1;
             pw[j] = pack2<T>(p0, p1);
           }
-          tmem_st16_async(s_addr + hw * 32 + cc * 16, pw);  // keys 64 hw + 32 cc .. + 31 as 16-bit pairs
+          tmem_st16_async(s_addr + cc * 16, pw);  // P over the buffer's first 32 columns
         }
         l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-        if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access; the partner warp agrees
+        if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access
           bool ab2 = aborted;
-          mbar_wait(o_done, (c + i - 1) & 1, ab2);  // PV(i-1) finished writing O
+          mbar_wait(&o_done[set], (k - 1) & 1, ab2);  // PV_h(k - 1) finished writing O_h
           aborted = ab2;
           tc_fence_after();
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
+          for (int cc = 0; cc < 4; ++cc) {
             float ov[32];
-            tmem_ld32(tmem + o_col + lane_base + cc * 32, ov);
+            tmem_ld32(o_addr + cc * 32, ov);
 #pragma unroll
             for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-            tmem_st32(tmem + o_col + lane_base + cc * 32, ov);
+            tmem_st32(o_addr + cc * 32, ov);
           }
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) remote_arrive(p_full_leader[b]);
+        if (lane == 0) remote_arrive(p_full_leader[par]);
       }
       c += n;
-      // ---- epilogue of the item: the row sum over both halves, O out of TMEM (then free for
-      // item + 2), global stores of this half's 64 columns
+      // ---- epilogue of the item: merge the two sets' (m, l, O) per row; set s stores output
+      // columns [64 s, 64 s + 64)
       {
         bool ab = aborted;
         mbar_wait(o_final, items & 1, ab);
         aborted = ab;
       }
       tc_fence_after();
-      xsum[hw * kTcRows + r] = l_run;
+      xmax[set * kTcRows + r] = m_ref;
+      xsum[set * kTcRows + r] = l_run;
       pair_sync(bar_id);
-      const float l_all = l_run + xsum[(hw ^ 1) * kTcRows + r];
+      const float m0 = xmax[r], m1 = xmax[kTcRows + r];
+      const float m = fmaxf(m0, m1);
+      // a set with nothing visible for this row (or no tile in the item) contributes nothing: its
+      // O columns are not read into the sum (they may hold an earlier item's values)
+      const float a0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
+      const float a1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
+      const float l_all = xsum[r] * a0 + xsum[kTcRows + r] * a1;
       const float inv = l_all > 0.f ? 1.f / l_all : 0.f;
-      uint32_t ov[2][32];
+      uint32_t o0[2][32], o1[2][32];
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) tmem_ld32_async(tmem + o_col + lane_base + cc * 32, ov[cc]);
+      for (int cc = 0; cc < 2; ++cc) {
+        tmem_ld32_async(tmem + kP2TmemO + lane_base + set * 64 + cc * 32, o0[cc]);
+        tmem_ld32_async(tmem + kP2TmemO + 128 + lane_base + set * 64 + cc * 32, o1[cc]);
+      }
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) remote_arrive(o_free_leader[items & 1]);
+      if (lane == 0) remote_arrive(o_free_leader);
+      float ov[2][32];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          ov[cc][e] = (a0 != 0.f ? __uint_as_float(o0[cc][e]) * a0 : 0.f) +
+                      (a1 != 0.f ? __uint_as_float(o1[cc][e]) * a1 : 0.f);
+      }
       const int64_t part = (int64_t)it.slot * kPair + g;
       if (it.slot < 0) {
         if (row_valid) {
           T* dst = out + (u.b * a.padded_len + u.row.first + my_tok) * row_elems + (int64_t)(it.h * G + r % G) * kTcDim +
-                   hw * 64;
+                   set * 64;
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
-              const uint32_t* f = &ov[cc][v * 8];
+              const float* f = &ov[cc][v * 8];
               uint4 pk;
-              pk.x = pack2<T>(__uint_as_float(f[0]) * inv, __uint_as_float(f[1]) * inv);
-              pk.y = pack2<T>(__uint_as_float(f[2]) * inv, __uint_as_float(f[3]) * inv);
-              pk.z = pack2<T>(__uint_as_float(f[4]) * inv, __uint_as_float(f[5]) * inv);
-              pk.w = pack2<T>(__uint_as_float(f[6]) * inv, __uint_as_float(f[7]) * inv);
+              pk.x = pack2<T>(f[0] * inv, f[1] * inv);
+              pk.y = pack2<T>(f[2] * inv, f[3] * inv);
+              pk.z = pack2<T>(f[4] * inv, f[5] * inv);
+              pk.w = pack2<T>(f[6] * inv, f[7] * inv);
               *reinterpret_cast<uint4*>(dst + cc * 32 + v * 8) = pk;
             }
           }
         }
       } else {
-        float* po = ws_o + (part * kTcRows + r) * kTcDim + hw * 64;
+        float* po = ws_o + (part * kTcRows + r) * kTcDim + set * 64;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
           for (int v = 0; v < 8; ++v)
-            *reinterpret_cast<uint4*>(po + cc * 32 + v * 4) =
-                make_uint4(ov[cc][v * 4], ov[cc][v * 4 + 1], ov[cc][v * 4 + 2], ov[cc][v * 4 + 3]);
+            *reinterpret_cast<float4*>(po + cc * 32 + v * 4) =
+                make_float4(ov[cc][v * 4], ov[cc][v * 4 + 1], ov[cc][v * 4 + 2], ov[cc][v * 4 + 3]);
         }
-        if (hw == 0) *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m_ref, l_all);
+        if (set == 0) *reinterpret_cast<float2*>(ws_ml + (part * kTcRows + r) * 2) = make_float2(m, l_all);
       }
+      // the exchange words are rewritten at the next epilogue, after at least one more pair
+      // barrier; the next item's first pair barrier is this one's partner's too
+      pair_sync(bar_id);
       ++items;
     }
-    // tail: the last PV's o_done arrival (committed before o_final) has landed as well
-    mbar_wait(o_done, (c - 1) & 1, aborted);
+    // tail: this set's last o_done arrival (committed before o_final) has landed as well
+    mbar_wait(&o_done[set], (c - 1) & 1, aborted);
   }
   tc_fence_before();
   cluster_sync_all();  // every MMA into either CTA's TMEM has been waited for
