@@ -214,16 +214,6 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
                      size_t workspace_bytes, int dtype, void* stream);
 
 /*
- * mi_set_prefill_variant — which tensor-core form mi_paged_prefill launches (process-wide, read at
- * each launch): 0 (default) = CTA pairs (two SMs per work unit, one 256-row MMA over both of the
- * unit's row tiles, each SM staging half of every K/V tile) wherever tensor maps apply (block size
- * 16/32/64) and two CTAs can be co-scheduled; 1 = one CTA per unit.  Both give the same results
- * to within fp32 summation order.  Returns the previous setting, or MI_ERR_INVALID.  Not part of
- * the reference interface: a switch for comparing the two forms.
- */
-int mi_set_prefill_variant(int variant);
-
-/*
  * mi_decode_rows — the packed decode-step inputs of PagedRunner.prepare_decode_inputs
  * (worker/paged_runner.py:138-166: per sequence [token, position, slot, position + 1, block table
  * null-padded]) built on the device from a device mirror of the block tables, so a step uploads

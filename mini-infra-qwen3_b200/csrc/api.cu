@@ -536,9 +536,4 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
   return e == cudaSuccess ? MI_OK : cuda_fail(e, "mi_paged_prefill launch");
 }
 
-int mi_set_prefill_variant(int variant) {
-  if (variant != 0 && variant != 1) return fail(MI_ERR_INVALID, "prefill variant must be 0 or 1, got %d", variant);
-  return mi::set_prefill_variant(variant);
-}
-
 }  // extern "C"

@@ -160,14 +160,6 @@ size_t prefill_tc_workspace_bytes(const PrefillArgs& a);
 bool prefill_tc_tma_block_size(int block_size);
 cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, const PrefillMaps* maps, int dtype,
                                     cudaStream_t s);
-// CTA-pair form of the tcgen05 variant (paged_prefill_tc2.cu): clusters of two CTAs issue M = 256
-// MMAs over both row tiles of a unit.  prefill_tc2_clusters gives the clusters to launch (a multiple
-// of hkv), 0 where the form does not apply (no tensor maps, block size above 64, no room for a pair).
-int prefill_tc2_clusters(const PrefillArgs& a, const PrefillMaps* maps);
-cudaError_t launch_paged_prefill_tc2(const PrefillArgs& a, float* ws, const PrefillMaps& maps, int clusters,
-                                     int dtype, cudaStream_t s);
-// Which tcgen05 prefill form runs: 0 = the CTA pair where it applies (default), 1 = one CTA per unit.
-int set_prefill_variant(int variant);
 
 // Model-side fused row operations around the attention (layer_ops.cu).
 struct RmsNormArgs {

@@ -3,7 +3,6 @@
 #include "kv_scatter.cu"
 #include "paged_decode.cu"
 #include "paged_prefill_tc.cu"
-#include "paged_prefill_tc2.cu"
 #include "paged_prefill.cu"
 #include "layer_ops.cu"
 #include "api.cu"

@@ -1128,14 +1128,6 @@ bool prefill_tc_supported(const PrefillArgs& a, int dtype) {
   return true;
 }
 
-static int g_prefill_variant = 0;
-
-int set_prefill_variant(int variant) {
-  const int prev = g_prefill_variant;
-  if (variant == 0 || variant == 1) g_prefill_variant = variant;
-  return prev;
-}
-
 bool prefill_tc_tma_block_size(int block_size) {
   return block_size == 16 || block_size == 32 || block_size == 64;
 }
@@ -1143,10 +1135,6 @@ bool prefill_tc_tma_block_size(int block_size) {
 cudaError_t launch_paged_prefill_tc(const PrefillArgs& a, float* ws, const PrefillMaps* maps, int dtype,
                                     cudaStream_t s) {
   static const PrefillMaps kNoMaps{};
-  if (maps && g_prefill_variant == 0) {
-    const int clusters = prefill_tc2_clusters(a, maps);
-    if (clusters > 0) return launch_paged_prefill_tc2(a, ws, *maps, clusters, dtype, s);
-  }
   if (maps) {
     if (dtype == MI_BF16) return launch_tc<__nv_bfloat16, true>(a, ws, *maps, s);
     return launch_tc<__half, true>(a, ws, *maps, s);

@@ -55,7 +55,6 @@ SIGNATURES: dict[str, tuple] = {
          ctypes.c_size_t, _I, _P],
     ),
     "mi_decode_rows": (_I, [_P, _L, _P, _L, _P, _L, _L, _P, _L, _L, _I, _P]),
-    "mi_set_prefill_variant": (_I, [_I]),
     # include/mi_layers.h
     "mi_rmsnorm": (_I, [_P, _L, _P, _L, _P, _L, _P, _P, _L, _L, _I, ctypes.c_float, _I, _P]),
     "mi_qk_norm_rope": (

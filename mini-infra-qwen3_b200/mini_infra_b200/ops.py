@@ -459,15 +459,6 @@ def read_status(device: torch.device | None = None, clear: bool = True) -> int:
     return int(value.value)
 
 
-def set_prefill_variant(variant: int) -> int:
-    """Select the tensor-core form of ``paged_prefill`` for this process: 0 (default) runs CTA pairs
-    (two SMs per work unit, one 256-row MMA over the unit's two row tiles) wherever tensor maps
-    apply, 1 runs one CTA per unit.  Returns the previous setting."""
-    if variant not in (0, 1):
-        raise ValueError(f"prefill variant must be 0 or 1, got {variant}")
-    return int(nat.load().mi_set_prefill_variant(int(variant)))
-
-
 def decode_rows(
     rows: torch.Tensor,
     deltas: torch.Tensor | None,

@@ -93,16 +93,8 @@ TC_SHAPES = [
 ]
 
 
-@pytest.fixture(params=[0, 1], ids=["pair", "single"])
-def variant(request):
-    """Both tcgen05 forms: CTA pairs (the default where tensor maps apply) and one CTA per unit."""
-    prev = ops.set_prefill_variant(request.param)
-    yield request.param
-    ops.set_prefill_variant(prev)
-
-
 @pytest.mark.parametrize("shape", TC_SHAPES, ids=[str(s) for s in TC_SHAPES])
-def test_prefill_tensor_core_path(shape, variant):
+def test_prefill_tensor_core_path(shape):
     hq, h, d, bs, starts, lens = shape
     inp = _random_prefill(hq, h, d, bs, starts, lens, "bfloat16", seed=len(starts) * 31 + sum(lens))
     out = run_prefill(inp, bs, d)
@@ -128,7 +120,7 @@ STREAM_SHAPES = [
 
 
 @pytest.mark.parametrize("shape", STREAM_SHAPES, ids=[str(s[:4]) for s in STREAM_SHAPES])
-def test_prefill_tensor_core_stream_split(shape, variant):
+def test_prefill_tensor_core_stream_split(shape):
     hq, h, d, bs, starts, lens = shape
     inp = _random_prefill(hq, h, d, bs, starts, lens, "bfloat16", seed=7)
     out = run_prefill(inp, bs, d)
@@ -141,7 +133,7 @@ def test_prefill_tensor_core_stream_split(shape, variant):
     assert not got[~valid].any()  # padding positions, and rows without a chunk, are zeros
 
 
-def test_prefill_tensor_core_rescales_on_growing_scores(variant):
+def test_prefill_tensor_core_rescales_on_growing_scores():
     """Queries aligned with later keys make the running max jump by far more than 2^8 across KV
     tiles, so the TMEM accumulator rescale path runs; result must still match the oracle."""
     hq, h, d, bs, starts, lens = 16, 8, 128, 16, [600], [128]
@@ -161,7 +153,7 @@ def test_prefill_tensor_core_rescales_on_growing_scores(variant):
     assert_attention_close(out, want, "bfloat16")
 
 
-def test_prefill_tensor_core_fp16(variant):
+def test_prefill_tensor_core_fp16():
     hq, h, d, bs, starts, lens = 16, 8, 128, 16, [200, 0], [64, 100]
     inp = _random_prefill(hq, h, d, bs, starts, lens, "float32", seed=99)
     t = lambda k: to_cuda(inp[k]).half()  # noqa: E731
@@ -178,21 +170,3 @@ def test_prefill_tensor_core_fp16(variant):
     got = out.float().cpu().numpy()
     assert_attention_close(got[valid], want[valid], "float16")
 
-
-def test_prefill_pair_and_single_forms_agree():
-    """The CTA-pair and one-CTA kernels on the same long-history batch (block size 16, G = 4, the
-    stream cut into pieces merged by the combine in both): the same attention up to fp32 rounding
-    of the different cuts, and identical zeros on padding."""
-    hq, h, d, bs, starts, lens = 32, 8, 128, 16, [5000, 0, 1700, 333], [128, 256, 77, 1]
-    inp = _random_prefill(hq, h, d, bs, starts, lens, "bfloat16", seed=4242)
-    outs = []
-    for v in (0, 1):
-        prev = ops.set_prefill_variant(v)
-        try:
-            outs.append(po.as_float(to_numpy(run_prefill(inp, bs, d)), np.float64))
-        finally:
-            ops.set_prefill_variant(prev)
-    length = max(lens)
-    valid = np.arange(length)[None, :] >= (length - np.asarray(lens))[:, None]
-    assert np.abs(outs[0][valid] - outs[1][valid]).max() <= 2e-2
-    assert not outs[0][~valid].any() and not outs[1][~valid].any()

@@ -28,8 +28,6 @@ KV_TILE = 128   # kTcKv
 PAIR = 2        # kPair
 K_STAGES = 2    # kStagesK
 V_STAGES = 2    # kStagesV
-PAIR_K_STAGES = 5  # kP2StagesK (CTA-pair kernel)
-PAIR_V_STAGES = 4  # kP2StagesV
 UNIT_COST = 2   # kUnitCost
 
 
@@ -370,236 +368,3 @@ def test_barrier_protocol_has_no_deadlock_or_phase_slip():
                 walkers, _, _ = split(shape, per_head)
                 for c, w in enumerate(walkers):
                     run_cta(w, seed=1000 * per_head + c, loader=loader)
-
-
-# ------------------------------------------------------------------------------------------------
-# The CTA-pair kernel (`prefill_tc2_kernel`): a unit's two row tiles live in the two CTAs of a
-# cluster; the leader (rank 0) issues M = 256 MMAs for both; each CTA stages half of every K tile
-# (its keys) and half of every V tile (its head dims); TMA bytes of both CTAs complete on the
-# leader's full barriers (the leader posts the expected bytes); commits arrive on both CTAs'
-# barriers.  Each CTA has two softmax sets: set b takes the tiles c of the stream with c % 2 == b,
-# from S buffer b, with its own running max / sum and O accumulator O_b; the sets merge their rows
-# in the item's epilogue through a two-party barrier (the kernel's per-quadrant named barriers).
-# A set's 4 warps each arrive on the leader's p_full / o_free in the kernel; modelled here as one
-# arrival per set.  S(i + 2) is issued right after PV(i), which reads P(i) from the same buffer;
-# two Q buffers (item m in m % 2; item m + 2's Q loads once every S of item m is done).
-# ------------------------------------------------------------------------------------------------
-def run_pair(walk0, seed):
-    rnd = random.Random(seed)
-    bars = {}
-    for cta in range(2):
-        for i in range(PAIR_K_STAGES):
-            bars[f"k_empty{i}@{cta}"] = Barrier(1)
-        for i in range(PAIR_V_STAGES):
-            bars[f"v_empty{i}@{cta}"] = Barrier(1)
-        for b in range(4):
-            bars[f"s_full{b}@{cta}"] = Barrier(1)
-        for b in range(2):
-            bars[f"o_done{b}@{cta}"] = Barrier(1)
-        bars[f"o_final@{cta}"] = Barrier(1)
-        bars[f"pair@{cta}"] = Barrier(2)
-    # the leader's barriers that both CTAs feed
-    for i in range(PAIR_K_STAGES):
-        bars[f"k_full{i}@0"] = Barrier(1)
-    for i in range(PAIR_V_STAGES):
-        bars[f"v_full{i}@0"] = Barrier(1)
-    for b in range(4):  # per S buffer 2h + t % 2
-        bars[f"p_full{b}@0"] = Barrier(2)
-    for b in range(2):  # per Q buffer
-        bars[f"q_full{b}@0"] = Barrier(1)
-    bars["o_free@0"] = Barrier(4)  # both sets of both CTAs read both O accumulators out
-    tx = {}  # pending transaction bytes per leader barrier phase: expected minus arrived
-    items = []
-    w = walk0.copy()
-    while (it := w.next()) is not None:
-        items.append(it)
-    n_tiles = sum(it["n"] for it in items)
-    if n_tiles == 0:
-        return
-    tile_items = [(it, i) for it in items for i in range(it["n"])]
-
-    def k_loader(cta):  # Q of items 0 and 1, then this CTA's half of every K tile, Q(m + 2) after item m
-        def load(bar, nbytes):
-            if cta == 0:
-                yield ("expect", bar, 2 * nbytes)
-            yield ("tma", bar, nbytes)
-        for m in range(min(2, len(items))):
-            yield from load(f"q_full{m % 2}@0", 32)
-        for j in range(min(n_tiles, PAIR_K_STAGES)):
-            yield from load(f"k_full{j % PAIR_K_STAGES}@0", 16)
-        m = 0
-        for j in range(n_tiles):
-            it, i = tile_items[j]
-            item_end = i + 1 == it["n"]
-            if item_end or j + PAIR_K_STAGES < n_tiles:
-                yield ("wait", f"k_empty{j % PAIR_K_STAGES}@{cta}", j // PAIR_K_STAGES)
-            if item_end:
-                if m + 2 < len(items):  # into the buffer item m used: every S of item m is done
-                    yield ("check_s_done", cta, j + 1)
-                    yield from load(f"q_full{m % 2}@0", 32)
-                m += 1
-            if j + PAIR_K_STAGES < n_tiles:
-                yield from load(f"k_full{(j + PAIR_K_STAGES) % PAIR_K_STAGES}@0", 16)
-        for j in range(max(0, n_tiles - PAIR_K_STAGES), n_tiles):  # tail
-            yield ("wait", f"k_empty{j % PAIR_K_STAGES}@{cta}", j // PAIR_K_STAGES)
-
-    def v_loader(cta):
-        for j in range(n_tiles):
-            if j >= PAIR_V_STAGES:
-                yield ("wait", f"v_empty{j % PAIR_V_STAGES}@{cta}", j // PAIR_V_STAGES - 1)
-            if cta == 0:
-                yield ("expect", f"v_full{j % PAIR_V_STAGES}@0", 32)
-            yield ("tma", f"v_full{j % PAIR_V_STAGES}@0", 16)
-        for j in range(max(0, n_tiles - PAIR_V_STAGES), n_tiles):  # tail
-            yield ("wait", f"v_empty{j % PAIR_V_STAGES}@{cta}", j // PAIR_V_STAGES)
-
-    def mma():  # the leader's MMA warp
-        c, j0 = 0, 0
-        for k, it in enumerate(items):
-            n = it["n"]
-
-            def commit(name):
-                yield ("commit", name)  # multicast: both CTAs' copies
-
-            def issue_s(i, h):  # S_h(c + i) into buffer 2h + (c + i) % 2
-                yield ("s_issue", (h, c + i))
-                yield from commit(f"s_full{2 * h + (c + i) % 2}")
-                if h == 1:
-                    yield from commit(f"k_empty{(j0 + i) % PAIR_K_STAGES}")
-
-            yield ("wait", f"q_full{k % 2}@0", k // 2)
-            for i in range(min(n, 2)):
-                yield ("wait", f"k_full{(j0 + i) % PAIR_K_STAGES}@0", (j0 + i) // PAIR_K_STAGES)
-                yield from issue_s(i, 0)
-                yield from issue_s(i, 1)
-            for i in range(n):
-                t = c + i
-                yield ("wait", f"v_full{(j0 + i) % PAIR_V_STAGES}@0", (j0 + i) // PAIR_V_STAGES)
-                if i == 0 and k > 0:
-                    yield ("wait", "o_free@0", k - 1)
-                if i == 0:
-                    yield ("o_write", k)
-                for h in range(2):
-                    yield ("wait", f"p_full{2 * h + t % 2}@0", t // 2)
-                    yield ("pv_issue", (h, t))
-                    yield from commit(f"o_done{h}")
-                    if h == 1:
-                        yield from commit(f"v_empty{(j0 + i) % PAIR_V_STAGES}")
-                        if i + 1 == n:
-                            yield from commit("o_final")
-                    if i + 2 < n:
-                        if h == 0:
-                            yield ("wait", f"k_full{(j0 + i + 2) % PAIR_K_STAGES}@0", (j0 + i + 2) // PAIR_K_STAGES)
-                        yield from issue_s(i + 2, h)
-            c += n
-            j0 += n
-
-    def softmax(cta, h):  # softmax set h of one CTA: half h of every tile, then the merge
-        c, syncs = 0, 0
-        for k, it in enumerate(items):
-            n = it["n"]
-            for i in range(n):
-                t = c + i
-                yield ("wait", f"s_full{2 * h + t % 2}@{cta}", t // 2)
-                yield ("s_read", (h, t))
-                if i >= 1 and rnd.random() < 0.3:  # rescale: this set's previous PV is done
-                    yield ("wait", f"o_done{h}@{cta}", t - 1)
-                yield ("arrive", f"p_full{2 * h + t % 2}@0")
-            c += n
-            yield ("wait", f"o_final@{cta}", k)
-            for _ in range(2):  # the merge's exchange between the two sets, then its reuse guard
-                yield ("arrive", f"pair@{cta}")
-                yield ("wait", f"pair@{cta}", syncs)
-                syncs += 1
-                if _ == 0:
-                    yield ("o_read", (cta, h), k)
-                    yield ("arrive", "o_free@0")
-        yield ("wait", f"o_done{h}@{cta}", c - 1)
-
-    roles = {"k0": k_loader(0), "k1": k_loader(1), "v0": v_loader(0), "v1": v_loader(1), "mma": mma(),
-             "sm00": softmax(0, 0), "sm01": softmax(0, 1), "sm10": softmax(1, 0), "sm11": softmax(1, 1)}
-    blocked = dict.fromkeys(roles)
-    done, inflight, clock, mma_clock = set(), [], 0, 0
-    s_issued, pv_issued, o_read = [], set(), set()
-
-    def complete_tx(bar, nbytes):
-        tx[bar] = tx.get(bar, 0) - nbytes
-        if tx[bar] == 0 and bars[bar].pending == 0 and tx.get(bar + "#armed"):
-            tx[bar + "#armed"] = False
-            bars[bar].phases += 1
-
-    while len(done) < len(roles) or inflight:
-        progressed = False
-        order = list(roles)
-        rnd.shuffle(order)
-        for r in order:
-            while r not in done:
-                if blocked[r] is not None:
-                    _, bar, phase = blocked[r]
-                    seen = bars[bar].phases
-                    assert seen < phase + 2, f"{r} waits for phase {phase} of {bar}, already {seen} done"
-                    if seen < phase + 1:
-                        break
-                    blocked[r] = None
-                try:
-                    ev = next(roles[r])
-                except StopIteration:
-                    done.add(r)
-                    break
-                progressed = True
-                kind = ev[0]
-                if kind == "wait":
-                    blocked[r] = ev
-                elif kind == "expect":  # the leader's arrive.expect_tx: arms the phase
-                    tx[ev[1]] = tx.get(ev[1], 0) + ev[2]
-                    tx[ev[1] + "#armed"] = True
-                    if tx[ev[1]] == 0:
-                        tx[ev[1] + "#armed"] = False
-                        bars[ev[1]].phases += 1
-                elif kind == "tma":
-                    inflight.append((clock + rnd.randint(1, 60), "tx", ev[1], ev[2]))
-                elif kind == "check_s_done":
-                    done_s = sum(bars[f"s_full{b}@{ev[1]}"].phases for b in range(4))
-                    assert done_s >= 2 * ev[2], f"Q reloaded while {2 * ev[2] - done_s} S MMAs were in flight"
-                elif kind == "s_issue":  # S_h(t) overwrites buffer 2h + t % 2: PV_h(t - 2) must have been issued
-                    h, t = ev[1]
-                    assert t < 2 or (h, t - 2) in pv_issued, f"S_{h}({t}) issued before PV_{h}({t - 2})"
-                    s_issued.append(ev[1])
-                elif kind == "pv_issue":
-                    pv_issued.add(ev[1])
-                elif kind == "o_write":  # item k's first PVs overwrite O_0 / O_1: item k - 1 read out
-                    assert ev[1] < 1 or {((cta, st), ev[1] - 1) for cta in (0, 1) for st in (0, 1)} <= o_read, \
-                        f"O of item {ev[1] - 1} overwritten"
-                elif kind == "o_read":
-                    o_read.add((ev[1], ev[2]))
-                elif kind == "s_read":
-                    h, t = ev[1]
-                    later = [v for v in s_issued if v[0] == h and v[1] > t and v[1] % 2 == t % 2]
-                    assert ev[1] in s_issued and not later, f"softmax reads S_{h}({t}) over S {later}"
-                elif kind == "commit":  # both CTAs' copies, in issue order
-                    mma_clock = max(mma_clock, clock) + rnd.randint(0, 20)
-                    inflight.append((mma_clock, "arrive", f"{ev[1]}@0", 0))
-                    inflight.append((mma_clock, "arrive", f"{ev[1]}@1", 0))
-                elif kind == "arrive":
-                    bars[ev[1]].arrive()
-                if rnd.random() < 0.3:
-                    break
-        clock += 1
-        inflight.sort(key=lambda x: x[0])
-        while inflight and inflight[0][0] <= clock:
-            _, what, bar, nbytes = inflight.pop(0)
-            if what == "tx":
-                complete_tx(bar, nbytes)
-            else:
-                bars[bar].arrive()
-            progressed = True
-        assert progressed or inflight or len(done) == len(roles), \
-            f"deadlock: {[(r, blocked[r]) for r in roles if r not in done]}"
-
-
-def test_pair_barrier_protocol_has_no_deadlock_or_phase_slip():
-    for shape in _shapes():
-        for per_head in (9, 4, 1):
-            walkers, _, _ = split(shape, per_head)
-            for c, w in enumerate(walkers):
-                run_pair(w, seed=77 * per_head + c)
