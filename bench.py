@@ -416,6 +416,49 @@ def prefill_record(device, iters: int) -> dict:
                        "status_bits": status, "reference": "float32 torch on the device"}}
 
 
+def prefill_long_record(device, iters: int) -> dict:
+    """A compute-bound chunked-prefill launch beside config 4's: 4 rows of 4096-token chunks with no
+    history at the Qwen3-8B attention shape (Hq 32, H_kv 8, G 4), so K/V come from L2-resident
+    chunks and the tensor pipe, not the pool reads, sets the time.  TFLOP/s of the causal
+    algorithmic FLOPs, its fraction of the measured bf16 peak, and a parity check of the last 128
+    positions of row 0 against float32 torch on the device."""
+    from mini_infra_b200 import ops
+
+    b, length, hq, hkv = 4, 4096, 32, 8
+    g = torch.Generator(device=device).manual_seed(SEED + 7)
+    rnd = lambda *sh: torch.randn(sh, generator=g, device=device, dtype=torch.bfloat16)  # noqa: E731
+    q, kc, vc = rnd(b, length, hq, D), rnd(b, length, hkv, D), rnd(b, length, hkv, D)
+    tables = torch.zeros((b, 0), dtype=torch.long, device=device)
+    starts = torch.zeros(b, dtype=torch.long, device=device)
+    lens = torch.full((b,), length, dtype=torch.long, device=device)
+    out = torch.empty((b, length, hq * D), dtype=torch.bfloat16, device=device)
+    scale = D**-0.5
+
+    def launch():
+        ops.paged_prefill(q, kc, vc, None, None, tables, starts, lens, scale, out=out)
+
+    for _ in range(3):
+        launch()
+    ms = event_ms(launch, iters, device)
+    flops = b * 4.0 * length * (length + 1) / 2.0 * hq * D
+    tflops = flops / (ms * 1e-3) / 1e12
+    pk = peaks()
+    tail = 128  # queries [length - tail, length) of row 0 against all their keys
+    gq = hq // hkv
+    qq = q[0, length - tail :].float().view(tail, hkv, gq, D)
+    scores = torch.einsum("jhgd,thd->hgjt", qq, kc[0].float()) * scale
+    allowed = torch.arange(length, device=device)[None, :] <= (length - tail + torch.arange(tail, device=device))[:, None]
+    want = torch.einsum("hgjt,thd->jhgd", torch.softmax(scores.masked_fill(~allowed, float("-inf")), dim=-1),
+                        vc[0].float()).reshape(tail, hq * D)
+    err = float((out[0, length - tail :].float() - want).abs().max())
+    status = ops.read_status(device)
+    return {"ms": ms, "tflops": tflops, "frac": tflops / pk["bf16_tflops"], "peak_tflops": pk["bf16_tflops"],
+            "peak_source": pk["source"], "algorithmic_gflop": flops / 1e9, "iters": iters,
+            "shape": {"rows": b, "chunk": length, "history": 0, "hq": hq, "hkv": hkv, "head_dim": D},
+            "parity": {"max_abs": err, "tol": 2e-2, "ok": bool(err <= 2e-2 and status == 0), "rows": 1,
+                       "positions": tail, "status_bits": status, "reference": "float32 torch on the device"}}
+
+
 def scatter_record(device, iters: int) -> dict:
     """KV scatter at config 4's chunk size (16 rows x 128 tokens, 8 KV heads, D 128, bf16): the
     reference's write_prefill (mi_kv_scatter with host-built slots) and store_prefill with the slots
@@ -569,6 +612,7 @@ def run_decode(args, spec: dict) -> None:
     sub_prefill = sub_scatter = None
     if not args.no_subrecords:
         sub_prefill = prefill_record(device, iters=200)
+        sub_prefill["long_chunk"] = prefill_long_record(device, iters=20)
         sub_scatter = scatter_record(device, iters=20)
         torch.cuda.empty_cache()
     barrier()

@@ -501,7 +501,7 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
   a.scale_log2 = scale * 1.4426950408889634f;
   a.out = static_cast<char*>(out);
   float* ws = nullptr;
-  mi::PrefillMaps maps;
+  mi::PrefillMaps maps{};
   bool use_maps = false;
   if (mi::prefill_tc_supported(a, dtype)) {
     const size_t need = mi::prefill_tc_workspace_bytes(a);
@@ -511,8 +511,9 @@ int mi_paged_prefill(const void* q, const int64_t* q_strides, const void* k_chun
                     workspace_bytes);
       ws = static_cast<float*>(workspace);
     }
-    // TMA staging when every operand has a tensor map; otherwise the kernel uses cp.async.
-    if (mi::prefill_tc_tma_block_size(block_size) && padded_len < (int64_t(1) << 31)) {
+    // TMA staging when every operand it reads has a tensor map (without history the pools are not
+    // read, so any block size qualifies); otherwise the kernel uses cp.async.
+    if ((table_stride == 0 || mi::prefill_tc_tma_block_size(block_size)) && padded_len < (int64_t(1) << 31)) {
       const int G = a.groups;
       const cuuint64_t qd[4] = {(cuuint64_t)head_dim, (cuuint64_t)num_q_heads, (cuuint64_t)padded_len,
                                 (cuuint64_t)batch};

@@ -7,7 +7,8 @@ host work and upload) timed as cache_ms, then the decode forward (model_ms) — 
 replay per batch bucket unless ``cuda_graphs=False`` (a bucket's first step captures its graph
 before the timing starts).  Per
 mixed step (mixed chunked prefill): one forward over decode rows and chunks (model_ms), then the
-chunks' ``store_prefill`` as cache_ms.  ``accessed_kv_cache_tokens`` counts history tokens
+chunks' ``store_prefill`` as cache_ms — both CUDA-graph replays per step shape unless
+``cuda_graphs=False`` (a shape's first step captures its graphs before the timing starts).  ``accessed_kv_cache_tokens`` counts history tokens
 read: sum of chunk starts (prefill) and sum of context lengths (decode).
 """
 
@@ -83,11 +84,14 @@ class PagedScheduleBackend:
                 attach_peer_exchange(model, rows, self.block_size)
         if cuda_graphs and self.device.type == "cuda":
             # decode tables never exceed the largest request; round the graphs' width up to a power of two
-            self.runner.enable_decode_graphs(self.pool.kv_pools, 1 << max(4, (largest - 1).bit_length()))
+            width = 1 << max(4, (largest - 1).bit_length())
+            self.runner.enable_decode_graphs(self.pool.kv_pools, width)
+            self.runner.enable_mixed_graphs(self.pool, width)
 
     def close(self) -> None:
-        """Drop the decode graphs (they may hold NCCL calls: before the process group goes)."""
+        """Drop the decode and mixed-step graphs (they may hold NCCL calls: before the process group goes)."""
         self.runner.release_decode_graphs()
+        self.runner.release_mixed_graphs()
 
     @property
     def kv_cache_config(self) -> PagedCacheConfig:
@@ -145,12 +149,17 @@ class PagedScheduleBackend:
         d_tables = [self.kv_cache_manager.block_table(s.request.request_idx) for s in decoding]
         c_tables = [self.kv_cache_manager.block_table(c.state.request.request_idx) for c in chunks]
         starts = [c.start for c in chunks]
+        chunk_ids = [c.state.request.token_ids[c.start : c.end] for c in chunks]
+        self.runner.warm_mixed_graph(d_tables, chunk_ids, c_tables, self.pool)  # first use of a shape: capture
         out = self.runner.run_mixed_step(
-            d_tables, [s.generated[-1] for s in decoding], [s.cache_length for s in decoding],
-            [c.state.request.token_ids[c.start : c.end] for c in chunks], starts, c_tables, self.pool)
+            d_tables, [s.generated[-1] for s in decoding], [s.cache_length for s in decoding], chunk_ids, starts,
+            c_tables, self.pool)
         synchronize(self.device)
         t0 = time.perf_counter()
-        self.runner.store_prefill(self.pool, out.prefill_cache, c_tables, [c.num_tokens for c in chunks], starts)
+        if out.prefill_cache is None:  # served by a graph: its store graph
+            self.runner.store_mixed()
+        else:
+            self.runner.store_prefill(self.pool, out.prefill_cache, c_tables, [c.num_tokens for c in chunks], starts)
         synchronize(self.device)
         cache_ms = (time.perf_counter() - t0) * 1000.0
         return ScheduleStepOutput(

@@ -21,7 +21,9 @@ tables).  Attention reads history in place from the pools; nothing gathers the h
   only new entries, so the host work per step is O(batch), not O(batch x max_blocks).
 * ``run_mixed_step`` — decode rows and prefill chunks in one forward (the mixed chunked-prefill
   policy; no reference counterpart): one packed upload, projections over all tokens, one decode
-  and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.
+  and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.  With
+  ``enable_mixed_graphs`` a step whose shape has a graph (``worker/mixed_graphs.py``) replays it;
+  its chunks' store is then ``store_mixed`` (a second replay) instead of ``store_prefill``.
 """
 
 from __future__ import annotations
@@ -38,6 +40,7 @@ from mini_infra_b200.model.qwen3 import ChunkPrefillMetadata, MixedMetadata, Pag
 from mini_infra_b200.worker.base_runner import BaseModelRunner, PrefillOutput
 from mini_infra_b200.worker.block_tables import DeviceBlockTables
 from mini_infra_b200.worker.decode_graphs import DecodeGraphSet, packed_length
+from mini_infra_b200.worker.mixed_graphs import MixedGraphSet
 from mini_infra_b200.worker.kv_cache import KVCache
 from mini_infra_b200.worker.paged_kv_cache import PagedKVCachePool
 from mini_infra_b200.worker.sampler import greedy_sample
@@ -53,7 +56,7 @@ class PagedDecodeOutput(NamedTuple):
 class PagedMixedOutput(NamedTuple):
     decode_tokens: list[int]   # one per decode row
     prefill_tokens: list[int]  # one per chunk row (its last position; meaningful for final chunks)
-    prefill_cache: KVCache     # the chunks' K/V for store_prefill
+    prefill_cache: KVCache | None  # the chunks' K/V for store_prefill; None: a graph replay (store_mixed)
     model_ms: float
 
 
@@ -81,7 +84,10 @@ class PagedRunner(BaseModelRunner):
     h2d_bytes = 0
     d2h_bytes = 0
     graph_replays = 0  # decode steps served by a CUDA-graph replay
+    mixed_graph_replays = 0  # mixed steps served by a CUDA-graph replay
     decode_graphs: DecodeGraphSet | None = None
+    mixed_graphs: MixedGraphSet | None = None
+    _mixed_store = None  # the replayed mixed step's graphs, whose store is pending
     device_tables: DeviceBlockTables | None = None
     _graph_step: tuple[int, int, int] | None = None  # (bucket, batch, static buffer address)
 
@@ -99,6 +105,38 @@ class PagedRunner(BaseModelRunner):
             self.decode_graphs.release()
         self.decode_graphs = None
         self._graph_step = None
+
+    def enable_mixed_graphs(self, pool: PagedKVCachePool, width: int) -> None:
+        """Replay mixed steps whose tables hold at most `width` blocks from CUDA graphs over `pool`."""
+        self.release_mixed_graphs()
+        self.mixed_graphs = MixedGraphSet(self.model, pool, width, width, self.pad_token_id)
+
+    def release_mixed_graphs(self) -> None:
+        if self.mixed_graphs is not None:
+            self.mixed_graphs.release()
+        self.mixed_graphs = None
+        self._mixed_store = None
+
+    def _mixed_key(self, decode_tables, chunk_token_ids, chunk_tables, pool):
+        g = self.mixed_graphs
+        if (g is None or not decode_tables or not chunk_token_ids
+                or g.kv_pools[0][0].data_ptr() != pool.kv_pools[0][0].data_ptr()):
+            return None
+        return g.key_for(len(decode_tables), len(chunk_token_ids), padded_width(max(len(t) for t in chunk_token_ids)),
+                         max(len(t) for t in decode_tables), max(len(t) for t in chunk_tables))
+
+    def warm_mixed_graph(self, decode_tables, chunk_token_ids, chunk_tables, pool) -> None:
+        """Capture the graphs a mixed step of this shape will replay (outside any step timing)."""
+        key = self._mixed_key(decode_tables, chunk_token_ids, chunk_tables, pool)
+        if key is not None:
+            self.mixed_graphs.get(key)
+
+    def store_mixed(self) -> None:
+        """The pending store of the last replayed mixed step's chunks (no sync, no timing)."""
+        g, self._mixed_store = self._mixed_store, None
+        if g is None:
+            raise RuntimeError("store_mixed follows a mixed step served by a graph")
+        g.store.replay()
 
     def warm_decode_graph(self, batch: int, max_blocks: int) -> None:
         """Capture the graph a step of this shape will replay (outside any step timing)."""
@@ -257,6 +295,10 @@ class PagedRunner(BaseModelRunner):
         lens = [len(t) for t in chunk_token_ids]
         if nd == 0 or bp == 0 or min(lens) < 1:
             raise ValueError("a mixed step needs decode rows and non-empty chunks")
+        key = self._mixed_key(decode_block_tables, chunk_token_ids, chunk_block_tables, pool)
+        if key is not None:
+            return self._replay_mixed(key, decode_block_tables, last_tokens, positions, chunk_token_ids,
+                                      start_positions, chunk_block_tables)
         bs = pool.block_size
         width = padded_width(max(lens))
         n_hist = [-(-int(st) // bs) for st in start_positions]
@@ -296,6 +338,27 @@ class PagedRunner(BaseModelRunner):
         tokens = next_token.squeeze(-1).tolist()
         self.d2h_bytes += 8 * (nd + bp)
         return PagedMixedOutput(tokens[:nd], tokens[nd:], KVCache(presents), timer.elapsed_ms)
+
+    def _replay_mixed(self, key, decode_tables, last_tokens, positions, chunk_token_ids, start_positions,
+                      chunk_tables) -> PagedMixedOutput:
+        g = self.mixed_graphs
+        for table, st, toks in zip(chunk_tables, start_positions, chunk_token_ids):
+            need = -(-(int(st) + len(toks)) // g.pool.block_size)
+            if len(table) < need:
+                raise ValueError(f"block table {list(table)} does not cover {need} blocks")
+        graphs = g.get(key)
+        host = g.fill(key, decode_tables, last_tokens, positions, chunk_token_ids, start_positions, chunk_tables)
+        self.h2d_bytes += host.nbytes
+        nd, bp = len(decode_tables), len(chunk_token_ids)
+        with StepTimer(self.device) as timer:
+            graphs.static.copy_(torch.from_numpy(host).pin_memory(), non_blocking=True)
+            graphs.forward.replay()
+            tokens = graphs.tokens.tolist()
+        self.mixed_graph_replays += 1
+        self._mixed_store = graphs
+        self.d2h_bytes += 8 * (nd + bp)
+        ndb = key[0]
+        return PagedMixedOutput(tokens[:nd], tokens[ndb : ndb + bp], None, timer.elapsed_ms)
 
     def _prepare_graph_inputs(self, g: DecodeGraphSet, n: int, block_tables, last_tokens, positions, slots):
         """Packed rows padded to bucket n, copied into the bucket's static buffer; views of its first b rows."""

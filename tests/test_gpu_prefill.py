@@ -170,3 +170,25 @@ def test_prefill_tensor_core_fp16():
     got = out.float().cpu().numpy()
     assert_attention_close(got[valid], want[valid], "float16")
 
+
+
+@pytest.mark.parametrize("hq,h,lens", [(32, 8, [512, 300, 1]), (16, 8, [128, 77])], ids=["G4", "G2"])
+def test_prefill_without_pools(hq, h, lens):
+    """No history and no pools (k_pool None, empty block tables): the chunk's own causal attention,
+    staged by TMA like any other chunk."""
+    d, starts = 128, [0] * len(lens)
+    inp = _random_prefill(hq, h, d, 16, starts, lens, "bfloat16", seed=sum(lens))
+    q = to_cuda(inp["query"]).transpose(1, 2)
+    k = to_cuda(inp["key_chunk"]).transpose(1, 2)
+    v = to_cuda(inp["value_chunk"]).transpose(1, 2)
+    b = len(lens)
+    out = ops.paged_prefill(q, k, v, None, None, torch.zeros((b, 0), dtype=torch.long, device="cuda"),
+                            torch.zeros(b, dtype=torch.long, device="cuda"), torch.tensor(lens).cuda(), d**-0.5)
+    assert ops.read_status() == 0
+    want = po.chunk_prefill_attention(inp["query"], inp["key_chunk"], inp["value_chunk"], inp["key_pool"],
+                                      inp["value_pool"], inp["tables_list"], starts, lens, d**-0.5)
+    length = max(lens)
+    valid = np.arange(length)[None, :] >= (length - np.asarray(lens))[:, None]
+    got = po.as_float(to_numpy(out), np.float64)
+    assert_attention_close(got[valid], want[valid], "bfloat16")
+    assert not got[~valid].any()
