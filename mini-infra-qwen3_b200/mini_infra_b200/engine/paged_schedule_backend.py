@@ -7,8 +7,9 @@ host work and upload) timed as cache_ms, then the decode forward (model_ms) — 
 replay per batch bucket unless ``cuda_graphs=False`` (a bucket's first step captures its graph
 before the timing starts).  Per
 mixed step (mixed chunked prefill): one forward over decode rows and chunks (model_ms), then the
-chunks' ``store_prefill`` as cache_ms — both CUDA-graph replays per step shape unless
-``cuda_graphs=False`` (a shape's first step captures its graphs before the timing starts).  ``accessed_kv_cache_tokens`` counts history tokens
+chunks' ``store_prefill`` as cache_ms; unless ``cuda_graphs=False``, a shape's second and later
+steps replay one CUDA graph of forward + sample + store (model_ms; cache_ms ~0), captured before
+the timing starts.  ``accessed_kv_cache_tokens`` counts history tokens
 read: sum of chunk starts (prefill) and sum of context lengths (decode).
 """
 
@@ -156,9 +157,7 @@ class PagedScheduleBackend:
             c_tables, self.pool)
         synchronize(self.device)
         t0 = time.perf_counter()
-        if out.prefill_cache is None:  # served by a graph: its store graph
-            self.runner.store_mixed()
-        else:
+        if out.prefill_cache is not None:  # None: a graph replay stored the chunks (in model_ms)
             self.runner.store_prefill(self.pool, out.prefill_cache, c_tables, [c.num_tokens for c in chunks], starts)
         synchronize(self.device)
         cache_ms = (time.perf_counter() - t0) * 1000.0

@@ -15,11 +15,13 @@ never holds data a reader uses); padding chunk rows have length 0 (no output, no
 The chunk tables are the requests' whole tables: the attention reads the entries below each
 chunk's start, the store the entries its tokens land in.
 
-A key holds two graphs, replayed back to back by the runner: the forward with the greedy sample at
-every decode row and at each chunk row's last position, and the store of the chunks' K/V into the
-pools (timed apart, as ``store_prefill`` is on the eager path).  At most ``max_graphs`` keys are
-captured; a step of another shape runs eagerly.  The pools and the workspaces the graphs read must
-outlive them (``ops.workspace`` never frees a buffer it handed out).
+A key's graph holds the forward, the greedy sample at every decode row and at each chunk row's last
+position, and the store of the chunks' K/V into the pools (so the K/V stay intermediates of the
+capture, whose memory the graphs of a set share: they never run at once).  A shape is captured on
+its `capture_after`-th step (1: the first; a capture costs ~2-3 eager steps of host time, which a
+long-running server amortises; 2 leaves one-off shapes eager), and at most ``max_graphs`` shapes
+are.  The pools and the workspaces the graphs read must outlive them
+(``ops.workspace`` never frees a buffer it handed out).
 """
 
 from __future__ import annotations
@@ -38,7 +40,8 @@ from mini_infra_b200.worker.paged_kv_cache import PagedKVCachePool
 from mini_infra_b200.worker.sampler import greedy_sample
 
 DECODE_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
-CHUNK_BUCKETS = (1, 2, 4, 8, 16, 32)
+# a padding chunk row costs `width` tokens of projections and MLP, so these buckets are fine
+CHUNK_BUCKETS = (1, 2, 3, 4, 5, 6, 8, 10, 12, 16, 20, 24, 32)
 
 
 def mixed_packed_length(nd: int, nc: int, width: int, wd: int, wc: int) -> int:
@@ -50,10 +53,8 @@ def mixed_packed_length(nd: int, nc: int, width: int, wd: int, wc: int) -> int:
 class _MixedGraph:
     key: tuple[int, int, int]
     static: torch.Tensor   # packed int64 inputs
-    forward: torch.cuda.CUDAGraph
-    store: torch.cuda.CUDAGraph
+    graph: torch.cuda.CUDAGraph
     tokens: torch.Tensor   # [nd + nc] int64: decode rows, then each chunk row's last position
-    presents: list         # the chunks' K/V per layer, read by the store graph
     rows: torch.Tensor     # the sampled rows of the forward's hidden states
 
 
@@ -66,7 +67,7 @@ def _first_at_least(buckets: Sequence[int], n: int) -> int | None:
 
 class MixedGraphSet:
     def __init__(self, model: torch.nn.Module, pool: PagedKVCachePool, decode_width: int, chunk_width: int,
-                 pad_token_id: int = 0, max_graphs: int = 48):
+                 pad_token_id: int = 0, max_graphs: int = 64, capture_after: int = 1):
         self.model = model
         self.device = next(model.parameters()).device
         if self.device.type != "cuda":
@@ -76,7 +77,9 @@ class MixedGraphSet:
         self.wd, self.wc = int(decode_width), int(chunk_width)
         self.pad_token_id = int(pad_token_id)
         self.max_graphs = int(max_graphs)
+        self.capture_after = max(1, int(capture_after))
         self._graphs: dict[tuple[int, int, int], _MixedGraph] = {}
+        self._seen: dict[tuple[int, int, int], int] = {}
         self._mempool = torch.cuda.graph_pool_handle()
         attn = model.model.layers[0].self_attn  # type: ignore[attr-defined]
         # every decode bucket's split-K workspace, before any capture (see DecodeGraphSet)
@@ -84,17 +87,20 @@ class MixedGraphSet:
                       slot="decode")
 
     def key_for(self, nd: int, nc: int, width: int, decode_blocks: int, chunk_blocks: int) -> tuple[int, int, int] | None:
-        """The key serving this step, or None when it must run eagerly (too wide or too many rows,
-        or a new shape once max_graphs keys are captured)."""
+        """The key of this step's shape if a graph serves (or will now be captured to serve) it;
+        None runs it eagerly: too wide or too many rows, the shape's first step, or a new shape
+        once max_graphs are captured.  Counts the shape's steps."""
         if decode_blocks > self.wd or chunk_blocks > self.wc or nd < 1 or nc < 1:
             return None
         ndb, ncb = _first_at_least(DECODE_BUCKETS, nd), _first_at_least(CHUNK_BUCKETS, nc)
         if ndb is None or ncb is None:
             return None
         key = (ndb, ncb, int(width))
-        if key not in self._graphs and len(self._graphs) >= self.max_graphs:
-            return None
-        return key
+        if key in self._graphs:
+            return key
+        seen = self._seen.get(key, 0) + 1
+        self._seen[key] = seen
+        return key if seen >= self.capture_after and len(self._graphs) < self.max_graphs else None
 
     def get(self, key: tuple[int, int, int]) -> _MixedGraph:
         """The key's graphs, captured on first use."""
@@ -138,6 +144,9 @@ class MixedGraphSet:
             ctab[j, : len(tab)] = tab
         return host
 
+    def has(self, key) -> bool:
+        return key in self._graphs
+
     def release(self) -> None:
         self._graphs.clear()
 
@@ -167,31 +176,24 @@ class MixedGraphSet:
         with torch.inference_mode():
             ids, pos, md = self._views(static, key)
 
-            def forward():
+            def step():
                 hidden, presents = self.model.model(ids, position_ids=pos, attn_metadata=md)
                 logits = self.model.lm_head(hidden[0, rows]).unsqueeze(1)
                 next_token, _ = greedy_sample(logits)
-                return next_token.view(-1), presents
-
-            def store(presents):
                 self.pool.store_chunks(KVCache(presents), md.prefill.chunk_lens, md.prefill.start_positions,
                                        md.prefill.block_tables)
+                return next_token.view(-1)
 
             current = torch.cuda.current_stream(self.device)
             side = torch.cuda.Stream(self.device)
             side.wait_stream(current)
-            with torch.cuda.stream(side):  # warm-up: lazy initialisation stays out of the graphs
-                for _ in range(2):
-                    _, presents = forward()
-                    store(presents)
+            with torch.cuda.stream(side):  # warm-up: lazy initialisation stays out of the graph
+                step()
             current.wait_stream(side)
-            fwd = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(fwd, pool=self._mempool):
-                tokens, presents = forward()
-            st = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(st, pool=self._mempool):
-                store(presents)
-        return _MixedGraph(key, static, fwd, st, tokens, list(presents), rows)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, pool=self._mempool):
+                tokens = step()
+        return _MixedGraph(key, static, graph, tokens, rows)
 
 
 __all__ = ["CHUNK_BUCKETS", "DECODE_BUCKETS", "MixedGraphSet", "mixed_packed_length"]

@@ -22,8 +22,8 @@ tables).  Attention reads history in place from the pools; nothing gathers the h
 * ``run_mixed_step`` — decode rows and prefill chunks in one forward (the mixed chunked-prefill
   policy; no reference counterpart): one packed upload, projections over all tokens, one decode
   and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.  With
-  ``enable_mixed_graphs`` a step whose shape has a graph (``worker/mixed_graphs.py``) replays it;
-  its chunks' store is then ``store_mixed`` (a second replay) instead of ``store_prefill``.
+  ``enable_mixed_graphs`` a step whose shape has a graph (``worker/mixed_graphs.py``) replays it,
+  the chunks' store included (no ``store_prefill`` follows: ``prefill_cache`` is None).
 """
 
 from __future__ import annotations
@@ -87,7 +87,7 @@ class PagedRunner(BaseModelRunner):
     mixed_graph_replays = 0  # mixed steps served by a CUDA-graph replay
     decode_graphs: DecodeGraphSet | None = None
     mixed_graphs: MixedGraphSet | None = None
-    _mixed_store = None  # the replayed mixed step's graphs, whose store is pending
+    _mixed_key_pending = None  # (step shape, key) counted by warm_mixed_graph for the next step
     device_tables: DeviceBlockTables | None = None
     _graph_step: tuple[int, int, int] | None = None  # (bucket, batch, static buffer address)
 
@@ -115,7 +115,7 @@ class PagedRunner(BaseModelRunner):
         if self.mixed_graphs is not None:
             self.mixed_graphs.release()
         self.mixed_graphs = None
-        self._mixed_store = None
+        self._mixed_key_pending = None
 
     def _mixed_key(self, decode_tables, chunk_token_ids, chunk_tables, pool):
         g = self.mixed_graphs
@@ -126,17 +126,12 @@ class PagedRunner(BaseModelRunner):
                          max(len(t) for t in decode_tables), max(len(t) for t in chunk_tables))
 
     def warm_mixed_graph(self, decode_tables, chunk_token_ids, chunk_tables, pool) -> None:
-        """Capture the graphs a mixed step of this shape will replay (outside any step timing)."""
+        """Capture the graph a mixed step of this shape will replay, if its shape has one now
+        (outside any step timing); the next run_mixed_step of these rows uses the decision."""
         key = self._mixed_key(decode_tables, chunk_token_ids, chunk_tables, pool)
         if key is not None:
             self.mixed_graphs.get(key)
-
-    def store_mixed(self) -> None:
-        """The pending store of the last replayed mixed step's chunks (no sync, no timing)."""
-        g, self._mixed_store = self._mixed_store, None
-        if g is None:
-            raise RuntimeError("store_mixed follows a mixed step served by a graph")
-        g.store.replay()
+        self._mixed_key_pending = (id(decode_tables), id(chunk_token_ids), key)
 
     def warm_decode_graph(self, batch: int, max_blocks: int) -> None:
         """Capture the graph a step of this shape will replay (outside any step timing)."""
@@ -295,8 +290,12 @@ class PagedRunner(BaseModelRunner):
         lens = [len(t) for t in chunk_token_ids]
         if nd == 0 or bp == 0 or min(lens) < 1:
             raise ValueError("a mixed step needs decode rows and non-empty chunks")
-        key = self._mixed_key(decode_block_tables, chunk_token_ids, chunk_block_tables, pool)
-        if key is not None:
+        pending, self._mixed_key_pending = self._mixed_key_pending, None
+        if pending is not None and pending[:2] == (id(decode_block_tables), id(chunk_token_ids)):
+            key = pending[2]
+        else:
+            key = self._mixed_key(decode_block_tables, chunk_token_ids, chunk_block_tables, pool)
+        if key is not None and self.mixed_graphs.has(key):
             return self._replay_mixed(key, decode_block_tables, last_tokens, positions, chunk_token_ids,
                                       start_positions, chunk_block_tables)
         bs = pool.block_size
@@ -352,10 +351,9 @@ class PagedRunner(BaseModelRunner):
         nd, bp = len(decode_tables), len(chunk_token_ids)
         with StepTimer(self.device) as timer:
             graphs.static.copy_(torch.from_numpy(host).pin_memory(), non_blocking=True)
-            graphs.forward.replay()
+            graphs.graph.replay()
             tokens = graphs.tokens.tolist()
         self.mixed_graph_replays += 1
-        self._mixed_store = graphs
         self.d2h_bytes += 8 * (nd + bp)
         ndb = key[0]
         return PagedMixedOutput(tokens[:nd], tokens[ndb : ndb + bp], None, timer.elapsed_ms)
