@@ -1,0 +1,70 @@
+"""Host-side packing of a mixed step's static graph inputs (``MixedGraphSet.fill``), on CPU.
+
+The layout a graph reads — ids | positions | decode slots | decode context lengths | chunk starts |
+chunk lengths | decode tables | chunk tables — must carry exactly the values the eager mixed step
+builds: decode rows first, then left-padded chunk rows, padding rows that decode into slot 0 of
+the null block (context length 1) and padding chunk rows of length 0.
+"""
+
+from types import SimpleNamespace
+
+from mini_infra_b200.worker.mixed_graphs import CHUNK_BUCKETS, DECODE_BUCKETS, MixedGraphSet, mixed_packed_length
+
+
+def _set(wd=8, wc=8, bs=4, pad=3):
+    g = object.__new__(MixedGraphSet)  # the packing needs no device
+    g.wd, g.wc, g.pad_token_id = wd, wc, pad
+    g.pool = SimpleNamespace(block_size=bs)
+    g.max_graphs, g.capture_after = 4, 1
+    g._graphs, g._seen = {}, {}
+    return g
+
+
+def test_fill_layout_matches_the_eager_step():
+    g = _set()
+    key = (4, 2, 8)  # decode bucket 4, chunk-row bucket 2, width 8
+    d_tables = [[5, 9], [7], [2, 3, 4]]
+    last, positions = [11, 12, 13], [6, 1, 9]
+    chunks, starts, c_tables = [[21, 22, 23]], [5], [[6, 8]]
+    host = g.fill(key, d_tables, last, positions, chunks, starts, c_tables)
+    nd, nc, w = key
+    t = nd + nc * w
+    assert host.shape == (mixed_packed_length(nd, nc, w, g.wd, g.wc),)
+    ids, pos = host[:t], host[t : 2 * t]
+    o = 2 * t
+    slots, ctx = host[o : o + nd], host[o + nd : o + 2 * nd]
+    starts_h, lens_h = host[o + 2 * nd : o + 2 * nd + nc], host[o + 2 * nd + nc : o + 2 * nd + 2 * nc]
+    q = o + 2 * nd + 2 * nc
+    dtab, ctab = host[q : q + nd * g.wd].reshape(nd, g.wd), host[q + nd * g.wd :].reshape(nc, g.wc)
+    # decode rows, then one padding row
+    assert ids[:nd].tolist() == [11, 12, 13, 0] and pos[:nd].tolist() == [6, 1, 9, 0]
+    assert slots.tolist() == [9 * 4 + 2, 7 * 4 + 1, 4 * 4 + 1, 0]  # table[pos // bs] * bs + pos % bs
+    assert ctx.tolist() == [7, 2, 10, 1]
+    assert dtab[:, :3].tolist() == [[5, 9, 0], [7, 0, 0], [2, 3, 4], [0, 0, 0]] and not dtab[:, 3:].any()
+    # chunk row 0 left-padded to the width, padding chunk row 1 empty
+    row0, row1 = ids[nd : nd + w], ids[nd + w : nd + 2 * w]
+    assert row0.tolist() == [3] * 5 + [21, 22, 23] and row1.tolist() == [3] * w
+    assert pos[nd : nd + w].tolist() == [0] * 5 + [5, 6, 7] and not pos[nd + w :].any()
+    assert starts_h.tolist() == [5, 0] and lens_h.tolist() == [3, 0]
+    assert ctab.tolist() == [[6, 8, 0, 0, 0, 0, 0, 0], [0] * 8]
+
+
+def test_keys_bucket_rows_and_reject_what_a_graph_cannot_hold():
+    g = _set(wd=8, wc=16)
+    assert g.key_for(3, 2, 64, 8, 16) == (4, 2, 64)
+    assert g.key_for(5, 7, 64, 1, 1) == (8, 8, 64)
+    assert g.key_for(3, 2, 64, 9, 1) is None  # decode table wider than the graphs'
+    assert g.key_for(3, 2, 64, 1, 17) is None  # chunk table wider
+    assert g.key_for(DECODE_BUCKETS[-1] + 1, 1, 32, 1, 1) is None
+    assert g.key_for(1, CHUNK_BUCKETS[-1] + 1, 32, 1, 1) is None
+
+
+def test_capture_budget_and_first_use():
+    g = _set()
+    g.capture_after = 2
+    assert g.key_for(1, 1, 32, 1, 1) is None  # first step of the shape: eager
+    assert g.key_for(1, 1, 32, 1, 1) == (1, 1, 32)  # second: captured
+    g.capture_after, g.max_graphs = 1, 1
+    g._graphs[(1, 1, 32)] = object()
+    assert g.key_for(1, 1, 32, 1, 1) == (1, 1, 32)  # captured shapes keep their graph
+    assert g.key_for(2, 1, 32, 1, 1) is None  # budget spent: new shapes run eagerly
