@@ -87,28 +87,30 @@ class MixedGraphSet:
                       slot="decode")
 
     def key_for(self, nd: int, nc: int, width: int, decode_blocks: int, chunk_blocks: int) -> tuple[int, int, int] | None:
-        """The key of this step's shape if a graph serves (or will now be captured to serve) it;
-        None runs it eagerly: too wide or too many rows, the shape's first step, or a new shape
-        once max_graphs are captured.  Counts the shape's steps."""
+        """The key of a step's shape, or None when no graph of this set can hold it (tables too
+        wide, too many decode or chunk rows)."""
         if decode_blocks > self.wd or chunk_blocks > self.wc or nd < 1 or nc < 1:
             return None
         ndb, ncb = _first_at_least(DECODE_BUCKETS, nd), _first_at_least(CHUNK_BUCKETS, nc)
         if ndb is None or ncb is None:
             return None
-        key = (ndb, ncb, int(width))
+        return (ndb, ncb, int(width))
+
+    def consider(self, key: tuple[int, int, int]) -> bool:
+        """Counts a step of this shape and captures its graph on the `capture_after`-th one (while
+        fewer than max_graphs are captured); True when the shape has a graph to replay."""
         if key in self._graphs:
-            return key
+            return True
         seen = self._seen.get(key, 0) + 1
         self._seen[key] = seen
-        return key if seen >= self.capture_after and len(self._graphs) < self.max_graphs else None
+        if seen < self.capture_after or len(self._graphs) >= self.max_graphs:
+            return False
+        self._graphs[key] = self._capture(key)
+        return True
 
     def get(self, key: tuple[int, int, int]) -> _MixedGraph:
-        """The key's graphs, captured on first use."""
-        g = self._graphs.get(key)
-        if g is None:
-            g = self._capture(key)
-            self._graphs[key] = g
-        return g
+        """The key's captured graph (``consider`` captures)."""
+        return self._graphs[key]
 
     def fill(self, key, decode_tables, last_tokens, positions, chunk_token_ids, start_positions,
              chunk_tables) -> np.ndarray:

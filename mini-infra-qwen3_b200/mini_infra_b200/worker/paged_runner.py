@@ -87,7 +87,6 @@ class PagedRunner(BaseModelRunner):
     mixed_graph_replays = 0  # mixed steps served by a CUDA-graph replay
     decode_graphs: DecodeGraphSet | None = None
     mixed_graphs: MixedGraphSet | None = None
-    _mixed_key_pending = None  # (step shape, key) counted by warm_mixed_graph for the next step
     device_tables: DeviceBlockTables | None = None
     _graph_step: tuple[int, int, int] | None = None  # (bucket, batch, static buffer address)
 
@@ -115,7 +114,6 @@ class PagedRunner(BaseModelRunner):
         if self.mixed_graphs is not None:
             self.mixed_graphs.release()
         self.mixed_graphs = None
-        self._mixed_key_pending = None
 
     def _mixed_key(self, decode_tables, chunk_token_ids, chunk_tables, pool):
         g = self.mixed_graphs
@@ -126,12 +124,11 @@ class PagedRunner(BaseModelRunner):
                          max(len(t) for t in decode_tables), max(len(t) for t in chunk_tables))
 
     def warm_mixed_graph(self, decode_tables, chunk_token_ids, chunk_tables, pool) -> None:
-        """Capture the graph a mixed step of this shape will replay, if its shape has one now
-        (outside any step timing); the next run_mixed_step of these rows uses the decision."""
+        """Count a mixed step of this shape and capture its graph when the set decides to (outside
+        any step timing).  Only shapes counted here are served by graphs."""
         key = self._mixed_key(decode_tables, chunk_token_ids, chunk_tables, pool)
         if key is not None:
-            self.mixed_graphs.get(key)
-        self._mixed_key_pending = (id(decode_tables), id(chunk_token_ids), key)
+            self.mixed_graphs.consider(key)
 
     def warm_decode_graph(self, batch: int, max_blocks: int) -> None:
         """Capture the graph a step of this shape will replay (outside any step timing)."""
@@ -290,11 +287,7 @@ class PagedRunner(BaseModelRunner):
         lens = [len(t) for t in chunk_token_ids]
         if nd == 0 or bp == 0 or min(lens) < 1:
             raise ValueError("a mixed step needs decode rows and non-empty chunks")
-        pending, self._mixed_key_pending = self._mixed_key_pending, None
-        if pending is not None and pending[:2] == (id(decode_block_tables), id(chunk_token_ids)):
-            key = pending[2]
-        else:
-            key = self._mixed_key(decode_block_tables, chunk_token_ids, chunk_block_tables, pool)
+        key = self._mixed_key(decode_block_tables, chunk_token_ids, chunk_block_tables, pool)
         if key is not None and self.mixed_graphs.has(key):
             return self._replay_mixed(key, decode_block_tables, last_tokens, positions, chunk_token_ids,
                                       start_positions, chunk_block_tables)

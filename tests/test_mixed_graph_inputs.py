@@ -61,10 +61,13 @@ def test_keys_bucket_rows_and_reject_what_a_graph_cannot_hold():
 
 def test_capture_budget_and_first_use():
     g = _set()
+    captured = []
+    g._capture = lambda key: captured.append(key) or object()  # no device: record the captures
     g.capture_after = 2
-    assert g.key_for(1, 1, 32, 1, 1) is None  # first step of the shape: eager
-    assert g.key_for(1, 1, 32, 1, 1) == (1, 1, 32)  # second: captured
+    key = g.key_for(1, 1, 32, 1, 1)
+    assert key == (1, 1, 32) and not g.consider(key) and not g.has(key)  # first step: eager
+    assert g.consider(key) and g.has(key) and captured == [key]  # second: captured
+    assert g.consider(key) and captured == [key]  # captured shapes keep their graph
     g.capture_after, g.max_graphs = 1, 1
-    g._graphs[(1, 1, 32)] = object()
-    assert g.key_for(1, 1, 32, 1, 1) == (1, 1, 32)  # captured shapes keep their graph
-    assert g.key_for(2, 1, 32, 1, 1) is None  # budget spent: new shapes run eagerly
+    other = g.key_for(2, 1, 32, 1, 1)
+    assert not g.consider(other) and not g.has(other)  # budget spent: new shapes run eagerly
