@@ -1,7 +1,8 @@
 """Paged backend (reference ``engine/paged_schedule_backend.py``): glues scheduler, runner and pool.
 
 Per prefill step: chunk forward (model_ms, StepTimer), then ``store_prefill`` timed as cache_ms
-(host wall clock between two synchronisations).  Per decode step: the step inputs built on the
+(host wall clock between two synchronisations); unless ``cuda_graphs=False``, one CUDA-graph
+replay per step shape of forward + sample + store (model_ms; cache_ms ~0), as for mixed steps.  Per decode step: the step inputs built on the
 device from the slot-indexed block-table mirror (``PagedRunner.prepare_decode_rows``: O(batch)
 host work and upload) timed as cache_ms, then the decode forward (model_ms) — a CUDA-graph
 replay per batch bucket unless ``cuda_graphs=False`` (a bucket's first step captures its graph
@@ -87,7 +88,8 @@ class PagedScheduleBackend:
             # decode tables never exceed the largest request; round the graphs' width up to a power of two
             width = 1 << max(4, (largest - 1).bit_length())
             self.runner.enable_decode_graphs(self.pool.kv_pools, width)
-            self.runner.enable_mixed_graphs(self.pool, width)
+            if part is None or part.world == 1:  # head-partitioned models keep eager prefill / mixed steps
+                self.runner.enable_mixed_graphs(self.pool, width)
 
     def close(self) -> None:
         """Drop the decode and mixed-step graphs (they may hold NCCL calls: before the process group goes)."""
@@ -101,16 +103,23 @@ class PagedScheduleBackend:
     def execute_prefill(self, chunks: Sequence[PrefillChunk]) -> ScheduleStepOutput:
         tables = [self.kv_cache_manager.block_table(c.state.request.request_idx) for c in chunks]
         starts = [c.start for c in chunks]
-        out = self.runner.run_prefill_chunk_step(
-            [c.state.request.token_ids[c.start : c.end] for c in chunks], starts, tables, self.pool)
+        chunk_ids = [c.state.request.token_ids[c.start : c.end] for c in chunks]
+        if self.runner.warm_mixed_graph([], chunk_ids, tables, self.pool):  # a shape's first step captures
+            # a graph replay of forward + sample + the chunks' store (in model_ms)
+            mixed = self.runner.run_mixed_step([], [], [], chunk_ids, starts, tables, self.pool)
+            next_tokens, model_ms, cache = mixed.prefill_tokens, mixed.model_ms, None
+        else:
+            out = self.runner.run_prefill_chunk_step(chunk_ids, starts, tables, self.pool)
+            next_tokens, model_ms, cache = out.next_tokens, out.model_ms, out.prefill_cache
         synchronize(self.device)
         t0 = time.perf_counter()
-        self.runner.store_prefill(self.pool, out.prefill_cache, tables, [c.num_tokens for c in chunks], starts)
+        if cache is not None:
+            self.runner.store_prefill(self.pool, cache, tables, [c.num_tokens for c in chunks], starts)
         synchronize(self.device)
         cache_ms = (time.perf_counter() - t0) * 1000.0
         return ScheduleStepOutput(
-            next_tokens=[t for t, c in zip(out.next_tokens, chunks) if c.is_last],
-            model_ms=out.model_ms,
+            next_tokens=[t for t, c in zip(next_tokens, chunks) if c.is_last],
+            model_ms=model_ms,
             cache_ms=cache_ms,
             physical_batch_size=len(chunks),
             live_kv_cache_bytes=self.kv_cache_manager.num_used_blocks * self.pool.bytes_per_block,

@@ -82,7 +82,8 @@ def _run_loop(backend: PagedScheduleBackend, requests: Sequence[Request], max_ru
     result = summarize_schedule(states, events, max_running_requests, wall_ms, backend.collect_paged_cache_profile())
     result.extra.update(h2d_bytes=backend.runner.h2d_bytes, d2h_bytes=backend.runner.d2h_bytes,
                         decode_graph_replays=backend.runner.graph_replays,
-                        mixed_graph_replays=backend.runner.mixed_graph_replays)
+                        mixed_graph_replays=backend.runner.mixed_graph_replays,
+                        prefill_graph_replays=backend.runner.prefill_graph_replays)
     return result
 
 
@@ -100,8 +101,8 @@ def run_scheduler(
 ) -> ScheduleResult:
     """Run the requests through the paged engine; returns sequences, events and metrics.
 
-    ``cuda_graphs`` replays decode steps from per-batch-bucket CUDA graphs and mixed steps from
-    per-shape graphs (False: eager).
+    ``cuda_graphs`` replays decode steps from per-batch-bucket CUDA graphs and prefill and mixed
+    steps from per-shape graphs (False: eager).
     ``peer_exchange`` (head-partitioned bf16/fp16 models): decode outputs are exchanged by the
     decode kernel's peer stores (``exchange.PeerExchange``); False keeps the NCCL all-gather."""
     if not requests:

@@ -1,6 +1,8 @@
-"""CUDA graphs of the mixed step (decode rows and prefill chunks in one forward).
+"""CUDA graphs of the mixed step (decode rows and prefill chunks in one forward), and of the
+prefill step as its case without decode rows.
 
-An eager mixed step of a 28-layer model issues ~1,500 launches from Python; a graph replays them.
+An eager mixed or prefill step of a 28-layer model issues ~1,500 launches from Python (~6 ms of
+host time against 1-3 ms of device time at serving sizes); a graph replays them.
 A step's shape is (decode rows, chunk rows, padded chunk length).  The graph of a key
 (decode bucket, chunk-row bucket, width) serves every step whose decode rows fit the first bucket,
 whose chunk rows fit the second and whose chunk length pads to `width` (``padded_width`` already
@@ -39,7 +41,7 @@ from mini_infra_b200.worker.kv_cache import KVCache
 from mini_infra_b200.worker.paged_kv_cache import PagedKVCachePool
 from mini_infra_b200.worker.sampler import greedy_sample
 
-DECODE_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+DECODE_BUCKETS = (0, 1, 2, 4, 8, 16, 32, 64, 128, 256)  # 0: a prefill step
 # a padding chunk row costs `width` tokens of projections and MLP, so these buckets are fine
 CHUNK_BUCKETS = (1, 2, 3, 4, 5, 6, 8, 10, 12, 16, 20, 24, 32)
 
@@ -83,13 +85,13 @@ class MixedGraphSet:
         self._mempool = torch.cuda.graph_pool_handle()
         attn = model.model.layers[0].self_attn  # type: ignore[attr-defined]
         # every decode bucket's split-K workspace, before any capture (see DecodeGraphSet)
-        ops.workspace(self.device, workspace_bytes_for(DECODE_BUCKETS, attn.num_heads, self.kv_pools[0][0], self.wd),
-                      slot="decode")
+        ops.workspace(self.device, workspace_bytes_for([b for b in DECODE_BUCKETS if b], attn.num_heads,
+                                                       self.kv_pools[0][0], self.wd), slot="decode")
 
     def key_for(self, nd: int, nc: int, width: int, decode_blocks: int, chunk_blocks: int) -> tuple[int, int, int] | None:
-        """The key of a step's shape, or None when no graph of this set can hold it (tables too
-        wide, too many decode or chunk rows)."""
-        if decode_blocks > self.wd or chunk_blocks > self.wc or nd < 1 or nc < 1:
+        """The key of a step's shape (nd = 0: a prefill step), or None when no graph of this set can
+        hold it (tables too wide, too many decode or chunk rows)."""
+        if decode_blocks > self.wd or chunk_blocks > self.wc or nd < 0 or nc < 1:
             return None
         ndb, ncb = _first_at_least(DECODE_BUCKETS, nd), _first_at_least(CHUNK_BUCKETS, nc)
         if ndb is None or ncb is None:

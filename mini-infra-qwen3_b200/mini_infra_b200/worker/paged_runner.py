@@ -23,7 +23,8 @@ tables).  Attention reads history in place from the pools; nothing gathers the h
   policy; no reference counterpart): one packed upload, projections over all tokens, one decode
   and one chunked-prefill attention launch per layer, lm_head only on the rows that sample.  With
   ``enable_mixed_graphs`` a step whose shape has a graph (``worker/mixed_graphs.py``) replays it,
-  the chunks' store included (no ``store_prefill`` follows: ``prefill_cache`` is None).
+  the chunks' store included (no ``store_prefill`` follows: ``prefill_cache`` is None); a step
+  without decode rows is a prefill step, served the same way.
 """
 
 from __future__ import annotations
@@ -85,6 +86,7 @@ class PagedRunner(BaseModelRunner):
     d2h_bytes = 0
     graph_replays = 0  # decode steps served by a CUDA-graph replay
     mixed_graph_replays = 0  # mixed steps served by a CUDA-graph replay
+    prefill_graph_replays = 0  # prefill steps served by a (mixed-step) CUDA-graph replay
     decode_graphs: DecodeGraphSet | None = None
     mixed_graphs: MixedGraphSet | None = None
     device_tables: DeviceBlockTables | None = None
@@ -117,18 +119,18 @@ class PagedRunner(BaseModelRunner):
 
     def _mixed_key(self, decode_tables, chunk_token_ids, chunk_tables, pool):
         g = self.mixed_graphs
-        if (g is None or not decode_tables or not chunk_token_ids
+        if (g is None or not chunk_token_ids or min(len(t) for t in chunk_token_ids) < 1
                 or g.kv_pools[0][0].data_ptr() != pool.kv_pools[0][0].data_ptr()):
             return None
         return g.key_for(len(decode_tables), len(chunk_token_ids), padded_width(max(len(t) for t in chunk_token_ids)),
-                         max(len(t) for t in decode_tables), max(len(t) for t in chunk_tables))
+                         max((len(t) for t in decode_tables), default=0), max(len(t) for t in chunk_tables))
 
-    def warm_mixed_graph(self, decode_tables, chunk_token_ids, chunk_tables, pool) -> None:
-        """Count a mixed step of this shape and capture its graph when the set decides to (outside
-        any step timing).  Only shapes counted here are served by graphs."""
+    def warm_mixed_graph(self, decode_tables, chunk_token_ids, chunk_tables, pool) -> bool:
+        """Count a mixed step (no decode rows: a prefill step) of this shape and capture its graph
+        when the set decides to (outside any step timing); True when a graph serves the step.
+        Only shapes counted here are served by graphs."""
         key = self._mixed_key(decode_tables, chunk_token_ids, chunk_tables, pool)
-        if key is not None:
-            self.mixed_graphs.consider(key)
+        return key is not None and self.mixed_graphs.consider(key)
 
     def warm_decode_graph(self, batch: int, max_blocks: int) -> None:
         """Capture the graph a step of this shape will replay (outside any step timing)."""
@@ -282,15 +284,19 @@ class PagedRunner(BaseModelRunner):
         pool: PagedKVCachePool,
     ) -> PagedMixedOutput:
         """Decode rows (their new token at `positions`, appended to the pool) and prefill chunks
-        (history = the first ceil(start / bs) blocks of their table) in one forward."""
+        (history = the first ceil(start / bs) blocks of their table) in one forward.  Without
+        decode rows (a prefill step) only a graph serves it (``warm_mixed_graph`` said so); the
+        eager prefill step is ``run_prefill_chunk_step``."""
         nd, bp = len(decode_block_tables), len(chunk_token_ids)
         lens = [len(t) for t in chunk_token_ids]
-        if nd == 0 or bp == 0 or min(lens) < 1:
-            raise ValueError("a mixed step needs decode rows and non-empty chunks")
+        if bp == 0 or min(lens) < 1:
+            raise ValueError("a mixed step needs non-empty chunks")
         key = self._mixed_key(decode_block_tables, chunk_token_ids, chunk_block_tables, pool)
         if key is not None and self.mixed_graphs.has(key):
             return self._replay_mixed(key, decode_block_tables, last_tokens, positions, chunk_token_ids,
                                       start_positions, chunk_block_tables)
+        if nd == 0:
+            raise ValueError("a mixed step needs decode rows (a prefill step without a graph: run_prefill_chunk_step)")
         bs = pool.block_size
         width = padded_width(max(lens))
         n_hist = [-(-int(st) // bs) for st in start_positions]
@@ -346,7 +352,10 @@ class PagedRunner(BaseModelRunner):
             graphs.static.copy_(torch.from_numpy(host).pin_memory(), non_blocking=True)
             graphs.graph.replay()
             tokens = graphs.tokens.tolist()
-        self.mixed_graph_replays += 1
+        if nd:
+            self.mixed_graph_replays += 1
+        else:
+            self.prefill_graph_replays += 1
         self.d2h_bytes += 8 * (nd + bp)
         ndb = key[0]
         return PagedMixedOutput(tokens[:nd], tokens[ndb : ndb + bp], None, timer.elapsed_ms)

@@ -219,3 +219,22 @@ def test_bf16_mixed_steps_same_tokens_from_graphs_and_eager():
     assert runs[True].extra["mixed_graph_replays"] == runs[True].schedule_metrics.num_mixed_steps
     assert runs[False].extra["mixed_graph_replays"] == 0
     assert ops.read_status() == 0
+
+
+def test_bf16_prefill_steps_same_tokens_from_graphs_and_eager():
+    """Prefill steps (prefill-first policy) replayed from the mixed-step graphs without decode rows
+    (forward + sample + the chunks' store) give the same greedy ids as eager prefill steps."""
+    from mini_infra_b200.model.config import TINY_C1
+
+    cfg = Qwen3Config(**dict(TINY_C1, head_dim=128, hidden_size=256), torch_dtype="bfloat16")
+    model = build_model(cfg, seed=12, device="cuda", dtype=torch.bfloat16)
+    rng = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(1, cfg.vocab_size, (n,), generator=rng).tolist() for n in [90, 30] * 5]
+    ecfg = EngineConfig(PagedCacheConfig(block_size=16), BatchingMethod.CONTINUOUS,
+                        scheduler_config=SchedulerConfig(4, PrefillFirstConfig()))
+    runs = {g: run_scheduler(ecfg, model, make_requests(prompts, 16), None, stop_on_eos=False, cuda_graphs=g)
+            for g in (True, False)}
+    assert [s.token_ids for s in runs[True].sequences] == [s.token_ids for s in runs[False].sequences]
+    assert runs[True].extra["prefill_graph_replays"] == runs[True].schedule_metrics.num_prefill_steps > 0
+    assert runs[False].extra["prefill_graph_replays"] == 0
+    assert ops.read_status() == 0

@@ -49,9 +49,18 @@ def test_fill_layout_matches_the_eager_step():
     assert ctab.tolist() == [[6, 8, 0, 0, 0, 0, 0, 0], [0] * 8]
 
 
+def test_fill_of_a_prefill_step_has_no_decode_sections():
+    g = _set(wc=4)
+    host = g.fill((0, 1, 4), [], [], [], [[8, 9]], [6], [[3, 5]])
+    assert host.shape == (mixed_packed_length(0, 1, 4, g.wd, g.wc),)
+    assert host[:4].tolist() == [3, 3, 8, 9] and host[4:8].tolist() == [0, 0, 6, 7]
+    assert host[8:10].tolist() == [6, 2] and host[10:].tolist() == [3, 5, 0, 0]
+
+
 def test_keys_bucket_rows_and_reject_what_a_graph_cannot_hold():
     g = _set(wd=8, wc=16)
     assert g.key_for(3, 2, 64, 8, 16) == (4, 2, 64)
+    assert g.key_for(0, 3, 64, 0, 16) == (0, 3, 64)  # a prefill step: no decode rows
     assert g.key_for(5, 7, 64, 1, 1) == (8, 8, 64)
     assert g.key_for(3, 2, 64, 9, 1) is None  # decode table wider than the graphs'
     assert g.key_for(3, 2, 64, 1, 17) is None  # chunk table wider
