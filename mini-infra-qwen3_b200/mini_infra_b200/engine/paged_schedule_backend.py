@@ -1,17 +1,15 @@
 """Paged backend (reference ``engine/paged_schedule_backend.py``): glues scheduler, runner and pool.
 
 Per prefill step: chunk forward (model_ms, StepTimer), then ``store_prefill`` timed as cache_ms
-(host wall clock between two synchronisations); unless ``cuda_graphs=False``, one CUDA-graph
-replay per step shape of forward + sample + store (model_ms; cache_ms ~0), as for mixed steps.  Per decode step: the step inputs built on the
+(host wall clock between two synchronisations).  Per decode step: the step inputs built on the
 device from the slot-indexed block-table mirror (``PagedRunner.prepare_decode_rows``: O(batch)
-host work and upload) timed as cache_ms, then the decode forward (model_ms) — a CUDA-graph
-replay per batch bucket unless ``cuda_graphs=False`` (a bucket's first step captures its graph
-before the timing starts).  Per
-mixed step (mixed chunked prefill): one forward over decode rows and chunks (model_ms), then the
-chunks' ``store_prefill`` as cache_ms; unless ``cuda_graphs=False``, a shape's second and later
-steps replay one CUDA graph of forward + sample + store (model_ms; cache_ms ~0), captured before
-the timing starts.  ``accessed_kv_cache_tokens`` counts history tokens
-read: sum of chunk starts (prefill) and sum of context lengths (decode).
+host work and upload) timed as cache_ms, then the decode forward (model_ms).  Per mixed step
+(mixed chunked prefill): one forward over decode rows and chunks (model_ms), then the chunks'
+``store_prefill`` as cache_ms.  Unless ``cuda_graphs=False``, decode steps replay a CUDA graph per
+batch bucket, and prefill and mixed steps one graph per step shape holding forward + sample +
+store (model_ms; cache_ms ~0; head-partitioned models keep these two eager); a bucket's or
+shape's first step captures its graph before the timing starts.  ``accessed_kv_cache_tokens``
+counts history tokens read: sum of chunk starts (prefill) and sum of context lengths (decode).
 """
 
 from __future__ import annotations
