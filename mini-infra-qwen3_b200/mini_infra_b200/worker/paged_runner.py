@@ -340,10 +340,14 @@ class PagedRunner(BaseModelRunner):
     def _replay_mixed(self, key, decode_tables, last_tokens, positions, chunk_token_ids, start_positions,
                       chunk_tables) -> PagedMixedOutput:
         g = self.mixed_graphs
+        bs = g.pool.block_size
         for table, st, toks in zip(chunk_tables, start_positions, chunk_token_ids):
-            need = -(-(int(st) + len(toks)) // g.pool.block_size)
+            need = -(-(int(st) + len(toks)) // bs)
             if len(table) < need:
                 raise ValueError(f"block table {list(table)} does not cover {need} blocks")
+        for table, p in zip(decode_tables, positions):
+            if len(table) <= int(p) // bs:
+                raise ValueError(f"block table {list(table)} does not cover position {int(p)}")
         graphs = g.get(key)
         host = g.fill(key, decode_tables, last_tokens, positions, chunk_token_ids, start_positions, chunk_tables)
         self.h2d_bytes += host.nbytes
