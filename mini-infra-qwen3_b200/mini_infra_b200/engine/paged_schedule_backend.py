@@ -7,7 +7,7 @@ host work and upload) timed as cache_ms, then the decode forward (model_ms).  Pe
 (mixed chunked prefill): one forward over decode rows and chunks (model_ms), then the chunks'
 ``store_prefill`` as cache_ms.  Unless ``cuda_graphs=False``, decode steps replay a CUDA graph per
 batch bucket, and prefill and mixed steps one graph per step shape holding forward + sample +
-store (model_ms; cache_ms ~0; head-partitioned models keep these two eager); a bucket's or
+store (model_ms; cache_ms ~0; on a head partition they hold the NCCL all-gathers); a bucket's or
 shape's first step captures its graph before the timing starts.  ``accessed_kv_cache_tokens``
 counts history tokens read: sum of chunk starts (prefill) and sum of context lengths (decode).
 """
@@ -86,8 +86,7 @@ class PagedScheduleBackend:
             # decode tables never exceed the largest request; round the graphs' width up to a power of two
             width = 1 << max(4, (largest - 1).bit_length())
             self.runner.enable_decode_graphs(self.pool.kv_pools, width)
-            if part is None or part.world == 1:  # head-partitioned models keep eager prefill / mixed steps
-                self.runner.enable_mixed_graphs(self.pool, width)
+            self.runner.enable_mixed_graphs(self.pool, width)
 
     def close(self) -> None:
         """Drop the decode and mixed-step graphs (they may hold NCCL calls: before the process group goes)."""

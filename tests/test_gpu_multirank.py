@@ -1,7 +1,7 @@
 """KV-head-partitioned engine on 2 GPUs (one process per GPU, NCCL all-gather of attention
 outputs): the C1 tiny model split over two ranks (one KV head each) must produce the same greedy
-tokens as the reference engine (golden), with the same schedule on both ranks, with decode steps
-replayed from CUDA graphs (NCCL all-gather captured) and eagerly.  Skipped when the process sees
+tokens as the reference engine (golden), with the same schedule on both ranks, with decode and
+prefill steps replayed from CUDA graphs (NCCL all-gather captured) and eagerly.  Skipped when the process sees
 fewer than 2 GPUs."""
 
 import datetime
@@ -51,7 +51,7 @@ def _engine_worker(rank, port, case, graphs, results):
                         stop_on_eos=False, cuda_graphs=graphs)
     results[rank] = ([s.token_ids for s in res.sequences], [e.phase.value for e in res.events],
                      res.paged_cache.num_blocks, model.model.layers[0].self_attn.num_kv_heads,
-                     res.extra["decode_graph_replays"])
+                     res.extra["decode_graph_replays"], res.extra["prefill_graph_replays"])
     dist.barrier()
     dist.destroy_process_group()
 
@@ -63,12 +63,13 @@ def test_two_gpu_head_partition_matches_reference_tokens(case, graphs):
     port = _free_port()
     results = mp.get_context("spawn").Manager().dict()
     mp.spawn(_engine_worker, args=(port, case, graphs, results), nprocs=2)
-    tokens0, phases0, blocks0, heads0, replays0 = results[0]
-    tokens1, phases1, blocks1, heads1, replays1 = results[1]
+    tokens0, phases0, blocks0, heads0, replays0, pre0 = results[0]
+    tokens1, phases1, blocks1, heads1, replays1, pre1 = results[1]
     assert heads0 == heads1 == 1  # each rank holds one of the two KV heads
     assert phases0 == phases1 and blocks0 == blocks1
     assert tokens0 == tokens1 == case["tokens"]
     assert replays0 == replays1 == (case["num_decode_steps"] if graphs else 0)
+    assert pre0 == pre1 == (case["num_prefill_steps"] if graphs else 0)  # prefill steps from graphs too
 
 
 def _exchange_case(seed, b, hq, h):
