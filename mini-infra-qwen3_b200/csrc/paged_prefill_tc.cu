@@ -465,14 +465,14 @@ struct KvTileLoader {
 
 // Zeros for the padding positions (left of the chunk) of rows b = blockIdx.x (mod gridDim.x), all
 // query heads.
-template <typename T, int kThreads>
+template <typename T>
 __device__ __forceinline__ void zero_padding(const PrefillArgs& a, int tid) {
   const int64_t row_elems = (int64_t)a.hq * kTcDim;
   for (int64_t b = blockIdx.x; b < a.batch; b += gridDim.x) {
     const int64_t first = tc_row(a, b, tid == 0).first;
     const int64_t units = first * row_elems * (int64_t)sizeof(T) / 16;  // 16-byte stores
     uint4* dst = reinterpret_cast<uint4*>(a.out + b * a.padded_len * row_elems * (int64_t)sizeof(T));
-    for (int64_t i = tid; i < units; i += kThreads) dst[i] = make_uint4(0, 0, 0, 0);
+    for (int64_t i = tid; i < units; i += kTcThreads) dst[i] = make_uint4(0, 0, 0, 0);
   }
 }
 
@@ -481,14 +481,11 @@ __device__ __forceinline__ void zero_padding(const PrefillArgs& a, int tid) {
 // then the thread whose chunk holds the CTA's first position locates it.  Returns the walker at
 // that position, the cost of a head's stream (`total`) and the CTAs per head that share it
 // (`ctas`).
-// `unit` / `n_units`: the index and count of the work owners the heads' streams are cut between
-// (CTAs of the one-CTA kernel, clusters of the CTA-pair kernel); kThreads: the block's threads.
-template <int kThreads>
 __device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, int64_t* scratch, int tid, int64_t& total,
-                                             int64_t& ctas, int unit, int n_units) {
+                                             int64_t& ctas) {
   const int warp = tid >> 5, lane = tid & 31;
   const int rows = (int)(a.batch * pairs);
-  const int r0 = (int)((int64_t)rows * tid / kThreads), r1 = (int)((int64_t)rows * (tid + 1) / kThreads);
+  const int r0 = (int)((int64_t)rows * tid / kTcThreads), r1 = (int)((int64_t)rows * (tid + 1) / kTcThreads);
   int64_t mine = 0;
   for (int rp = r0; rp < r1; ++rp) {
     const int n = tc_pair(a, rp, pairs).n;
@@ -504,14 +501,14 @@ __device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, in
   __syncthreads();
   int64_t before = 0;
   total = 0;
-  for (int w = 0; w < kThreads / 32; ++w) {
+  for (int w = 0; w < kTcThreads / 32; ++w) {
     const int64_t v = scratch[w];
     if (w < warp) before += v;
     total += v;
   }
   const int64_t excl = before + x - mine;  // cost units ahead of this thread's chunk
-  ctas = min((int64_t)(n_units / a.hkv), total);
-  const int64_t c = unit / a.hkv;  // range index within the head
+  ctas = min((int64_t)(gridDim.x / a.hkv), total);
+  const int64_t c = blockIdx.x / a.hkv;  // range index within the head
   const int64_t x0 = c < ctas ? c * total / ctas : 0;
   const int64_t x1 = c < ctas ? (c + 1) * total / ctas : 0;
   __syncthreads();  // every warp total read before the start is written over them
@@ -532,11 +529,11 @@ __device__ __forceinline__ TcWalker tc_start(const PrefillArgs& a, int pairs, in
   TcWalker w;
   w.rows = rows;
   w.pairs = pairs;
-  w.cta = unit;
+  w.cta = (int)blockIdx.x;
   w.left = (int)(x1 - x0);
   w.used = 0;
   w.rp = w.left > 0 ? (int)scratch[0] : 0;
-  w.h = unit % a.hkv;
+  w.h = (int)(blockIdx.x % a.hkv);
   w.off = w.left > 0 ? (int)scratch[1] : 0;
   return w;
 }
@@ -573,10 +570,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   const int row_elems = a.hq * kTcDim;  // elements per output position
   T* out = reinterpret_cast<T*>(a.out);
 
-  zero_padding<T, kTcThreads>(a, tid);
+  zero_padding<T>(a, tid);
   int64_t total, ctas;
-  const TcWalker walk0 =
-      tc_start<kTcThreads>(a, pairs, reinterpret_cast<int64_t*>(smem + kOffK), tid, total, ctas, blockIdx.x, gridDim.x);
+  const TcWalker walk0 = tc_start(a, pairs, reinterpret_cast<int64_t*>(smem + kOffK), tid, total, ctas);
   int64_t* const scratch = reinterpret_cast<int64_t*>(smem + kOffK);
   if (tid == 0) {  // the CTA's tiles, and the unit it opens and leaves unfinished (for the combine)
     int64_t d0 = -1, d1 = 0, d2 = 0, tiles = 0;
