@@ -41,8 +41,8 @@ from mini_infra_b200.model.qwen3 import ChunkPrefillMetadata, MixedMetadata, Pag
 from mini_infra_b200.worker.base_runner import BaseModelRunner, PrefillOutput
 from mini_infra_b200.worker.block_tables import DeviceBlockTables
 from mini_infra_b200.worker.decode_graphs import DecodeGraphSet, packed_length
-from mini_infra_b200.worker.mixed_graphs import MixedGraphSet
 from mini_infra_b200.worker.kv_cache import KVCache
+from mini_infra_b200.worker.mixed_graphs import MixedGraphSet
 from mini_infra_b200.worker.paged_kv_cache import PagedKVCachePool
 from mini_infra_b200.worker.sampler import greedy_sample
 
@@ -57,7 +57,7 @@ class PagedDecodeOutput(NamedTuple):
 class PagedMixedOutput(NamedTuple):
     decode_tokens: list[int]   # one per decode row
     prefill_tokens: list[int]  # one per chunk row (its last position; meaningful for final chunks)
-    prefill_cache: KVCache | None  # the chunks' K/V for store_prefill; None: a graph replay (store_mixed)
+    prefill_cache: KVCache | None  # the chunks' K/V for store_prefill; None: a graph replay stored them
     model_ms: float
 
 
