@@ -64,7 +64,7 @@ NCU_DECODE = {"traffic": 1.129850e9 + 11.344896e6, "algorithmic": 1.129404160e9,
               "source": "ncu dram read+write of decode_split_kernel at the config-5 shape (batch 16, one "
                         "resident pool; profiles/decode_split_c5.md) / that launch's algorithmic bytes, "
                         "times this launch's algorithmic bytes"}
-NCU_PREFILL_C4 = {"traffic": 367.751168e6 + 16.403712e6,
+NCU_PREFILL_C4 = {"traffic": 364.092672e6 + 4.324864e6,
                   "source": "ncu dram read+write of prefill_tc_kernel at config 4 (profiles/prefill_tc_c4.md)"}
 
 # name -> heads, batch, contexts, layer calls per step, resident layer pools, whether the batch grows with N

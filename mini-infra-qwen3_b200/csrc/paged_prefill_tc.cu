@@ -455,7 +455,12 @@ struct KvTileLoader {
     if (lane == 0) mbar_arrive_expect_tx(full, kKvBytes);
     __syncwarp();
     if (lane < boxes) {
-      if (hist) tma_load_3d(dst + cc * kKvRegion + q * a.block_size * 128, &pool_map, full, cc * 64, h, row0);
+      // History pages go evict-first: at config-4 shapes that keeps the chunk K/V (re-read by
+      // the row's other tiles) and the split partials in L2 (111.3 against 113.5 us); the chunk
+      // loads stay unhinted, since an evict-first hint there cost ~8% on compute-bound chunks.
+      if (hist)
+        tma_load_3d_hint(dst + cc * kKvRegion + q * a.block_size * 128, &pool_map, full, cc * 64, h, row0,
+                         l2_policy_evict_first());
       else tma_load_4d(dst + cc * kKvRegion + q * 64 * 128, &chunk_map, full, cc * 64, h, pos + q * 64, b);
     }
     c.advance(a);
