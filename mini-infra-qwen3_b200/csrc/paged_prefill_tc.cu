@@ -31,7 +31,10 @@
 //      more than 2^8 since its last rescale (p <= 2^8 stays exact in fp32 and the final 1/l
 //      absorbs it); P is written back with tcgen05.st as 16-bit pairs into the first 64 columns
 //      of g's S columns (S_g(i+1) overwrites them only after PV_g(i), issued before it, has read
-//      them: tcgen05.mma of one thread run in issue order).
+//      them: tcgen05.mma of one thread run in issue order).  P is released in two halves: keys
+//      0-63 (p_half) once stored, so the first half of PV_g(i) runs under the softmax's second
+//      half, and all 128 keys (p_full); a warp that rescales O releases its first half only
+//      after the rescale.
 // Epilogue: tcgen05.ld of O, divide by l (or store the partial), 16-byte stores.  Padding
 // positions get zeros.
 //
@@ -558,11 +561,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
   uint64_t* v_full = k_empty + kStagesK;          // [kStagesV] loader -> MMA: V stage landed
   uint64_t* v_empty = v_full + kStagesV;          // [kStagesV] MMA -> loader: the PVs of the stage done
   uint64_t* s_full = v_empty + kStagesV;          // [kPair] MMA -> softmax g: S tile ready
-  uint64_t* p_full = s_full + kPair;              // [kPair] softmax g -> MMA: P written into TMEM
+  uint64_t* p_full = s_full + kPair;              // [kPair] softmax g -> MMA: all of P written into TMEM
   uint64_t* o_done = p_full + kPair;              // [kPair] MMA -> softmax g: one phase per PV
   uint64_t* o_final = o_done + kPair;             // [kPair] MMA -> softmax g: the item's last PV is done
   uint64_t* o_free = o_final + kPair;             // [kPair] softmax g -> MMA: the item's O read out of TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + kPair);
+  uint64_t* p_half = o_free + kPair;              // [kPair] softmax g -> MMA: keys 0-63 of P in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_half + kPair);
   int64_t* pages = reinterpret_cast<int64_t*>(smem + kOffPages);  // cp.async: block ids; TMA: page-row ring
 
   // Launched as a programmatic dependent of the stream's previous kernel (so its CTAs are placed
@@ -619,6 +623,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
       mbar_init(&o_done[g], 1);
       mbar_init(&o_final[g], 1);
       mbar_init(&o_free[g], kSoftmaxThreads);
+      mbar_init(&p_half[g], kSoftmaxThreads);
     }
     fence_mbar_init();
   }
@@ -768,7 +773,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
     TcWalker w = walk0;
     TcItem it;
     int64_t j0 = 0;            // CTA tile index of the item's first tile (ring positions)
-    int cnt[kPair] = {0, 0};   // tiles of row tile g so far (phases of s_full, p_full, o_done)
+    int cnt[kPair] = {0, 0};   // tiles of row tile g so far (phases of s_full, p_half, p_full, o_done)
     int fin[kPair] = {0, 0};   // items with tiles of row tile g so far (phases of o_final, o_free)
     int items = 0;
     while (w.next(a, it)) {
@@ -785,19 +790,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         // K(i) is free once every row tile that uses tile i has issued its S (row tile 1 issues last)
         if (g == kPair - 1 || i >= it.ng[kPair - 1]) umma_commit(&k_empty[ks]);
       };
-      auto issue_pv = [&](int g, int i) {  // O_g += P_g(i) V(i)
+      auto issue_pv_half = [&](int g, int i, int h) {  // O_g += P_g(i) V(i) over keys 64h .. 64h+63
         const int vs = (int)((j0 + i) % kStagesV);
         tc_fence_after();
         const uint64_t dvs = dv + (uint64_t)(vs * (kKvBytes >> 4));
 #pragma unroll
-        for (int s = 0; s < kTcKv / 16; ++s)  // P: 16-bit pairs in the first 64 of g's S columns
+        for (int s = h * 4; s < h * 4 + 4; ++s)  // P: 16-bit pairs in the first 64 of g's S columns
           umma_f16_tmem_a(tmem + kTmemO + g * 128, tmem + g * 128 + s * 8, dvs + (uint64_t)((s * 2048) >> 4),
                           idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
+      };
+      auto issue_pv = [&](int g, int i) {  // the second half of PV_g(i), then its commits
+        const int vs = (int)((j0 + i) % kStagesV);
+        issue_pv_half(g, i, 1);
         umma_commit(&o_done[g]);
         if (g == kPair - 1 || i >= it.ng[kPair - 1]) umma_commit(&v_empty[vs]);
         if (i + 1 == it.ng[g]) umma_commit(&o_final[g]);
       };
-      // S_g(i+1) overwrites P_g(i) in g's S columns, so it follows PV_g(i); the waits suspend the
+      // S_g(i+1) overwrites P_g(i) in g's S columns, so it follows PV_g(i); PV_g(i) is issued in
+      // two halves, keys 0-63 after p_half and keys 64-127 after p_full.  The waits suspend the
       // warp instead of spinning.
       mbar_wait_warp(q_full, items & 1, aborted);
       mbar_wait_warp(&k_full[j0 % kStagesK], (j0 / kStagesK) & 1, aborted);
@@ -808,10 +818,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
 #pragma unroll
         for (int g = 0; g < kPair; ++g) {
           if (i >= it.ng[g]) continue;
-          mbar_wait_warp(&p_full[g], (cnt[g] + i) & 1, aborted);
+          mbar_wait_warp(&p_half[g], (cnt[g] + i) & 1, aborted);
           mbar_wait_warp(&v_full[(j0 + i) % kStagesV], ((j0 + i) / kStagesV) & 1, aborted);
           // the previous item's O of this row tile has been read out before PV overwrites it
           if (i == 0 && fin[g] > 0) mbar_wait_warp(&o_free[g], (fin[g] - 1) & 1, aborted);
+          issue_pv_half(g, i, 0);  // under the softmax's second half
+          mbar_wait_warp(&p_full[g], (cnt[g] + i) & 1, aborted);
           issue_pv(g, i);
           if (i + 1 < it.ng[g]) {
             mbar_wait_warp(&k_full[(j0 + i + 1) % kStagesK], ((j0 + i + 1) / kStagesK) & 1, aborted);
@@ -895,6 +907,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
           m_ref = m_new;
         }
         const float neg_m = m_ref == -INFINITY ? 0.f : -m_ref;  // a row with nothing visible yet: all -inf
+        // A warp that rescales O releases its half of P only after the rescale (PV must not add
+        // into O before it); the others release keys 0-63 as soon as they are stored.
+        const bool warp_need = __any_sync(0xffffffffu, need);
         float ps[4] = {0.f, 0.f, 0.f, 0.f};
         // P as the A operand of PV: 16-bit pairs over the first 64 S columns, 32 scores (16
         // columns) per store; every S value is in registers before the first store.
@@ -910,10 +925,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
             pw[j] = pack2<T>(p0, p1);
           }
           tmem_st16_async(s_addr + c * 16, pw);
+          if (c == 1 && !warp_need) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_half[g]);
+          }
         }
         l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
         // The running O is rescaled after P is out of registers; PV(i) waits for both.
-        if (__any_sync(0xffffffffu, need)) {  // warp-collective TMEM access
+        if (warp_need) {  // warp-collective TMEM access
           mbar_wait(&o_done[g], (cnt + i - 1) & 1, aborted);  // PV(i-1) of this row tile finished writing O
           tc_fence_after();
 #pragma unroll
@@ -927,6 +947,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const Prefill
         }
         tmem_wait_st();
         tc_fence_before();  // our tcgen05.ld of S / st of P and O before the next MMAs
+        if (warp_need) mbar_arrive(&p_half[g]);
         mbar_arrive(&p_full[g]);
       }
       cnt += my_n;

@@ -10,11 +10,12 @@ This file restates, in Python, the parts that decide who waits for what:
   tile it exactly, and the partial slots and descriptors (`prefill_tc_kernel` epilogue,
   `prefill_combine_kernel`) must name exactly those pieces;
 * the protocol: the K loader (Q reloads after the last S of a unit), the V loader, the MMA warp
-  (PV_0(i), S_0(i+1), PV_1(i), S_1(i+1); k_empty / v_empty / o_final commits) and the two softmax
-  warpgroups (s_full, p_full, o_done, o_final, o_free) as coroutines over counting barriers, run
-  with random completion delays for TMA copies and MMA commits.  Every parity wait must end on
-  exactly the phase it means (never one that has already been passed twice), and nothing may
-  deadlock.
+  (PV_0(i), S_0(i+1), PV_1(i), S_1(i+1), each PV in two halves; k_empty / v_empty / o_final
+  commits) and the two softmax warpgroups (s_full, p_half, p_full, o_done, o_final, o_free) as
+  coroutines over counting barriers, run with random completion delays for TMA copies and MMA
+  commits.  Every parity wait must end on exactly the phase it means (never one that has already
+  been passed twice), nothing may deadlock, and no half of a PV may be issued before the O rescale
+  that its softmax step decided (each of the four softmax warps rescales on its own).
 
 The model is test infrastructure for this library's own kernel; when the kernel's order of
 waits changes, this file changes with it.
@@ -154,10 +155,11 @@ class Barrier:
             self.phases += 1
 
 
-def run_cta(walk0, seed, loader="tma"):
+def run_cta(walk0, seed, loader="tma", early_half=False):
     """One CTA's roles as coroutines; ('wait', bar, k) waits for the completion of phase k.
     loader="tma": Q and K from warp 0, V from warp 10 (block sizes 16/32/64); loader="cp": one warp
-    stages Q, K and V with cp.async (other block sizes)."""
+    stages Q, K and V with cp.async (other block sizes).  early_half plants a mistake: warps that
+    rescale O release their half of P before the rescale."""
     rnd = random.Random(seed)
     bars = {"q_full": Barrier(1)}
     for i in range(K_STAGES):
@@ -165,7 +167,7 @@ def run_cta(walk0, seed, loader="tma"):
     for i in range(V_STAGES):
         bars[f"v_full{i}"], bars[f"v_empty{i}"] = Barrier(1), Barrier(1)
     for g in range(PAIR):
-        for name, count in (("s_full", 1), ("p_full", 128), ("o_done", 1), ("o_final", 1), ("o_free", 128)):
+        for name, count in (("s_full", 1), ("p_full", 128), ("o_done", 1), ("o_final", 1), ("o_free", 128), ("p_half", 128)):
             bars[f"{name}{g}"] = Barrier(count)
     items = []
     w = walk0.copy()
@@ -227,10 +229,12 @@ def run_cta(walk0, seed, loader="tma"):
                 for g in range(PAIR):
                     if i >= ng[g]:
                         continue
-                    yield ("wait", f"p_full{g}", cnt[g] + i)
+                    yield ("wait", f"p_half{g}", cnt[g] + i)
                     yield ("wait", f"v_full{(j0 + i) % V_STAGES}", (j0 + i) // V_STAGES)
                     if i == 0 and fin[g] > 0:
                         yield ("wait", f"o_free{g}", fin[g] - 1)
+                    yield ("pv_half", g, cnt[g] + i)  # keys 0-63: adds into O
+                    yield ("wait", f"p_full{g}", cnt[g] + i)
                     yield from issue_pv(g, i)
                     if i + 1 < ng[g]:
                         yield ("wait", f"k_full{(j0 + i + 1) % K_STAGES}", (j0 + i + 1) // K_STAGES)
@@ -246,8 +250,20 @@ def run_cta(walk0, seed, loader="tma"):
             my_n = it["ng"][g]
             for i in range(my_n):
                 yield ("wait", f"s_full{g}", cnt + i)
-                if i > 0 and rnd.random() < 0.3:  # the lazy O rescale waits for PV(i-1)
+                # per warp (32 arrivals each): a warp that rescales O releases its part of p_half
+                # after the rescale, the others once keys 0-63 of P are stored
+                rescale = [i > 0 and rnd.random() < 0.15 for _ in range(4)]
+                if any(rescale):
+                    yield ("will_rescale", g, cnt + i)
+                for q in range(4):
+                    if early_half or not rescale[q]:
+                        yield ("arrive_n", f"p_half{g}", 32)
+                if any(rescale):  # the lazy O rescale waits for PV(i-1)
                     yield ("wait", f"o_done{g}", cnt + i - 1)
+                    yield ("rescaled", g, cnt + i)
+                for q in range(4):
+                    if rescale[q] and not early_half:
+                        yield ("arrive_n", f"p_half{g}", 32)
                 yield ("arrive_all", f"p_full{g}")
             cnt += my_n
             if my_n > 0:
@@ -287,6 +303,7 @@ def run_cta(walk0, seed, loader="tma"):
     else:
         roles = {"cp": cp_loader(), "mma": mma(), "sm0": softmax(0), "sm1": softmax(1)}
     blocked = dict.fromkeys(roles)
+    pending_rescale = set()  # (row tile, tile) whose softmax decided an O rescale not yet done
     done, inflight, clock, mma_clock = set(), [], 0, 0
     while len(done) < len(roles) or inflight:
         progressed = False
@@ -311,6 +328,16 @@ def run_cta(walk0, seed, loader="tma"):
                     blocked[r] = ev
                 elif ev[0] == "tma":
                     inflight.append((clock + rnd.randint(1, 60), ev[1]))
+                elif ev[0] == "will_rescale":
+                    pending_rescale.add((ev[1], ev[2]))
+                elif ev[0] == "rescaled":
+                    pending_rescale.discard((ev[1], ev[2]))
+                elif ev[0] == "pv_half":
+                    assert (ev[1], ev[2]) not in pending_rescale, \
+                        f"PV of row tile {ev[1]}, tile {ev[2]} issued before its O rescale"
+                elif ev[0] == "arrive_n":
+                    for _ in range(ev[2]):
+                        bars[ev[1]].arrive()
                 elif ev[0] == "check_s_done":
                     done_s = bars["s_full0"].phases + bars["s_full1"].phases
                     assert done_s >= ev[1], f"Q reloaded while {ev[1] - done_s} S MMAs were in flight"
@@ -368,3 +395,16 @@ def test_barrier_protocol_has_no_deadlock_or_phase_slip():
                 walkers, _, _ = split(shape, per_head)
                 for c, w in enumerate(walkers):
                     run_cta(w, seed=1000 * per_head + c, loader=loader)
+
+
+def test_protocol_model_catches_an_early_half_release():
+    """The rescale check is live: P released before a rescale fails the model."""
+    caught = False
+    for shape in _shapes()[:3]:
+        walkers, _, _ = split(shape, 7)
+        for c, w in enumerate(walkers):
+            try:
+                run_cta(w, seed=c, early_half=True)
+            except AssertionError as e:
+                caught = caught or "before its O rescale" in str(e)
+    assert caught
