@@ -14,7 +14,7 @@ relative to ``src/mini_infra/``) with plain numpy, keeping the reference's own d
 * attention output ``[batch, q_len, H_q * head_dim]`` (``model/qwen3.py:232-255``).
 
 Floating-point work runs in ``acc_dtype`` (float32 by default, the "fp32 reference" against
-which bf16 kernels are judged).  bf16 tensors are carried as ``uint16`` bit patterns and widened
+which bf16 kernels are checked).  bf16 tensors are carried as ``uint16`` bit patterns and widened
 exactly with :func:`bf16_to_f32`.
 
 Parity of this oracle against the reference itself is pinned by ``tests/test_oracle_golden.py``

@@ -8,6 +8,8 @@ the null block (context length 1) and padding chunk rows of length 0.
 
 from types import SimpleNamespace
 
+import numpy as np
+
 from mini_infra_b200.worker.mixed_graphs import CHUNK_BUCKETS, DECODE_BUCKETS, MixedGraphSet, mixed_packed_length
 
 
@@ -66,6 +68,55 @@ def test_keys_bucket_rows_and_reject_what_a_graph_cannot_hold():
     assert g.key_for(3, 2, 64, 1, 17) is None  # chunk table wider
     assert g.key_for(DECODE_BUCKETS[-1] + 1, 1, 32, 1, 1) is None
     assert g.key_for(1, CHUNK_BUCKETS[-1] + 1, 32, 1, 1) is None
+
+
+def test_fill_agrees_with_the_oracle_packing_on_random_steps():
+    """Seeded random mixed and prefill steps: the decode sections equal the oracle's restatement of
+    the reference's decode packing (paged_runner.py:152-166), and each chunk row's ids, positions
+    and store slots equal its prefill indexing (paged_runner.py:118-130)."""
+    from oracle.paged_oracle import decode_index, prefill_index, slot_for_position
+
+    rng = np.random.RandomState(7)
+    for _ in range(200):
+        bs = int(rng.choice([1, 3, 4, 16]))
+        g = _set(wd=12, wc=64, bs=bs, pad=int(rng.randint(0, 50)))
+        nd, nc = int(rng.randint(0, 9)), int(rng.randint(1, 6))
+        width = int(rng.choice([8, 32]))
+        d_tables = [list(rng.permutation(np.arange(1, 200))[: rng.randint(1, 13)]) for _ in range(nd)]
+        positions = [int(rng.randint(0, len(t) * bs)) for t in d_tables]
+        last = [int(x) for x in rng.randint(0, 1000, size=nd)]
+        lens = [int(rng.randint(1, width + 1)) for _ in range(nc)]
+        starts = [int(rng.randint(0, g.wc * bs - n + 1)) for n in lens]
+        c_tables = [list(rng.permutation(np.arange(1, 200))[: -(-(s + n) // bs)]) for s, n in zip(starts, lens)]
+        chunks = [list(rng.randint(0, 1000, size=n)) for n in lens]
+        key = g.key_for(nd, nc, width, max((len(t) for t in d_tables), default=0), max(len(t) for t in c_tables))
+        assert key is not None
+        host = g.fill(key, d_tables, last, positions, chunks, starts, c_tables)
+        ndb, ncb, w = key
+        t = ndb + ncb * w
+        ids, pos = host[:t], host[t : 2 * t]
+        o = 2 * t
+        slots, ctx = host[o : o + ndb], host[o + ndb : o + 2 * ndb]
+        q = o + 2 * ndb + 2 * ncb
+        dtab = host[q : q + ndb * g.wd].reshape(ndb, g.wd)
+        if nd:
+            ref = decode_index(d_tables, last, positions, bs)
+            width_d = ref["block_tables"].shape[1]
+            assert ids[:nd].tolist() == ref["input_ids"][:, 0].tolist()
+            assert pos[:nd].tolist() == ref["position_ids"][:, 0].tolist()
+            assert slots[:nd].tolist() == ref["slot_mapping"].tolist()
+            assert ctx[:nd].tolist() == ref["context_lens"].tolist()
+            assert (dtab[:nd, :width_d] == ref["block_tables"]).all() and not dtab[:nd, width_d:].any()
+        assert not slots[nd:].any() and (ctx[nd:] == 1).all()  # padding rows: null block, context 1
+        rows, padded_pos, store_slots = prefill_index(c_tables, lens, starts, w, bs)
+        for r, p, s in zip(rows, padded_pos, store_slots):
+            flat = ndb + r * w + p
+            assert ids[flat] == chunks[r][p - (w - lens[r])]
+            # the position the row's token is at, and the slot the graph's store writes it to
+            assert slot_for_position(c_tables[r], int(pos[flat]), bs) == s
+        for r in range(nc):
+            pad = ids[ndb + r * w : ndb + r * w + w - lens[r]]
+            assert (pad == g.pad_token_id).all()
 
 
 def test_capture_budget_and_first_use():
