@@ -10,8 +10,10 @@ step's packed inputs on the device.
 
 A slot's row is identified with its sequence by a key (the request id): a new key in a slot
 resends that sequence's whole table once.  Tables only grow while their sequence holds its slot
-(the block manager appends and frees whole tables), which is what makes "entries past the last
-synced length" the complete change.
+(the block manager appends and frees whole tables; there is no preemption), which is what makes
+"entries past the last synced length" the complete change.  As a guard against a caller that
+rebuilds a table under the same key, a slot whose table is shorter than what was synced, or whose
+last synced entry changed, is resent whole.
 """
 
 from __future__ import annotations
@@ -31,6 +33,7 @@ class DeviceBlockTables:
         self.tables = torch.zeros((capacity, width), dtype=torch.long, device=device)
         self._owner = [None] * capacity  # key of the sequence whose table the row holds
         self._synced = [0] * capacity  # entries of that table already on the device
+        self._last = [0] * capacity  # the last of those entries (block id)
 
     def step_inputs(
         self,
@@ -50,12 +53,14 @@ class DeviceBlockTables:
             if len(table) > self.width:
                 raise ValueError(f"a block table of {len(table)} blocks exceeds the device tables' width {self.width}")
             start = self._synced[slot]
-            if self._owner[slot] != key or len(table) < start:
+            if self._owner[slot] != key or len(table) < start or (start and int(table[start - 1]) != self._last[slot]):
                 self._owner[slot] = key
                 start = 0
             for col in range(start, len(table)):
                 deltas += (slot, col, int(table[col]))
             self._synced[slot] = len(table)
+            if len(table):
+                self._last[slot] = int(table[-1])
             rows += (slot, int(token), int(pos))
         return np.asarray(rows + deltas, dtype=np.int64), len(rows) // 3, len(deltas) // 3
 
