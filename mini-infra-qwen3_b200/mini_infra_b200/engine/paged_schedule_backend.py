@@ -43,6 +43,11 @@ class PagedScheduleBackend:
     ) -> None:
         self.model = model
         self.device = next(model.parameters()).device
+        # memory before the pool (the run's baseline), and peaks counted from here
+        synchronize(self.device)
+        self.baseline_mb = torch.cuda.memory_allocated(self.device) / 1024**2 if self.device.type == "cuda" else 0.0
+        if self.device.type == "cuda":
+            torch.cuda.reset_peak_memory_stats(self.device)
         self.max_running_requests = max_running_requests
         self.batching_method = batching_method
         self.paged_cache_config = paged_cache_config

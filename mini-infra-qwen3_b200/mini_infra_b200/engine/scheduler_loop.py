@@ -79,7 +79,14 @@ def _run_loop(backend: PagedScheduleBackend, requests: Sequence[Request], max_ru
         ))
     synchronize(backend.device)
     wall_ms = (time.perf_counter() - wall0) * 1000.0
-    result = summarize_schedule(states, events, max_running_requests, wall_ms, backend.collect_paged_cache_profile())
+    dev = backend.device
+    cuda = dev.type == "cuda"
+    result = summarize_schedule(
+        states, events, max_running_requests, wall_ms, backend.collect_paged_cache_profile(),
+        batching_method=backend.batching_method, kv_cache_config=backend.kv_cache_config,
+        peak_allocated_mb=torch.cuda.max_memory_allocated(dev) / 1024**2 if cuda else 0.0,
+        peak_reserved_mb=torch.cuda.max_memory_reserved(dev) / 1024**2 if cuda else 0.0,
+        baseline_mb=backend.baseline_mb, is_cuda=cuda)
     result.extra.update(h2d_bytes=backend.runner.h2d_bytes, d2h_bytes=backend.runner.d2h_bytes,
                         decode_graph_replays=backend.runner.graph_replays,
                         mixed_graph_replays=backend.runner.mixed_graph_replays,
