@@ -168,7 +168,7 @@ def test_percentile_is_nearest_rank():
     assert percentile([5.0, 1.0, 3.0], 34) == 3.0  # ceil(3 * 0.34) = 2nd smallest
 
 
-def _reference_summary(result, backend, mrr):
+def _reference_summary(states, result, mrr):
     """The reference's summarize_schedule on the same states and events (its event type and enums)."""
     src = REFERENCE / "src"
     if not (src / "mini_infra" / "engine" / "metrics.py").exists():
@@ -181,7 +181,7 @@ def _reference_summary(result, backend, mrr):
 
     events = [ref.ScheduleEvent(**{f.name: (RefPhase[e.phase.name] if f.name == "phase" else getattr(e, f.name))
                                    for f in fields(ref.ScheduleEvent)}) for e in result.events]
-    return ref.summarize_schedule(RefBatching.CONTINUOUS, result._states, events, mrr, 0.0, 0.0,
+    return ref.summarize_schedule(RefBatching.CONTINUOUS, states, events, mrr, 0.0, 0.0,
                                   e2e_wall_ms=result.e2e_wall_ms, is_cuda=False)
 
 
@@ -207,9 +207,8 @@ def test_summary_equals_the_references_summarize_schedule(name, monkeypatch):
         return real(states, *a, **k)
 
     monkeypatch.setattr(loop, "summarize_schedule", keep_states)
-    result, backend = run(lengths, budgets, policy, mrr, arrivals=arrivals)
-    object.__setattr__(result, "_states", captured["states"])
-    theirs = _reference_summary(result, backend, mrr)
+    result, _ = run(lengths, budgets, policy, mrr, arrivals=arrivals)
+    theirs = _reference_summary(captured["states"], result, mrr)
     _same(result.schedule_metrics, theirs.schedule_metrics, "schedule_metrics")
     _same(result.metrics, theirs.metrics, "metrics")
     _same(result.batch_info, theirs.batch_info, "batch_info")
